@@ -1,0 +1,273 @@
+/*
+ * krill_kv.h — C ABI of the B200 int8 KV-cache hot path.
+ *
+ * This is the drop-in boundary for Krill's KrillCache / KrillEngine cache
+ * path (srvsngh99/Krill, Swift + MLX). Each entry point names the reference
+ * interface it replaces (file:line within the reference project). A Swift
+ * module map over this header lets the engine call it in place of
+ * QuantizedKVCache / RotatingKVCache / PrefixCache and the batched
+ * stack/scatter helpers.
+ *
+ * Model of the cache:
+ *   pool      One device-resident block pool per (device, layer group). It owns
+ *             all KV memory: 256-token blocks, each holding every layer and
+ *             KV head of the group (int8 codes + fp16 scale/zero per group of
+ *             `group_size` elements).
+ *   sequence  One request's per-layer caches (the reference's
+ *             `[QuantizedKVCache]` for one row): a block table plus a length
+ *             per layer. Blocks are ref-counted and shared copy-on-write
+ *             between sequences and prefix-cache entries.
+ *   prefix    A prefix cache bound to one pool; entries keep block references
+ *             instead of tensor copies.
+ *
+ * Conventions:
+ *   - Every function returns krill_status_t (KRILL_OK = 0). On error,
+ *     krill_last_error_string() gives a thread-local message. Nothing aborts.
+ *   - Device pointers are plain `void*`; `stream` is a `cudaStream_t` passed as
+ *     `void*` (NULL = legacy default stream). Buffers passed in and out are
+ *     caller-owned; the pool owns only its blocks and its scratch.
+ *   - Calls on one pool must be externally serialised (one host thread at a
+ *     time); the prefix cache is internally locked.
+ *   - Tensors are dense, row-major, in the reference's layouts:
+ *       new K/V   [layer_count][n_seqs][num_kv_heads][n_new][head_dim]
+ *       q / out   [layer_count][n_seqs][num_q_heads][head_dim]
+ *       snapshot  codes [num_kv_heads][S][head_dim] u8,
+ *                 scales/zeros [num_kv_heads][S][head_dim/group_size] f16
+ */
+#ifndef KRILL_KV_H_
+#define KRILL_KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t krill_status_t;
+enum {
+  KRILL_OK = 0,
+  KRILL_ERR_INVALID = 1,   /* bad argument, handle, shape or state        */
+  KRILL_ERR_OOM = 2,       /* block pool exhausted or allocation failed   */
+  KRILL_ERR_CUDA = 3,      /* a CUDA runtime call failed                  */
+  KRILL_ERR_PEER = 4,      /* peer access / peer copy unavailable          */
+  KRILL_ERR_TIMEOUT = 5,   /* a device-side bounded wait gave up          */
+  KRILL_ERR_NOT_FOUND = 6, /* lookup miss (not an error for lookups)      */
+  KRILL_ERR_NO_DEVICE = 7  /* compute call on a host-only pool            */
+};
+
+enum {
+  KRILL_DTYPE_F16 = 0,
+  KRILL_DTYPE_BF16 = 1,
+  KRILL_DTYPE_F32 = 2,
+  KRILL_DTYPE_U8 = 3
+};
+
+/* Quantizer arithmetic. F32 follows MLX's promotion of an f16/bf16 array
+ * against a Float32 scalar array (QuantizedKVCache.swift:185-192): scale and
+ * quotient in float32. F16 keeps them in the input dtype. */
+enum { KRILL_QUANT_F32 = 0, KRILL_QUANT_INPUT_DTYPE = 1 };
+
+/* Decode-attention implementation: tensor-core (mma.sync m16n8k16 on the
+ * dequantized tiles) or CUDA-core FMA. Both give the same results within the
+ * attention tolerance; the choice is a performance knob. */
+enum { KRILL_ATTN_TENSOR_CORE = 0, KRILL_ATTN_CUDA_CORE = 1 };
+
+typedef struct krill_pool_s* krill_pool_t;
+typedef uint64_t krill_seq_t;               /* generation << 32 | slot */
+typedef struct krill_prefix_s* krill_prefix_t;
+typedef struct krill_prefix_entry_s* krill_prefix_entry_t;
+
+typedef struct {
+  int32_t num_layers;     /* layers in this layer group                          */
+  int32_t num_kv_heads;   /* Hkv                                                 */
+  int32_t num_q_heads;    /* Hq (multiple of Hkv; Hq/Hkv <= 8)                    */
+  int32_t head_dim;       /* D: 64, 128 or 256                                   */
+  int32_t group_size;     /* quantization group: 64 or head_dim                  */
+  int32_t window;         /* 0 = full history (QuantizedKVCache); > 1 = sliding
+                             window of that many tokens (RotatingKVCache)        */
+  int32_t max_append;     /* largest n_new per append on a windowed pool (sizes
+                             the ring: window - 1 + max_append tokens); 0 -> 256  */
+  int32_t quant_variant;  /* KRILL_QUANT_*                                       */
+  int32_t attn_impl;      /* KRILL_ATTN_*                                        */
+  int32_t split_tokens;   /* decode split-K chunk in tokens (multiple of 64);
+                             0 -> 2048. Fixed per pool, so a sequence's output
+                             does not depend on what else is in the batch.      */
+  int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
+} krill_pool_cfg;
+
+/* ---- errors ------------------------------------------------------------- */
+const char* krill_last_error_string(void);
+const char* krill_version(void);
+
+/* ---- pool ----------------------------------------------------------------
+ * Replaces makeQuantizedKVCaches(numLayers:) (QuantizedKVCache.swift:208-210)
+ * and makeKVCaches(spec:numLayers:) for `.rotating(window:)` layers
+ * (KVCache.swift:198-209). device < 0 creates a host-only pool: block
+ * accounting, sequences and the prefix cache work, compute calls return
+ * KRILL_ERR_NO_DEVICE. */
+krill_status_t krill_pool_create(const krill_pool_cfg* cfg, int32_t device, krill_pool_t* out);
+krill_status_t krill_pool_destroy(krill_pool_t pool);
+krill_status_t krill_pool_block_bytes(krill_pool_t pool, int64_t* bytes);
+krill_status_t krill_pool_free_blocks(krill_pool_t pool, int64_t* n);
+krill_status_t krill_pool_block_refcount(krill_pool_t pool, int32_t block, int32_t* refcount);
+/* Device error flag set by a kernel whose bounded wait gave up (and cleared
+ * by reading it). */
+krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
+
+/* ---- sequences (one request's per-layer caches) -------------------------- */
+/* New empty sequence: every layer at length 0 (QuantizedKVCache.init). */
+krill_status_t krill_seq_create(krill_pool_t pool, krill_seq_t* out);
+/* Drop the sequence and its block references. */
+krill_status_t krill_seq_release(krill_pool_t pool, krill_seq_t seq);
+/* reset(): all layers back to empty (QuantizedKVCache.swift:92-99). */
+krill_status_t krill_seq_reset(krill_pool_t pool, krill_seq_t seq);
+/* sequenceLength of one layer (QuantizedKVCache.swift:28-30; for a windowed
+ * pool the total tokens seen, RotatingKVCache.swift:60). */
+krill_status_t krill_seq_length(krill_pool_t pool, krill_seq_t seq, int32_t layer, int64_t* len);
+/* Rows physically retained for a layer (RotatingKVCache.retainedLength,
+ * RotatingKVCache.swift:63; equals the length on a full-history pool). */
+krill_status_t krill_seq_retained(krill_pool_t pool, krill_seq_t seq, int32_t layer, int64_t* n);
+/* memorySizeBytes (QuantizedKVCache.swift:33-42), generalised to groups. */
+krill_status_t krill_seq_memory_bytes(krill_pool_t pool, krill_seq_t seq, int32_t layer, int64_t* bytes);
+/* truncate(to:) on every layer (QuantizedKVCache.swift:135-145; on a windowed
+ * pool RotatingKVCache.truncate, RotatingKVCache.swift:134-142, which fails
+ * with KRILL_ERR_INVALID where canTruncate is false). n >= length is a no-op. */
+krill_status_t krill_seq_truncate(krill_pool_t pool, krill_seq_t seq, int64_t n);
+/* canTruncate(to:) (RotatingKVCache.swift:128-130; KVCache.swift:218). */
+krill_status_t krill_seq_can_truncate(krill_pool_t pool, krill_seq_t seq, int64_t n, int32_t* ok);
+/* Number of blocks in the sequence's table and their ids (for tests/tools). */
+krill_status_t krill_seq_blocks(krill_pool_t pool, krill_seq_t seq, int32_t* ids, int32_t cap, int32_t* n);
+
+/* ---- hot path ------------------------------------------------------------ */
+/* Quantize n_new tokens of K and V per (token, head, group) and append them at
+ * each layer's current length, in place (no concatenation copy). Replaces the
+ * quantize + concatenate half of QuantizedKVCache.update
+ * (QuantizedKVCache.swift:49-69) and quantizePerHead (:181-197).
+ * k_new/v_new: [layer_count][n_seqs][Hkv][n_new][D], dtype F16 or BF16. */
+krill_status_t krill_append_quantize(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                     int32_t layer_begin, int32_t layer_count, int32_t n_new,
+                                     const void* k_new, const void* v_new, int32_t dtype,
+                                     void* stream);
+
+/* Decode attention for one query token per (layer, sequence), reading the
+ * int8 cache directly: dequantization (with the reference's fp16 rounding) is
+ * fused into q·Kᵀ, online softmax and ·V. Replaces the dequantize half of
+ * QuantizedKVCache.update (:71-74) plus MLXFast.scaledDotProductAttention with
+ * GQA (Gemma4Model.swift:516, Attention.swift:95). Each sequence attends its
+ * current length (its window on a windowed pool), so no pad mask is needed.
+ * q: [layer_count][n_seqs][Hq][D] F16 or BF16; out: same shape, F16, BF16 or
+ * F32. scale: 1/sqrt(D) for Llama (Attention.swift:44), 1.0 for Gemma 4. */
+krill_status_t krill_decode_attention(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, const void* q,
+                                      int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                      void* stream);
+
+/* One decode step: krill_append_quantize (n_new = 1) then
+ * krill_decode_attention over the same layers. */
+krill_status_t krill_decode_step(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                 int32_t layer_begin, int32_t layer_count, const void* k_new,
+                                 const void* v_new, int32_t kv_dtype, const void* q,
+                                 int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                 void* stream);
+
+/* ---- snapshots / restore -------------------------------------------------- */
+/* quantizedSnapshot() for one layer (QuantizedKVCache.swift:106-115): the raw
+ * codes and fp16 scales/zeros of the retained rows, in the QuantizedKVSnapshot
+ * layout (QuantizedKVCache.swift:150-157). Any output pointer may be NULL. */
+krill_status_t krill_seq_snapshot_quantized(krill_pool_t pool, krill_seq_t seq, int32_t layer,
+                                            void* keys, void* values, void* key_scales,
+                                            void* key_zeros, void* value_scales,
+                                            void* value_zeros, void* stream);
+/* snapshot() / the tensors update() returns (QuantizedKVCache.swift:82-89,
+ * :72-74): the retained rows dequantized to fp16, bit-exact with the
+ * reference's dequantize (:200-204). Output [Hkv][S][D] f16 each. */
+krill_status_t krill_seq_snapshot_dequantized(krill_pool_t pool, krill_seq_t seq, int32_t layer,
+                                              void* keys, void* values, void* stream);
+/* restoreQuantized(_:) for one layer (QuantizedKVCache.swift:122-129): copy
+ * (never alias) `rows` rows in the snapshot layout into the sequence; the
+ * layer's length becomes total_seen (= rows on a full-history pool; on a
+ * windowed pool the rows are the tail ending at total_seen - 1, as
+ * RotatingKVCache.restore, RotatingKVCache.swift:148-163). */
+krill_status_t krill_seq_restore_quantized(krill_pool_t pool, krill_seq_t seq, int32_t layer,
+                                           int64_t rows, int64_t total_seen, const void* keys,
+                                           const void* values, const void* key_scales,
+                                           const void* key_zeros, const void* value_scales,
+                                           const void* value_zeros, void* stream);
+
+/* ---- continuous-batch glue ------------------------------------------------ */
+/* stackCachesLeftPaddedQuantized for one layer (BatchedDecode.swift:96-151):
+ * rows right-aligned at s_max = max length, left pad = code 0, scale 0,
+ * zero 0. Outputs [n_seqs][Hkv][s_max][D] u8 and [n_seqs][Hkv][s_max][D/G] f16. */
+krill_status_t krill_stack_left_padded(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                       int32_t layer, int64_t s_max, void* keys, void* values,
+                                       void* key_scales, void* key_zeros, void* value_scales,
+                                       void* value_zeros, void* stream);
+/* ContinuousBatcher.scatterBack int8 branch (ContinuousBatcher.swift:763-773):
+ * row i's columns [s_max - base_len[i], s_max + steps) of a stacked layer are
+ * restored into sequence i (its new length for that layer). */
+krill_status_t krill_scatter_back(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                  int32_t layer, const int64_t* base_lens, int64_t s_max,
+                                  int64_t steps, const void* keys, const void* values,
+                                  const void* key_scales, const void* key_zeros,
+                                  const void* value_scales, const void* value_zeros,
+                                  void* stream);
+/* buildBatchedDecodeMask (BatchedDecode.swift:277-287), host memory:
+ * out [n][total_len] float, -10000 on each row's left pad, 0 elsewhere. */
+krill_status_t krill_build_decode_mask(const int64_t* lengths, int32_t n, int64_t s_max,
+                                       int64_t total_len, float* out);
+
+/* ---- prefix cache ---------------------------------------------------------
+ * PrefixCache (PrefixCache.swift:15-114) bound to one pool. Entries hold
+ * block references (zero-copy store); a hit is consumed by forking a new
+ * sequence that shares the entry's blocks copy-on-write. */
+krill_status_t krill_prefix_create(krill_pool_t pool, int32_t max_memory_entries,
+                                   int32_t min_prefix_length, krill_prefix_t* out);
+krill_status_t krill_prefix_destroy(krill_prefix_t pc);
+/* storeQuantized(tokens:modelId:snapshots:mediaHash:) (PrefixCache.swift:369-400):
+ * the first n_tokens positions of `seq` become an entry keyed by
+ * FNV-1a(v3, int8, modelId, mediaHash, tokens) (:513-532); LRU-evicts at
+ * max_memory_entries (:540-551). n_tokens < min_prefix_length is a no-op. */
+krill_status_t krill_prefix_store(krill_prefix_t pc, krill_seq_t seq, const int64_t* tokens,
+                                  int64_t n_tokens, const char* model_id, const char* media_hash);
+/* lookupQuantized (PrefixCache.swift:161-170 via scan :273-308): exact-key
+ * scan from the full length down in steps of max(1, min/2). On a hit *entry
+ * holds a reference (release it) and *prefix_length is the matched length;
+ * a miss returns KRILL_ERR_NOT_FOUND with *entry = NULL. */
+krill_status_t krill_prefix_lookup(krill_prefix_t pc, const int64_t* tokens, int64_t n_tokens,
+                                   const char* model_id, const char* media_hash,
+                                   krill_prefix_entry_t* entry, int64_t* prefix_length);
+/* lookupLongestPrefixQuantized (PrefixCache.swift:235-263): the in-memory
+ * entry with the longest common prefix >= min_prefix_length. */
+krill_status_t krill_prefix_lookup_longest(krill_prefix_t pc, const int64_t* tokens,
+                                           int64_t n_tokens, const char* model_id,
+                                           const char* media_hash, krill_prefix_entry_t* entry,
+                                           int64_t* prefix_length);
+/* Stored token count of an entry (PrefixCacheHit.storedLength, :443-448). */
+krill_status_t krill_prefix_entry_length(krill_prefix_entry_t entry, int64_t* stored_length);
+krill_status_t krill_prefix_entry_release(krill_prefix_t pc, krill_prefix_entry_t entry);
+/* Restore-and-truncate of a hit (InferenceEngine.swift:1305-1320, 1378-1417):
+ * a new sequence sharing the entry's blocks for positions [0, keep); no KV is
+ * copied and no prefill runs. keep <= stored length. */
+krill_status_t krill_seq_fork_prefix(krill_prefix_t pc, krill_prefix_entry_t entry, int64_t keep,
+                                     krill_seq_t* out);
+/* clear() (PrefixCache.swift:403-414) and memoryCount (:417-420). */
+krill_status_t krill_prefix_clear(krill_prefix_t pc);
+krill_status_t krill_prefix_memory_count(krill_prefix_t pc, int32_t* count);
+/* FNV-1a cache key (PrefixCache.swift:513-532) for tools and tests. */
+uint64_t krill_prefix_key(const int64_t* tokens, int64_t n_tokens, const char* model_id,
+                          const char* media_hash, int32_t dtype_tag);
+
+/* ---- multi-GPU ------------------------------------------------------------
+ * Copy a prefix entry owned by another GPU's pool into dst's pool over NVLink
+ * (cudaMemcpyPeerAsync, copy engine) and register it in dst's prefix cache.
+ * Pools must have identical geometry. No reference counterpart (the reference
+ * is single-device); the entry is afterwards ref-counted locally. */
+krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
+                                       krill_prefix_entry_t src_entry, void* stream,
+                                       krill_prefix_entry_t* dst_entry);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KRILL_KV_H_ */

@@ -1,0 +1,1326 @@
+// host.cpp — host side of the B200 KV-cache library: block pool accounting,
+// sequences (per-layer lengths over one shared block table), copy-on-write,
+// the decode-attention planner, the prefix cache, and every C-ABI entry
+// point declared in include/krill_kv.h.
+//
+// The reference keeps one MLXArray set per layer per request and lets Swift
+// ARC reference-count them (Sources/KrillCache/QuantizedKVCache.swift,
+// PrefixCache.swift). Here the same state is a table of 256-token blocks per
+// sequence; blocks carry explicit reference counts so that prefix entries and
+// forked sequences share them without copies.
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <list>
+#include <mutex>
+#include <queue>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/krill_kv.h"
+#include "internal.h"
+
+using namespace krill;
+
+namespace {
+
+thread_local std::string g_err;
+
+krill_status_t fail(krill_status_t code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                       \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess) return fail(KRILL_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+#define TRY(expr)                        \
+  do {                                   \
+    krill_status_t _s = (expr);          \
+    if (_s != KRILL_OK) return _s;       \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (dev < 0) return;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev) {
+      cudaSetDevice(dev);
+      prev = cur;
+    }
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+struct Seq {
+  uint32_t gen = 0;
+  bool alive = false;
+  std::vector<int32_t> blocks;  // full history: block i holds positions [256i, 256i+256);
+                                // windowed: ring slot i, -1 until first written
+  std::vector<int64_t> len;     // per layer: tokens seen (sequenceLength)
+  std::vector<int64_t> ret;     // per layer: rows retained (== len on full history)
+};
+
+// Pinned host + device staging buffer for one launch's metadata packet; the
+// event guards reuse until every kernel reading it has finished.
+struct StageSlot {
+  uint8_t* h = nullptr;
+  uint8_t* d = nullptr;
+  size_t cap = 0;
+  cudaEvent_t ev = nullptr;
+  bool pending = false;
+};
+constexpr int kStageSlots = 8;
+
+}  // namespace
+
+struct krill_pool_s {
+  krill_pool_cfg cfg{};
+  Geom geom{};
+  int device = -1;
+  bool host_only = true;
+  uint8_t* d_pool = nullptr;
+  std::vector<int32_t> refcnt;
+  std::vector<int32_t> free_blocks;
+  std::vector<Seq> seqs;
+  std::vector<uint32_t> free_slots;
+  int num_sms = 148;
+  float* d_partials = nullptr;
+  int64_t partials_cap = 0;
+  int* d_counters = nullptr;
+  int64_t counters_cap = 0;
+  int* d_err = nullptr;
+  StageSlot stage[kStageSlots];
+  int stage_next = 0;
+  std::recursive_mutex mu;
+
+  int64_t ring_tokens() const { return (int64_t)geom.ring * kBlockTokens; }
+  bool windowed() const { return cfg.window > 0; }
+  uint8_t* block_ptr(int32_t b) const { return d_pool + (int64_t)b * geom.block_bytes; }
+};
+
+namespace {
+
+// ---------------------------------------------------------------- blocks
+krill_status_t block_alloc(krill_pool_t p, int32_t* out) {
+  if (p->free_blocks.empty())
+    return fail(KRILL_ERR_OOM, "block pool exhausted (%lld blocks)", (long long)p->cfg.num_blocks);
+  int32_t b = p->free_blocks.back();
+  p->free_blocks.pop_back();
+  p->refcnt[b] = 1;
+  *out = b;
+  return KRILL_OK;
+}
+void block_ref(krill_pool_t p, int32_t b) { p->refcnt[b] += 1; }
+void block_unref(krill_pool_t p, int32_t b) {
+  if (b < 0) return;
+  if (--p->refcnt[b] == 0) p->free_blocks.push_back(b);
+}
+
+// ---------------------------------------------------------------- sequences
+krill_status_t seq_get(krill_pool_t p, krill_seq_t h, Seq** out) {
+  uint32_t slot = (uint32_t)(h & 0xffffffffu), gen = (uint32_t)(h >> 32);
+  if (slot >= p->seqs.size() || !p->seqs[slot].alive || p->seqs[slot].gen != gen)
+    return fail(KRILL_ERR_INVALID, "stale or unknown sequence handle 0x%llx", (unsigned long long)h);
+  *out = &p->seqs[slot];
+  return KRILL_OK;
+}
+
+krill_status_t seq_new(krill_pool_t p, krill_seq_t* out, Seq** sp) {
+  uint32_t slot;
+  if (!p->free_slots.empty()) {
+    slot = p->free_slots.back();
+    p->free_slots.pop_back();
+  } else {
+    slot = (uint32_t)p->seqs.size();
+    p->seqs.emplace_back();
+  }
+  Seq& s = p->seqs[slot];
+  s.gen += 1;
+  s.alive = true;
+  s.blocks.clear();
+  if (p->windowed()) s.blocks.assign(p->geom.ring, -1);
+  s.len.assign(p->geom.L, 0);
+  s.ret.assign(p->geom.L, 0);
+  *out = ((uint64_t)s.gen << 32) | slot;
+  if (sp) *sp = &s;
+  return KRILL_OK;
+}
+
+void seq_drop_blocks(krill_pool_t p, Seq& s) {
+  for (int32_t b : s.blocks) block_unref(p, b);
+  s.blocks.clear();
+  if (p->windowed()) s.blocks.assign(p->geom.ring, -1);
+}
+
+// Full-history pools: release blocks past the longest layer.
+void seq_trim_blocks(krill_pool_t p, Seq& s) {
+  if (p->windowed()) return;
+  int64_t mx = 0;
+  for (int64_t l : s.len) mx = std::max(mx, l);
+  size_t need = (size_t)((mx + kBlockTokens - 1) / kBlockTokens);
+  while (s.blocks.size() > need) {
+    block_unref(p, s.blocks.back());
+    s.blocks.pop_back();
+  }
+}
+
+// Make block-table index `idx` writable: allocate it, or copy it if shared.
+krill_status_t seq_writable_block(krill_pool_t p, Seq& s, int64_t idx, cudaStream_t stream) {
+  if (!p->windowed()) {
+    while ((int64_t)s.blocks.size() <= idx) {
+      int32_t b = -1;
+      TRY(block_alloc(p, &b));
+      s.blocks.push_back(b);
+    }
+  } else if (s.blocks[idx] < 0) {
+    int32_t b = -1;
+    TRY(block_alloc(p, &b));
+    s.blocks[idx] = b;
+    return KRILL_OK;
+  }
+  int32_t b = s.blocks[idx];
+  if (p->refcnt[b] > 1) {
+    int32_t nb = -1;
+    TRY(block_alloc(p, &nb));
+    if (!p->host_only)
+      CUDA_TRY(cudaMemcpyAsync(p->block_ptr(nb), p->block_ptr(b), (size_t)p->geom.block_bytes,
+                               cudaMemcpyDeviceToDevice, stream));
+    block_unref(p, b);
+    s.blocks[idx] = nb;
+  }
+  return KRILL_OK;
+}
+
+int64_t block_index(krill_pool_t p, int64_t pos) {
+  int64_t bi = pos / kBlockTokens;
+  return p->windowed() ? bi % p->geom.ring : bi;
+}
+
+// ---------------------------------------------------------------- staging
+krill_status_t stage_acquire(krill_pool_t p, size_t bytes, StageSlot** out) {
+  StageSlot& s = p->stage[p->stage_next];
+  p->stage_next = (p->stage_next + 1) % kStageSlots;
+  if (s.pending) {
+    CUDA_TRY(cudaEventSynchronize(s.ev));
+    s.pending = false;
+  }
+  if (!s.ev) CUDA_TRY(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
+  if (s.cap < bytes) {
+    if (s.h) cudaFreeHost(s.h);
+    if (s.d) cudaFree(s.d);
+    s.h = nullptr;
+    s.d = nullptr;
+    size_t cap = 64 * 1024;
+    while (cap < bytes) cap *= 2;
+    CUDA_TRY(cudaMallocHost(&s.h, cap));
+    CUDA_TRY(cudaMalloc(&s.d, cap));
+    s.cap = cap;
+  }
+  *out = &s;
+  return KRILL_OK;
+}
+
+krill_status_t stage_upload(StageSlot* s, size_t bytes, cudaStream_t stream) {
+  CUDA_TRY(cudaMemcpyAsync(s->d, s->h, bytes, cudaMemcpyHostToDevice, stream));
+  return KRILL_OK;
+}
+
+krill_status_t stage_release(StageSlot* s, cudaStream_t stream) {
+  CUDA_TRY(cudaEventRecord(s->ev, stream));
+  s->pending = true;
+  return KRILL_OK;
+}
+
+size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+krill_status_t require_device(krill_pool_t p) {
+  if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "compute call on a host-only pool");
+  return KRILL_OK;
+}
+
+krill_status_t check_dtype16(int32_t dt, const char* what) {
+  if (dt != KRILL_DTYPE_F16 && dt != KRILL_DTYPE_BF16)
+    return fail(KRILL_ERR_INVALID, "%s dtype must be F16 or BF16 (got %d)", what, dt);
+  return KRILL_OK;
+}
+
+krill_status_t check_aligned(const void* ptr, const char* what) {
+  if (((uintptr_t)ptr & 15) != 0) return fail(KRILL_ERR_INVALID, "%s must be 16-byte aligned", what);
+  return KRILL_OK;
+}
+
+krill_status_t check_layers(krill_pool_t p, int32_t lb, int32_t lc) {
+  if (lb < 0 || lc < 0 || lb + lc > p->geom.L)
+    return fail(KRILL_ERR_INVALID, "layer range [%d, %d) outside [0, %d)", lb, lb + lc, p->geom.L);
+  return KRILL_OK;
+}
+
+// ---------------------------------------------------------------- append
+krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
+                         int32_t lc, int32_t n_new, const void* k, const void* v, int32_t dtype,
+                         cudaStream_t stream) {
+  TRY(require_device(p));
+  TRY(check_layers(p, lb, lc));
+  TRY(check_dtype16(dtype, "k/v"));
+  if (n_seqs < 0 || n_new < 0) return fail(KRILL_ERR_INVALID, "negative count");
+  if (n_seqs == 0 || lc == 0 || n_new == 0) return KRILL_OK;
+  if (!k || !v || !seqs) return fail(KRILL_ERR_INVALID, "null k/v/seqs");
+  if (p->windowed() && n_new > p->cfg.max_append)
+    return fail(KRILL_ERR_INVALID, "n_new %d exceeds the windowed pool's max_append %d", n_new,
+                p->cfg.max_append);
+  std::vector<Seq*> sv(n_seqs);
+  for (int i = 0; i < n_seqs; ++i) TRY(seq_get(p, seqs[i], &sv[i]));
+  for (int i = 0; i < n_seqs; ++i)
+    for (int j = 0; j < i; ++j)
+      if (sv[i] == sv[j]) return fail(KRILL_ERR_INVALID, "sequence listed twice in one call");
+  const size_t n_dst = (size_t)lc * n_seqs * n_new;
+  StageSlot* slot;
+  TRY(stage_acquire(p, n_dst * sizeof(AppendDst), &slot));
+  AppendDst* dst = reinterpret_cast<AppendDst*>(slot->h);
+  for (int si = 0; si < n_seqs; ++si) {
+    Seq& s = *sv[si];
+    // make every touched block writable first (allocation / copy-on-write)
+    for (int li = 0; li < lc; ++li) {
+      int64_t p0 = s.len[lb + li];
+      if (p0 + n_new > INT32_MAX) return fail(KRILL_ERR_INVALID, "sequence too long");
+      int64_t b0 = p0 / kBlockTokens, b1 = (p0 + n_new - 1) / kBlockTokens;
+      for (int64_t bi = b0; bi <= b1; ++bi)
+        TRY(seq_writable_block(p, s, p->windowed() ? bi % p->geom.ring : bi, stream));
+    }
+    for (int li = 0; li < lc; ++li) {
+      int64_t p0 = s.len[lb + li];
+      for (int t = 0; t < n_new; ++t) {
+        int64_t pos = p0 + t;
+        AppendDst& d = dst[((size_t)li * n_seqs + si) * n_new + t];
+        d.block = s.blocks[block_index(p, pos)];
+        d.pos = (int32_t)pos;
+      }
+    }
+  }
+  TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
+  CUDA_TRY(launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
+                         n_seqs, n_new, k, v, dtype, stream));
+  TRY(stage_release(slot, stream));
+  for (int si = 0; si < n_seqs; ++si) {
+    Seq& s = *sv[si];
+    for (int li = 0; li < lc; ++li) {
+      const int L = lb + li;
+      s.len[L] += n_new;
+      if (p->windowed())
+        s.ret[L] = std::min<int64_t>(s.ret[L], p->cfg.window - 1) + n_new;
+      else
+        s.ret[L] = s.len[L];
+    }
+  }
+  return KRILL_OK;
+}
+
+// ---------------------------------------------------------------- attention
+krill_status_t ensure_scratch(krill_pool_t p, int64_t partial_count, int64_t units) {
+  const int64_t pf = partial_floats(p->geom.D);
+  if (partial_count * pf > p->partials_cap || units > p->counters_cap) {
+    CUDA_TRY(cudaDeviceSynchronize());
+    if (partial_count * pf > p->partials_cap) {
+      if (p->d_partials) cudaFree(p->d_partials);
+      p->d_partials = nullptr;
+      int64_t cap = std::max<int64_t>(partial_count * pf * 3 / 2, 1 << 20);
+      CUDA_TRY(cudaMalloc(&p->d_partials, (size_t)cap * sizeof(float)));
+      p->partials_cap = cap;
+    }
+    if (units > p->counters_cap) {
+      if (p->d_counters) cudaFree(p->d_counters);
+      p->d_counters = nullptr;
+      int64_t cap = std::max<int64_t>(units * 3 / 2, 4096);
+      CUDA_TRY(cudaMalloc(&p->d_counters, (size_t)cap * sizeof(int)));
+      CUDA_TRY(cudaMemset(p->d_counters, 0, (size_t)cap * sizeof(int)));
+      p->counters_cap = cap;
+    }
+  }
+  return KRILL_OK;
+}
+
+krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
+                            int32_t lc, const void* q, int32_t q_dtype, void* out,
+                            int32_t out_dtype, float scale, cudaStream_t stream) {
+  TRY(require_device(p));
+  TRY(check_layers(p, lb, lc));
+  TRY(check_dtype16(q_dtype, "q"));
+  if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
+    return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
+  if (n_seqs < 0) return fail(KRILL_ERR_INVALID, "negative n_seqs");
+  if (n_seqs == 0 || lc == 0) return KRILL_OK;
+  if (!q || !out || !seqs) return fail(KRILL_ERR_INVALID, "null q/out/seqs");
+  TRY(check_aligned(q, "q"));
+  TRY(check_aligned(out, "out"));
+  const Geom& g = p->geom;
+  std::vector<Seq*> sv(n_seqs);
+  int64_t bt_stride = 1;
+  for (int i = 0; i < n_seqs; ++i) {
+    TRY(seq_get(p, seqs[i], &sv[i]));
+    bt_stride = std::max<int64_t>(bt_stride, (int64_t)sv[i]->blocks.size());
+  }
+  const int64_t n_units = (int64_t)lc * n_seqs * g.Hkv;
+  const int C = std::max(1, p->cfg.split_tokens / kSubTokens);
+  std::vector<AttnUnit> units((size_t)n_units);
+  std::vector<AttnItem> items;
+  items.reserve((size_t)n_units * 2);
+  int64_t partial_count = 0;
+  for (int li = 0; li < lc; ++li) {
+    const int L = lb + li;
+    for (int si = 0; si < n_seqs; ++si) {
+      const Seq& s = *sv[si];
+      const int64_t len = s.len[L];
+      if (len <= 0) return fail(KRILL_ERR_INVALID, "attention over an empty cache (layer %d)", L);
+      const int64_t t_hi = len;
+      const int64_t t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
+      const int64_t sb0 = t_lo / kSubTokens, sb1 = (t_hi + kSubTokens - 1) / kSubTokens;
+      const int64_t n_sb = sb1 - sb0;
+      const int64_t n_it = (n_sb + C - 1) / C;
+      const int64_t base = n_sb / n_it, extra = n_sb % n_it;
+      for (int h = 0; h < g.Hkv; ++h) {
+        const int64_t ui = ((int64_t)li * n_seqs + si) * g.Hkv + h;
+        AttnUnit& u = units[ui];
+        u.qo_row = li * n_seqs + si;
+        u.si = si;
+        u.layer = L;
+        u.h = h;
+        u.t_lo = (int32_t)t_lo;
+        u.t_hi = (int32_t)t_hi;
+        u.n_items = (int32_t)n_it;
+        u.first_item = n_it > 1 ? (int32_t)partial_count : 0;
+        if (n_it > 1) partial_count += n_it;
+        int64_t b = sb0;
+        for (int64_t i = 0; i < n_it; ++i) {
+          const int64_t sz = base + (i < extra ? 1 : 0);
+          items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int32_t)i});
+          b += sz;
+        }
+      }
+    }
+  }
+  TRY(ensure_scratch(p, partial_count, n_units));
+  // Longest-processing-time assignment of items to persistent CTAs.
+  const int64_t n_items = (int64_t)items.size();
+  const int grid = (int)std::min<int64_t>(p->num_sms, n_items);
+  std::vector<int32_t> order((size_t)n_items);
+  for (int64_t i = 0; i < n_items; ++i) order[i] = (int32_t)i;
+  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+    return (items[a].sb_end - items[a].sb_begin) > (items[b].sb_end - items[b].sb_begin);
+  });
+  std::vector<int32_t> owner((size_t)n_items);
+  std::vector<int32_t> count((size_t)grid, 0);
+  {
+    using E = std::pair<int64_t, int32_t>;
+    std::priority_queue<E, std::vector<E>, std::greater<E>> heap;
+    for (int c = 0; c < grid; ++c) heap.push({0, c});
+    for (int32_t i : order) {
+      E e = heap.top();
+      heap.pop();
+      owner[i] = e.second;
+      count[e.second] += 1;
+      e.first += items[i].sb_end - items[i].sb_begin;
+      heap.push(e);
+    }
+  }
+  const size_t units_bytes = align16(units.size() * sizeof(AttnUnit));
+  const size_t items_bytes = align16((size_t)n_items * sizeof(AttnItem));
+  const size_t off_bytes = align16((size_t)(grid + 1) * sizeof(int32_t));
+  const size_t bt_bytes = align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
+  const size_t total = units_bytes + items_bytes + off_bytes + bt_bytes;
+  StageSlot* slot;
+  TRY(stage_acquire(p, total, &slot));
+  uint8_t* h = slot->h;
+  std::memcpy(h, units.data(), units.size() * sizeof(AttnUnit));
+  AttnItem* hi = reinterpret_cast<AttnItem*>(h + units_bytes);
+  int32_t* off = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes);
+  off[0] = 0;
+  for (int c = 0; c < grid; ++c) off[c + 1] = off[c] + count[c];
+  {
+    std::vector<int32_t> fill(off, off + grid);
+    for (int32_t i : order) hi[fill[owner[i]]++] = items[i];
+  }
+  int32_t* bt = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes + off_bytes);
+  for (int si = 0; si < n_seqs; ++si) {
+    const Seq& s = *sv[si];
+    for (int64_t j = 0; j < bt_stride; ++j)
+      bt[si * bt_stride + j] = j < (int64_t)s.blocks.size() ? s.blocks[j] : -1;
+  }
+  TRY(stage_upload(slot, total, stream));
+  AttnParams ap{};
+  ap.pool = p->d_pool;
+  ap.page_bytes = g.page_bytes;
+  ap.sb_bytes = g.sb_bytes;
+  ap.L = g.L;
+  ap.Hkv = g.Hkv;
+  ap.Hq = g.Hq;
+  ap.g = g.g;
+  ap.ring = g.ring;
+  ap.units = reinterpret_cast<const AttnUnit*>(slot->d);
+  ap.items = reinterpret_cast<const AttnItem*>(slot->d + units_bytes);
+  ap.cta_off = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes);
+  ap.bt = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes);
+  ap.bt_stride = (int)bt_stride;
+  ap.q = q;
+  ap.q_dtype = q_dtype;
+  ap.out = out;
+  ap.out_dtype = out_dtype;
+  ap.scale_log2 = scale * 1.4426950408889634f;
+  ap.partials = p->d_partials;
+  ap.counters = p->d_counters;
+  ap.err = p->d_err;
+  CUDA_TRY(launch_attention(g, ap, grid, p->cfg.attn_impl, stream));
+  TRY(stage_release(slot, stream));
+  return KRILL_OK;
+}
+
+// ---------------------------------------------------------------- gather helpers
+// Rows physically available for a layer: positions [p0, p0 + S).
+void layer_span(krill_pool_t p, const Seq& s, int L, int64_t* p0, int64_t* S) {
+  if (p->windowed()) {
+    *S = std::min<int64_t>(s.ret[L], p->ring_tokens());
+    *p0 = s.len[L] - *S;
+  } else {
+    *S = s.len[L];
+    *p0 = 0;
+  }
+}
+
+krill_status_t upload_bt(krill_pool_t p, const Seq& s, cudaStream_t stream, StageSlot** out) {
+  size_t n = std::max<size_t>(1, s.blocks.size());
+  StageSlot* slot;
+  TRY(stage_acquire(p, n * sizeof(int32_t), &slot));
+  int32_t* bt = reinterpret_cast<int32_t*>(slot->h);
+  for (size_t i = 0; i < n; ++i) bt[i] = i < s.blocks.size() ? s.blocks[i] : -1;
+  TRY(stage_upload(slot, n * sizeof(int32_t), stream));
+  *out = slot;
+  return KRILL_OK;
+}
+
+krill_status_t do_restore(krill_pool_t p, Seq& s, int32_t layer, int64_t rows, int64_t total_seen,
+                          const ScatterIn& in, cudaStream_t stream) {
+  if (rows < 0 || total_seen < rows) return fail(KRILL_ERR_INVALID, "bad restore span");
+  if (!p->windowed() && rows != total_seen)
+    return fail(KRILL_ERR_INVALID, "full-history restore needs rows == total_seen");
+  if (p->windowed() && rows > p->ring_tokens())
+    return fail(KRILL_ERR_INVALID, "restore of %lld rows exceeds the ring (%lld)", (long long)rows,
+                (long long)p->ring_tokens());
+  if (rows > 0 && (!in.keys || !in.values || !in.key_scales || !in.key_zeros || !in.value_scales ||
+                   !in.value_zeros))
+    return fail(KRILL_ERR_INVALID, "restore needs all six tensors");
+  const int64_t p0 = total_seen - rows;
+  if (rows > 0) {
+    int64_t b0 = p0 / kBlockTokens, b1 = (total_seen - 1) / kBlockTokens;
+    for (int64_t bi = b0; bi <= b1; ++bi)
+      TRY(seq_writable_block(p, s, p->windowed() ? bi % p->geom.ring : bi, stream));
+    StageSlot* slot;
+    TRY(upload_bt(p, s, stream, &slot));
+    CUDA_TRY(launch_scatter(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d),
+                            p0, rows, in, stream));
+    TRY(stage_release(slot, stream));
+  }
+  s.len[layer] = total_seen;
+  s.ret[layer] = rows;
+  seq_trim_blocks(p, s);
+  return KRILL_OK;
+}
+
+}  // namespace
+
+// =====================================================================
+// C ABI
+// =====================================================================
+extern "C" {
+
+const char* krill_last_error_string(void) { return g_err.c_str(); }
+const char* krill_version(void) { return "krill-kv-b200 0.1.0 (sm_100a)"; }
+
+krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, krill_pool_t* out) {
+  if (!cfg_in || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  krill_pool_cfg cfg = *cfg_in;
+  if (cfg.num_layers <= 0 || cfg.num_kv_heads <= 0 || cfg.num_q_heads <= 0)
+    return fail(KRILL_ERR_INVALID, "layers and heads must be positive");
+  if (cfg.num_q_heads % cfg.num_kv_heads != 0 || cfg.num_q_heads / cfg.num_kv_heads > 8)
+    return fail(KRILL_ERR_INVALID, "num_q_heads must be a multiple of num_kv_heads, ratio <= 8");
+  if (cfg.head_dim != 64 && cfg.head_dim != 128 && cfg.head_dim != 256)
+    return fail(KRILL_ERR_INVALID, "head_dim must be 64, 128 or 256");
+  if (cfg.group_size == 0) cfg.group_size = 64;
+  if (cfg.group_size < 64 || cfg.head_dim % cfg.group_size != 0)
+    return fail(KRILL_ERR_INVALID, "group_size must divide head_dim and be >= 64");
+  if (cfg.window == 1 || cfg.window < 0) return fail(KRILL_ERR_INVALID, "window must be 0 or > 1");
+  if (cfg.max_append <= 0) cfg.max_append = 256;
+  if (cfg.quant_variant != KRILL_QUANT_F32 && cfg.quant_variant != KRILL_QUANT_INPUT_DTYPE)
+    return fail(KRILL_ERR_INVALID, "bad quant_variant");
+  if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE)
+    return fail(KRILL_ERR_INVALID, "bad attn_impl");
+  if (cfg.split_tokens == 0) cfg.split_tokens = 2048;
+  if (cfg.split_tokens < 64 || cfg.split_tokens % 64 != 0)
+    return fail(KRILL_ERR_INVALID, "split_tokens must be a positive multiple of 64");
+  if (cfg.num_blocks <= 0 || cfg.num_blocks > INT32_MAX)
+    return fail(KRILL_ERR_INVALID, "num_blocks out of range");
+  int ring = 0;
+  if (cfg.window > 0) {
+    int64_t need = (int64_t)cfg.window - 1 + cfg.max_append;
+    ring = (int)((need + kBlockTokens - 1) / kBlockTokens);
+  }
+  auto* p = new krill_pool_s();
+  p->cfg = cfg;
+  p->geom = make_geom(cfg.num_layers, cfg.num_kv_heads, cfg.num_q_heads, cfg.head_dim,
+                      cfg.group_size, ring, cfg.window, cfg.quant_variant);
+  p->device = device;
+  p->host_only = device < 0;
+  p->refcnt.assign((size_t)cfg.num_blocks, 0);
+  p->free_blocks.reserve((size_t)cfg.num_blocks);
+  for (int64_t b = cfg.num_blocks - 1; b >= 0; --b) p->free_blocks.push_back((int32_t)b);
+  if (!p->host_only) {
+    DeviceGuard dg(device);
+    cudaError_t e = cudaSetDevice(device);
+    size_t bytes = (size_t)cfg.num_blocks * (size_t)p->geom.block_bytes;
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_pool, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p->d_pool, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) {
+      krill_status_t code = (e == cudaErrorMemoryAllocation) ? KRILL_ERR_OOM : KRILL_ERR_CUDA;
+      if (p->d_pool) cudaFree(p->d_pool);
+      if (p->d_err) cudaFree(p->d_err);
+      delete p;
+      cudaGetLastError();
+      return fail(code, "pool allocation on device %d failed: %s", device, cudaGetErrorString(e));
+    }
+  }
+  *out = p;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_destroy(krill_pool_t p) {
+  if (!p) return KRILL_OK;
+  if (!p->host_only) {
+    DeviceGuard dg(p->device);
+    cudaDeviceSynchronize();
+    for (auto& s : p->stage) {
+      if (s.h) cudaFreeHost(s.h);
+      if (s.d) cudaFree(s.d);
+      if (s.ev) cudaEventDestroy(s.ev);
+    }
+    if (p->d_pool) cudaFree(p->d_pool);
+    if (p->d_partials) cudaFree(p->d_partials);
+    if (p->d_counters) cudaFree(p->d_counters);
+    if (p->d_err) cudaFree(p->d_err);
+  }
+  delete p;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_block_bytes(krill_pool_t p, int64_t* bytes) {
+  if (!p || !bytes) return fail(KRILL_ERR_INVALID, "null argument");
+  *bytes = p->geom.block_bytes;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_free_blocks(krill_pool_t p, int64_t* n) {
+  if (!p || !n) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  *n = (int64_t)p->free_blocks.size();
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_block_refcount(krill_pool_t p, int32_t block, int32_t* rc) {
+  if (!p || !rc) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (block < 0 || block >= (int64_t)p->refcnt.size()) return fail(KRILL_ERR_INVALID, "bad block id");
+  *rc = p->refcnt[block];
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_device_error(krill_pool_t p, int32_t* flag) {
+  if (!p || !flag) return fail(KRILL_ERR_INVALID, "null argument");
+  *flag = 0;
+  if (p->host_only) return KRILL_OK;
+  DeviceGuard dg(p->device);
+  int v = 0;
+  CUDA_TRY(cudaMemcpy(&v, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    CUDA_TRY(cudaMemset(p->d_err, 0, sizeof(int)));
+    // a bounded wait gave up mid-launch: split counters may be left non-zero
+    if (p->d_counters) CUDA_TRY(cudaMemset(p->d_counters, 0, (size_t)p->counters_cap * sizeof(int)));
+  }
+  *flag = v;
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_create(krill_pool_t p, krill_seq_t* out) {
+  if (!p || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  return seq_new(p, out, nullptr);
+}
+
+krill_status_t krill_seq_release(krill_pool_t p, krill_seq_t h) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  seq_drop_blocks(p, *s);
+  s->alive = false;
+  s->len.clear();
+  s->ret.clear();
+  p->free_slots.push_back((uint32_t)(h & 0xffffffffu));
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_reset(krill_pool_t p, krill_seq_t h) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  seq_drop_blocks(p, *s);
+  std::fill(s->len.begin(), s->len.end(), 0);
+  std::fill(s->ret.begin(), s->ret.end(), 0);
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_length(krill_pool_t p, krill_seq_t h, int32_t layer, int64_t* len) {
+  if (!p || !len) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  *len = s->len[layer];
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_retained(krill_pool_t p, krill_seq_t h, int32_t layer, int64_t* n) {
+  if (!p || !n) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  *n = s->ret[layer];
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_memory_bytes(krill_pool_t p, krill_seq_t h, int32_t layer, int64_t* bytes) {
+  if (!p || !bytes) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  int64_t p0, S;
+  layer_span(p, *s, layer, &p0, &S);
+  const Geom& g = p->geom;
+  // QuantizedKVCache.memorySizeBytes: u8 K+V plus 4 f16 arrays per row (per group)
+  *bytes = 2 * S * g.Hkv * g.D + 4 * S * g.Hkv * g.NG * 2;
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_can_truncate(krill_pool_t p, krill_seq_t h, int64_t n, int32_t* ok) {
+  if (!p || !ok) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  bool good = n >= 0;
+  if (p->windowed())
+    for (int L = 0; L < p->geom.L && good; ++L)
+      good = n >= s->len[L] - s->ret[L] && n <= s->len[L];
+  *ok = good ? 1 : 0;
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_truncate(krill_pool_t p, krill_seq_t h, int64_t n) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (n < 0) return KRILL_OK;  // QuantizedKVCache.truncate ignores negative lengths (:138)
+  if (p->windowed()) {
+    for (int L = 0; L < p->geom.L; ++L)
+      if (n < s->len[L] && n < s->len[L] - s->ret[L])
+        return fail(KRILL_ERR_INVALID, "truncate(to: %lld) below the retained range of layer %d",
+                    (long long)n, L);
+    for (int L = 0; L < p->geom.L; ++L)
+      if (n < s->len[L]) {
+        s->ret[L] -= s->len[L] - n;
+        s->len[L] = n;
+      }
+  } else {
+    for (int L = 0; L < p->geom.L; ++L)
+      if (n < s->len[L]) s->len[L] = s->ret[L] = n;
+    seq_trim_blocks(p, *s);
+  }
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_blocks(krill_pool_t p, krill_seq_t h, int32_t* ids, int32_t cap, int32_t* n) {
+  if (!p || !n) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  *n = (int32_t)s->blocks.size();
+  for (int32_t i = 0; i < *n && i < cap && ids; ++i) ids[i] = s->blocks[i];
+  return KRILL_OK;
+}
+
+krill_status_t krill_append_quantize(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                     int32_t layer_begin, int32_t layer_count, int32_t n_new,
+                                     const void* k_new, const void* v_new, int32_t dtype,
+                                     void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  return do_append(p, n_seqs, seqs, layer_begin, layer_count, n_new, k_new, v_new, dtype,
+                   (cudaStream_t)stream);
+}
+
+krill_status_t krill_decode_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, const void* q,
+                                      int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                      void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
+                      (cudaStream_t)stream);
+}
+
+krill_status_t krill_decode_step(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                 int32_t layer_begin, int32_t layer_count, const void* k_new,
+                                 const void* v_new, int32_t kv_dtype, const void* q,
+                                 int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                 void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  TRY(do_append(p, n_seqs, seqs, layer_begin, layer_count, 1, k_new, v_new, kv_dtype,
+                (cudaStream_t)stream));
+  return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
+                      (cudaStream_t)stream);
+}
+
+krill_status_t krill_seq_snapshot_quantized(krill_pool_t p, krill_seq_t h, int32_t layer,
+                                            void* keys, void* values, void* key_scales,
+                                            void* key_zeros, void* value_scales,
+                                            void* value_zeros, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  DeviceGuard dg(p->device);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  int64_t p0, S;
+  layer_span(p, *s, layer, &p0, &S);
+  if (S == 0) return KRILL_OK;
+  StageSlot* slot;
+  TRY(upload_bt(p, *s, (cudaStream_t)stream, &slot));
+  GatherOut o{};
+  o.keys = (uint8_t*)keys;
+  o.values = (uint8_t*)values;
+  o.key_scales = (uint16_t*)key_scales;
+  o.key_zeros = (uint16_t*)key_zeros;
+  o.value_scales = (uint16_t*)value_scales;
+  o.value_zeros = (uint16_t*)value_zeros;
+  o.row_off = 0;
+  o.rows_total = S;
+  o.mode = 0;
+  CUDA_TRY(launch_gather(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S,
+                         o, (cudaStream_t)stream));
+  return stage_release(slot, (cudaStream_t)stream);
+}
+
+krill_status_t krill_seq_snapshot_dequantized(krill_pool_t p, krill_seq_t h, int32_t layer,
+                                              void* keys, void* values, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  DeviceGuard dg(p->device);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  int64_t p0, S;
+  layer_span(p, *s, layer, &p0, &S);
+  if (S == 0) return KRILL_OK;
+  StageSlot* slot;
+  TRY(upload_bt(p, *s, (cudaStream_t)stream, &slot));
+  GatherOut o{};
+  o.keys = (uint8_t*)keys;
+  o.values = (uint8_t*)values;
+  o.rows_total = S;
+  o.mode = 1;
+  CUDA_TRY(launch_gather(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S,
+                         o, (cudaStream_t)stream));
+  return stage_release(slot, (cudaStream_t)stream);
+}
+
+krill_status_t krill_seq_restore_quantized(krill_pool_t p, krill_seq_t h, int32_t layer,
+                                           int64_t rows, int64_t total_seen, const void* keys,
+                                           const void* values, const void* key_scales,
+                                           const void* key_zeros, const void* value_scales,
+                                           const void* value_zeros, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  DeviceGuard dg(p->device);
+  Seq* s = nullptr;
+  TRY(seq_get(p, h, &s));
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  ScatterIn in{};
+  in.keys = (const uint8_t*)keys;
+  in.values = (const uint8_t*)values;
+  in.key_scales = (const uint16_t*)key_scales;
+  in.key_zeros = (const uint16_t*)key_zeros;
+  in.value_scales = (const uint16_t*)value_scales;
+  in.value_zeros = (const uint16_t*)value_zeros;
+  in.row_off = 0;
+  in.rows_total = rows;
+  return do_restore(p, *s, layer, rows, total_seen, in, (cudaStream_t)stream);
+}
+
+krill_status_t krill_stack_left_padded(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                       int32_t layer, int64_t s_max, void* keys, void* values,
+                                       void* key_scales, void* key_zeros, void* value_scales,
+                                       void* value_zeros, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  DeviceGuard dg(p->device);
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  if (n_seqs <= 0) return KRILL_OK;
+  const Geom& g = p->geom;
+  cudaStream_t st = (cudaStream_t)stream;
+  std::vector<Seq*> sv(n_seqs);
+  for (int i = 0; i < n_seqs; ++i) {
+    TRY(seq_get(p, seqs[i], &sv[i]));
+    int64_t p0, S;
+    layer_span(p, *sv[i], layer, &p0, &S);
+    if (S > s_max) return fail(KRILL_ERR_INVALID, "row %d longer than s_max", i);
+  }
+  const size_t codes = (size_t)n_seqs * g.Hkv * s_max * g.D;
+  const size_t meta = (size_t)n_seqs * g.Hkv * s_max * g.NG * 2;
+  if (keys) CUDA_TRY(cudaMemsetAsync(keys, 0, codes, st));
+  if (values) CUDA_TRY(cudaMemsetAsync(values, 0, codes, st));
+  for (void* m : {key_scales, key_zeros, value_scales, value_zeros})
+    if (m) CUDA_TRY(cudaMemsetAsync(m, 0, meta, st));
+  for (int i = 0; i < n_seqs; ++i) {
+    int64_t p0, S;
+    layer_span(p, *sv[i], layer, &p0, &S);
+    if (S == 0) continue;
+    StageSlot* slot;
+    TRY(upload_bt(p, *sv[i], st, &slot));
+    const size_t co = (size_t)i * g.Hkv * s_max * g.D, mo = (size_t)i * g.Hkv * s_max * g.NG;
+    GatherOut o{};
+    o.keys = keys ? (uint8_t*)keys + co : nullptr;
+    o.values = values ? (uint8_t*)values + co : nullptr;
+    o.key_scales = key_scales ? (uint16_t*)key_scales + mo : nullptr;
+    o.key_zeros = key_zeros ? (uint16_t*)key_zeros + mo : nullptr;
+    o.value_scales = value_scales ? (uint16_t*)value_scales + mo : nullptr;
+    o.value_zeros = value_zeros ? (uint16_t*)value_zeros + mo : nullptr;
+    o.row_off = s_max - S;
+    o.rows_total = s_max;
+    o.mode = 0;
+    CUDA_TRY(launch_gather(g, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S, o, st));
+    TRY(stage_release(slot, st));
+  }
+  return KRILL_OK;
+}
+
+krill_status_t krill_scatter_back(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                  int32_t layer, const int64_t* base_lens, int64_t s_max,
+                                  int64_t steps, const void* keys, const void* values,
+                                  const void* key_scales, const void* key_zeros,
+                                  const void* value_scales, const void* value_zeros,
+                                  void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  DeviceGuard dg(p->device);
+  if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
+  if (n_seqs <= 0) return KRILL_OK;
+  if (!base_lens || steps < 0) return fail(KRILL_ERR_INVALID, "bad base_lens/steps");
+  const Geom& g = p->geom;
+  const int64_t width = s_max + steps;
+  for (int i = 0; i < n_seqs; ++i) {
+    Seq* s = nullptr;
+    TRY(seq_get(p, seqs[i], &s));
+    if (base_lens[i] < 0 || base_lens[i] > s_max) return fail(KRILL_ERR_INVALID, "bad base_len");
+    const int64_t rows = base_lens[i] + steps;
+    const size_t co = (size_t)i * g.Hkv * width * g.D, mo = (size_t)i * g.Hkv * width * g.NG;
+    ScatterIn in{};
+    in.keys = (const uint8_t*)keys + co;
+    in.values = (const uint8_t*)values + co;
+    in.key_scales = (const uint16_t*)key_scales + mo;
+    in.key_zeros = (const uint16_t*)key_zeros + mo;
+    in.value_scales = (const uint16_t*)value_scales + mo;
+    in.value_zeros = (const uint16_t*)value_zeros + mo;
+    in.row_off = s_max - base_lens[i];
+    in.rows_total = width;
+    int64_t total_seen = rows;
+    if (p->windowed()) total_seen = std::max<int64_t>(s->len[layer], rows);
+    TRY(do_restore(p, *s, layer, std::min<int64_t>(rows, p->windowed() ? p->ring_tokens() : rows),
+                   total_seen, in, (cudaStream_t)stream));
+  }
+  return KRILL_OK;
+}
+
+krill_status_t krill_build_decode_mask(const int64_t* lengths, int32_t n, int64_t s_max,
+                                       int64_t total_len, float* out) {
+  if (n < 0 || (n > 0 && (!lengths || !out)) || total_len < s_max)
+    return fail(KRILL_ERR_INVALID, "bad mask arguments");
+  for (int r = 0; r < n; ++r) {
+    const int64_t pad = s_max - lengths[r];
+    for (int64_t j = 0; j < total_len; ++j) out[(int64_t)r * total_len + j] = (j < pad) ? -10000.0f : 0.0f;
+  }
+  return KRILL_OK;
+}
+
+}  // extern "C"
+
+// =====================================================================
+// Prefix cache
+// =====================================================================
+struct krill_prefix_entry_s {
+  std::atomic<int> refs{1};  // one for the cache map + one per outstanding hit
+  uint64_t key = 0;
+  std::vector<int64_t> tokens;
+  std::string model, media;
+  std::vector<int32_t> blocks;
+  std::vector<int64_t> len, ret;
+  int64_t n_tokens = 0;
+};
+
+struct krill_prefix_s {
+  krill_pool_t pool = nullptr;
+  int max_entries = 8;
+  int min_len = 8;
+  std::unordered_map<uint64_t, krill_prefix_entry_t> map;
+  std::list<uint64_t> lru;  // front = least recently used
+  std::mutex mu;
+};
+
+namespace {
+
+constexpr uint8_t kKeySchema = 3;
+constexpr uint8_t kDtypeInt8 = 2;
+
+// FNV-1a 64 state after the key header (schema, dtype, model, 0xFF, media, 0xFF).
+uint64_t key_header(const char* model, const char* media, int dtype_tag) {
+  uint64_t h = 14695981039346656037ull;
+  auto mix = [&](uint8_t b) {
+    h ^= b;
+    h *= 1099511628211ull;
+  };
+  mix(kKeySchema);
+  mix((uint8_t)dtype_tag);
+  for (const char* c = model ? model : ""; *c; ++c) mix((uint8_t)*c);
+  mix(0xFF);
+  if (media)
+    for (const char* c = media; *c; ++c) mix((uint8_t)*c);
+  mix(0xFF);
+  return h;
+}
+uint64_t key_extend(uint64_t h, int64_t token) {
+  uint64_t t = (uint64_t)token;
+  for (int i = 0; i < 8; ++i) {
+    h ^= (uint8_t)(t >> (8 * i));
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+void entry_unref(krill_prefix_t pc, krill_prefix_entry_t e) {
+  if (e->refs.fetch_sub(1) == 1) {
+    std::lock_guard<std::recursive_mutex> lk(pc->pool->mu);
+    for (int32_t b : e->blocks) block_unref(pc->pool, b);
+    delete e;
+  }
+}
+
+void lru_touch(krill_prefix_t pc, uint64_t key) {
+  pc->lru.remove(key);
+  pc->lru.push_back(key);
+}
+
+void evict_locked(krill_prefix_t pc, uint64_t key) {
+  auto it = pc->map.find(key);
+  if (it == pc->map.end()) return;
+  krill_prefix_entry_t e = it->second;
+  pc->map.erase(it);
+  pc->lru.remove(key);
+  entry_unref(pc, e);
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t krill_prefix_key(const int64_t* tokens, int64_t n, const char* model_id,
+                          const char* media_hash, int32_t dtype_tag) {
+  uint64_t h = key_header(model_id, media_hash, dtype_tag);
+  for (int64_t i = 0; i < n; ++i) h = key_extend(h, tokens[i]);
+  return h;
+}
+
+krill_status_t krill_prefix_create(krill_pool_t pool, int32_t max_entries, int32_t min_len,
+                                   krill_prefix_t* out) {
+  if (!pool || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  if (max_entries <= 0) return fail(KRILL_ERR_INVALID, "max_memory_entries must be positive");
+  auto* pc = new krill_prefix_s();
+  pc->pool = pool;
+  pc->max_entries = max_entries;
+  pc->min_len = std::max(1, min_len);
+  *out = pc;
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_clear(krill_prefix_t pc) {
+  if (!pc) return fail(KRILL_ERR_INVALID, "null prefix cache");
+  std::lock_guard<std::mutex> lk(pc->mu);
+  std::vector<uint64_t> keys;
+  for (auto& kv : pc->map) keys.push_back(kv.first);
+  for (uint64_t k : keys) evict_locked(pc, k);
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_destroy(krill_prefix_t pc) {
+  if (!pc) return KRILL_OK;
+  krill_prefix_clear(pc);
+  delete pc;
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_memory_count(krill_prefix_t pc, int32_t* count) {
+  if (!pc || !count) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::mutex> lk(pc->mu);
+  *count = (int32_t)pc->map.size();
+  return KRILL_OK;
+}
+
+static void insert_locked(krill_prefix_t pc, krill_prefix_entry_t e) {
+  auto it = pc->map.find(e->key);
+  if (it != pc->map.end()) evict_locked(pc, e->key);  // same key: replace
+  while ((int)pc->map.size() >= pc->max_entries && !pc->lru.empty())
+    evict_locked(pc, pc->lru.front());
+  pc->map[e->key] = e;
+  pc->lru.push_back(e->key);
+}
+
+krill_status_t krill_prefix_store(krill_prefix_t pc, krill_seq_t seq, const int64_t* tokens,
+                                  int64_t n, const char* model_id, const char* media_hash) {
+  if (!pc) return fail(KRILL_ERR_INVALID, "null prefix cache");
+  if (n < pc->min_len) return KRILL_OK;  // PrefixCache.storeQuantized guard (:375)
+  if (!tokens) return fail(KRILL_ERR_INVALID, "null tokens");
+  krill_pool_t p = pc->pool;
+  auto* e = new krill_prefix_entry_s();
+  {
+    std::lock_guard<std::recursive_mutex> lk(p->mu);
+    Seq* s = nullptr;
+    krill_status_t st = seq_get(p, seq, &s);
+    if (st != KRILL_OK) {
+      delete e;
+      return st;
+    }
+    for (int L = 0; L < p->geom.L; ++L) {
+      const bool ok = p->windowed() ? s->len[L] == n : s->len[L] >= n;
+      if (!ok) {
+        delete e;
+        return fail(KRILL_ERR_INVALID, "layer %d holds %lld tokens, cannot store a %lld-token prefix",
+                    L, (long long)s->len[L], (long long)n);
+      }
+    }
+    if (p->windowed()) {
+      e->blocks = s->blocks;
+      e->len = s->len;
+      e->ret = s->ret;
+    } else {
+      const size_t nb = (size_t)((n + kBlockTokens - 1) / kBlockTokens);
+      e->blocks.assign(s->blocks.begin(), s->blocks.begin() + nb);
+      e->len.assign(p->geom.L, n);
+      e->ret.assign(p->geom.L, n);
+    }
+    for (int32_t b : e->blocks)
+      if (b >= 0) block_ref(p, b);
+  }
+  e->tokens.assign(tokens, tokens + n);
+  e->model = model_id ? model_id : "";
+  e->media = media_hash ? media_hash : "";
+  e->n_tokens = n;
+  e->key = krill_prefix_key(tokens, n, model_id, media_hash, kDtypeInt8);
+  std::lock_guard<std::mutex> lk(pc->mu);
+  insert_locked(pc, e);
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_lookup(krill_prefix_t pc, const int64_t* tokens, int64_t n,
+                                   const char* model_id, const char* media_hash,
+                                   krill_prefix_entry_t* entry, int64_t* prefix_length) {
+  if (!pc || !entry || !prefix_length) return fail(KRILL_ERR_INVALID, "null argument");
+  *entry = nullptr;
+  *prefix_length = 0;
+  if (n < pc->min_len || !tokens) return KRILL_ERR_NOT_FOUND;
+  // Running FNV-1a over the tokens gives the key of every prefix length in one
+  // pass; probe in the reference's scan order (PrefixCache.swift:283-305).
+  std::vector<uint64_t> keys((size_t)n + 1);
+  keys[0] = key_header(model_id, media_hash, kDtypeInt8);
+  for (int64_t i = 0; i < n; ++i) keys[i + 1] = key_extend(keys[i], tokens[i]);
+  const int64_t step = std::max(1, pc->min_len / 2);
+  std::lock_guard<std::mutex> lk(pc->mu);
+  for (int64_t check = n; check >= pc->min_len; check -= step) {
+    auto it = pc->map.find(keys[check]);
+    if (it == pc->map.end()) continue;
+    lru_touch(pc, it->first);
+    it->second->refs.fetch_add(1);
+    *entry = it->second;
+    *prefix_length = check;
+    return KRILL_OK;
+  }
+  return KRILL_ERR_NOT_FOUND;
+}
+
+krill_status_t krill_prefix_lookup_longest(krill_prefix_t pc, const int64_t* tokens, int64_t n,
+                                           const char* model_id, const char* media_hash,
+                                           krill_prefix_entry_t* entry, int64_t* prefix_length) {
+  if (!pc || !entry || !prefix_length) return fail(KRILL_ERR_INVALID, "null argument");
+  *entry = nullptr;
+  *prefix_length = 0;
+  if (n < pc->min_len || !tokens) return KRILL_ERR_NOT_FOUND;
+  const std::string model = model_id ? model_id : "", media = media_hash ? media_hash : "";
+  std::lock_guard<std::mutex> lk(pc->mu);
+  krill_prefix_entry_t best = nullptr;
+  int64_t best_len = 0;
+  for (auto& kv : pc->map) {
+    krill_prefix_entry_t e = kv.second;
+    if (e->model != model || e->media != media || e->tokens.empty()) continue;
+    const int64_t m = std::min<int64_t>(n, (int64_t)e->tokens.size());
+    int64_t i = 0;
+    while (i < m && tokens[i] == e->tokens[i]) ++i;
+    if (i >= pc->min_len && i > best_len) {
+      best_len = i;
+      best = e;
+    }
+  }
+  if (!best) return KRILL_ERR_NOT_FOUND;
+  lru_touch(pc, best->key);
+  best->refs.fetch_add(1);
+  *entry = best;
+  *prefix_length = best_len;
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_entry_length(krill_prefix_entry_t e, int64_t* stored_length) {
+  if (!e || !stored_length) return fail(KRILL_ERR_INVALID, "null argument");
+  *stored_length = e->n_tokens;
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_entry_release(krill_prefix_t pc, krill_prefix_entry_t e) {
+  if (!pc || !e) return fail(KRILL_ERR_INVALID, "null argument");
+  entry_unref(pc, e);
+  return KRILL_OK;
+}
+
+krill_status_t krill_seq_fork_prefix(krill_prefix_t pc, krill_prefix_entry_t e, int64_t keep,
+                                     krill_seq_t* out) {
+  if (!pc || !e || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  krill_pool_t p = pc->pool;
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (keep < 0 || keep > e->n_tokens)
+    return fail(KRILL_ERR_INVALID, "keep %lld outside [0, %lld]", (long long)keep, (long long)e->n_tokens);
+  if (p->windowed())
+    for (int L = 0; L < p->geom.L; ++L)
+      if (keep < e->len[L] - e->ret[L])
+        return fail(KRILL_ERR_INVALID, "keep %lld below the retained window of layer %d",
+                    (long long)keep, L);
+  Seq* s = nullptr;
+  TRY(seq_new(p, out, &s));
+  if (p->windowed()) {
+    s->blocks = e->blocks;
+    for (int L = 0; L < p->geom.L; ++L) {
+      s->len[L] = keep;
+      s->ret[L] = e->ret[L] - (e->len[L] - keep);
+    }
+  } else {
+    const size_t nb = (size_t)((keep + kBlockTokens - 1) / kBlockTokens);
+    s->blocks.assign(e->blocks.begin(), e->blocks.begin() + nb);
+    std::fill(s->len.begin(), s->len.end(), keep);
+    std::fill(s->ret.begin(), s->ret.end(), keep);
+  }
+  for (int32_t b : s->blocks)
+    if (b >= 0) block_ref(p, b);
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
+                                       krill_prefix_entry_t se, void* stream,
+                                       krill_prefix_entry_t* out) {
+  if (!dst || !src || !se || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  krill_pool_t dp = dst->pool, sp = src->pool;
+  if (dp->host_only || sp->host_only) return fail(KRILL_ERR_NO_DEVICE, "peer fetch needs device pools");
+  const Geom &a = dp->geom, &b = sp->geom;
+  if (a.L != b.L || a.Hkv != b.Hkv || a.D != b.D || a.G != b.G || a.ring != b.ring ||
+      dp->cfg.window != sp->cfg.window)
+    return fail(KRILL_ERR_INVALID, "peer fetch between pools of different geometry");
+  auto* e = new krill_prefix_entry_s();
+  {
+    std::lock_guard<std::recursive_mutex> lk(dp->mu);
+    DeviceGuard dg(dp->device);
+    if (dp->device != sp->device) {
+      int can = 0;
+      cudaDeviceCanAccessPeer(&can, dp->device, sp->device);
+      if (can) {
+        cudaError_t pe = cudaDeviceEnablePeerAccess(sp->device, 0);
+        if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) {
+          delete e;
+          return fail(KRILL_ERR_PEER, "cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(pe));
+        }
+        cudaGetLastError();
+      }
+    }
+    e->blocks.assign(se->blocks.size(), -1);
+    for (size_t i = 0; i < se->blocks.size(); ++i) {
+      if (se->blocks[i] < 0) continue;
+      krill_status_t st = block_alloc(dp, &e->blocks[i]);
+      if (st != KRILL_OK) {
+        for (int32_t bb : e->blocks) block_unref(dp, bb);
+        delete e;
+        return st;
+      }
+      cudaError_t ce = cudaMemcpyPeerAsync(dp->block_ptr(e->blocks[i]), dp->device,
+                                           sp->block_ptr(se->blocks[i]), sp->device,
+                                           (size_t)a.block_bytes, (cudaStream_t)stream);
+      if (ce != cudaSuccess) {
+        for (int32_t bb : e->blocks) block_unref(dp, bb);
+        delete e;
+        return fail(KRILL_ERR_PEER, "cudaMemcpyPeerAsync: %s", cudaGetErrorString(ce));
+      }
+    }
+  }
+  e->key = se->key;
+  e->tokens = se->tokens;
+  e->model = se->model;
+  e->media = se->media;
+  e->len = se->len;
+  e->ret = se->ret;
+  e->n_tokens = se->n_tokens;
+  std::lock_guard<std::mutex> lk(dst->mu);
+  insert_locked(dst, e);
+  e->refs.fetch_add(1);
+  *out = e;
+  return KRILL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+// internal.h — declarations shared between the host library (host.cpp) and
+// the CUDA kernels. Not part of the public ABI (that is include/krill_kv.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kv_common.cuh"
+
+namespace krill {
+
+// Destination of one appended token for one (layer, seq): the physical block
+// and the absolute position (slot = pos % 256).
+struct AppendDst {
+  int32_t block;
+  int32_t pos;
+};
+
+struct GatherOut {
+  uint8_t* keys;          // mode 0: u8 codes; mode 1: f16
+  uint8_t* values;
+  uint16_t* key_scales;   // f16 bits (mode 0 only)
+  uint16_t* key_zeros;
+  uint16_t* value_scales;
+  uint16_t* value_zeros;
+  int64_t row_off;        // first output row (stacking)
+  int64_t rows_total;     // output rows per head
+  int mode;               // 0 = raw codes + meta, 1 = dequantized f16
+};
+
+struct ScatterIn {
+  const uint8_t* keys;
+  const uint8_t* values;
+  const uint16_t* key_scales;
+  const uint16_t* key_zeros;
+  const uint16_t* value_scales;
+  const uint16_t* value_zeros;
+  int64_t row_off;
+  int64_t rows_total;
+};
+
+// One decode-attention unit: (layer, sequence, kv-head) with its valid token
+// positions [t_lo, t_hi). Its sub-block range is split into n_items items.
+struct AttnUnit {
+  int32_t qo_row;      // li * n_seqs + si : row of q/out
+  int32_t si;          // sequence index in the call (block-table row)
+  int32_t layer;       // absolute layer in the pool
+  int32_t h;           // kv head
+  int32_t t_lo, t_hi;  // attended positions
+  int32_t first_item;  // partial-slot base
+  int32_t n_items;
+};
+
+struct AttnItem {
+  int32_t unit;
+  int32_t sb_begin;  // logical sub-block range (positions 64*sb ...)
+  int32_t sb_end;
+  int32_t idx;       // item index within its unit
+};
+
+struct AttnParams {
+  const uint8_t* pool;
+  int64_t page_bytes, sb_bytes;
+  int L, Hkv, Hq, g, ring;
+  const AttnUnit* units;
+  const AttnItem* items;
+  const int32_t* cta_off;  // [grid + 1] item ranges per CTA
+  const int32_t* bt;       // [n_seqs][bt_stride]
+  int bt_stride;
+  const void* q;
+  int q_dtype;
+  void* out;
+  int out_dtype;
+  float scale_log2;  // softmax scale * log2(e)
+  float* partials;   // [items][16 + 8*D]
+  int* counters;     // [units], zero between launches
+  int* err;
+};
+
+cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
+                          int layer_count, int n_seqs, int n_new, const void* k, const void* v,
+                          int dtype, cudaStream_t stream);
+cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const int32_t* d_bt,
+                          int64_t p0, int64_t S, const GatherOut& out, cudaStream_t stream);
+cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
+                           int64_t S, const ScatterIn& in, cudaStream_t stream);
+// grid = number of persistent CTAs (cta_off has grid + 1 entries).
+cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
+                             cudaStream_t stream);
+// Floats per partial record for head_dim D.
+__host__ __device__ inline int64_t partial_floats(int D) { return 16 + 8 * (int64_t)D; }
+
+}  // namespace krill

@@ -1,0 +1,519 @@
+// kv_attn.cu — int8 decode attention, dequantize fused into q·Kᵀ and ·V.
+//
+// Replaces, for one query token per (layer, sequence): the full-cache
+// dequantize of QuantizedKVCache.update (Sources/KrillCache/QuantizedKVCache.swift:71-74,
+// dequantize :200-204) and MLXFast.scaledDotProductAttention with GQA
+// (Sources/KrillCore/Gemma4Model.swift:516, Attention.swift:95). K/V are
+// dequantized tile by tile with the reference's two fp16 roundings, so the
+// only differences from the reference math are fp32 accumulation order and
+// the fp16 rounding of the softmax weights fed to the ·V product.
+//
+// Structure (persistent, one CTA per SM):
+//   - the host plans work items = (layer, seq, kv-head, range of 64-token
+//     sub-blocks) and assigns them to CTAs by longest-processing-time;
+//   - a producer warp streams each item's sub-blocks HBM -> shared memory with
+//     bulk async copies (cp.async.bulk, no multicast) into an NSTAGE ring
+//     guarded by mbarriers;
+//   - NCW consumer warps take the item's sub-blocks round-robin. Tensor-core
+//     path (mma.sync m16n8k16, f16 in / f32 accumulate):
+//        Sᵀ[16 tok × 8 heads] = Kdeq[16 tok × D] · Qᵀ[D × 8]   (GQA group <= 8)
+//        Oᵀ[D × 8]           += Vdeqᵀ[D × 16 tok] · Pᵀ[16 tok × 8]
+//     with Pᵀ obtained from the Sᵀ accumulators by movmatrix.trans, online
+//     softmax in the exp2 domain;
+//   - warps combine in shared memory; a unit split over several items writes
+//     fp32 partials and the last CTA to finish (atomic counter) merges them.
+// Every mbarrier wait is bounded; on timeout the kernel raises an error flag
+// and runs to completion instead of hanging.
+#include "internal.h"
+
+namespace krill {
+namespace {
+
+constexpr int kConsumerBar = 1;  // named barrier id for consumer warps
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return done;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after ~2 s (or ~1 ms once the CTA has already seen a
+// timeout), records the error and returns false.
+__device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort, int* err) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t limit = *cta_abort ? 1000000ull : 2000000000ull;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (globaltimer() - t0 > limit) {
+      *cta_abort = 1;
+      atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Two u8 codes (bytes selected by `sel` from w) -> f16x2 dequantized with the
+// reference's rounding: f16_rn(f16_rn(c * s) + z). PRMT builds 1024 + c
+// exactly (exponent byte 0x64), the subtraction of 1024 is exact.
+__device__ __forceinline__ uint32_t deq2(uint32_t w, uint32_t sel, uint32_t s2, uint32_t z2) {
+  __half2 c = u2h(__byte_perm(w, 0x64646464u, sel));
+  c = __hsub2_rn(c, u2h(0x64006400u));
+  c = __hmul2_rn(c, u2h(s2));
+  c = __hadd2_rn(c, u2h(z2));
+  return h2u(c);
+}
+
+template <int D, int NG>
+struct SubGeom {
+  static constexpr int G = D / NG;
+  static constexpr int SB = 64 * (2 * D + 8 * NG);
+  static constexpr int VOFF = 64 * D;
+  static constexpr int META = 128 * D;
+  // meta array a, group gi, token t -> byte offset
+  static __device__ __forceinline__ int meta(int a, int gi, int t) {
+    return META + (a * NG + gi) * 128 + t * 2;
+  }
+};
+
+template <int D>
+struct TCState {
+  float o[D / 16][4];
+  float m[2], l[2];
+  uint32_t qf[D / 64][8];
+};
+
+__device__ __forceinline__ uint32_t f2h2(float lo, float hi) {
+  return h2u(__floats2half2_rn(lo, hi));
+}
+
+// Load this lane's Qᵀ fragments for one unit: q[head = r][16*(tig+4hh) + 0..15].
+template <int D>
+__device__ __forceinline__ void load_q(TCState<D>& st, const void* q, int q_dtype, int64_t row_elem,
+                                       int g, int lane) {
+  const int r = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int hh = 0; hh < D / 64; ++hh) {
+    if (r < g) {
+      const int64_t e = row_elem + (int64_t)r * D + 16 * (tig + 4 * hh);
+      const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q) + e);
+      uint4 a = __ldg(p), b = __ldg(p + 1);
+      uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
+          __nv_bfloat162 bv = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
+          float2 f = __bfloat1622float2(bv);
+          w[i] = f2h2(f.x, f.y);
+        }
+        st.qf[hh][i] = w[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) st.qf[hh][i] = 0u;
+    }
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void reset_state(TCState<D>& st) {
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) st.o[mt][c] = 0.f;
+  st.m[0] = st.m[1] = -INFINITY;
+  st.l[0] = st.l[1] = 0.f;
+}
+
+// Process one 64-token sub-block resident in shared memory at `sb`.
+// pos0 = absolute position of its token 0; tokens outside [t_lo, t_hi) are
+// masked (only checked when `boundary`).
+template <int D, int NG>
+__device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCState<D>& st,
+                                            int lane, float scale_log2, bool boundary, int pos0,
+                                            int t_lo, int t_hi) {
+  using SG = SubGeom<D, NG>;
+  constexpr bool SWZ = D >= 128;
+  const int r = lane >> 2, tig = lane & 3;
+  const uint32_t selh = (r & 1) ? 0x3232u : 0x1010u;
+
+  // ---- K phase: Sᵀ = Kdeq · Qᵀ for 4 m-tiles of 16 tokens ----
+  float s[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int tbase = 16 * (r >> 1) + 4 * u;
+    const int ta = tbase + (r & 1);
+    const int tb = ta + 2;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      const int grp = (64 * hh) / SG::G;
+      const int chunk = tig + 4 * hh;
+      const int phys = SWZ ? (chunk ^ ((r & 1) << 2)) : chunk;
+      const uint4 wa = *reinterpret_cast<const uint4*>(sb + ta * D + phys * 16);
+      const uint4 wb = *reinterpret_cast<const uint4*>(sb + tb * D + phys * 16);
+      const uint2 ks4 = *reinterpret_cast<const uint2*>(sb + SG::meta(0, grp, tbase));
+      const uint2 kz4 = *reinterpret_cast<const uint2*>(sb + SG::meta(1, grp, tbase));
+      const uint32_t sA = __byte_perm(ks4.x, 0, selh), sB = __byte_perm(ks4.y, 0, selh);
+      const uint32_t zA = __byte_perm(kz4.x, 0, selh), zB = __byte_perm(kz4.y, 0, selh);
+      const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t a0 = deq2(wav[k], 0x4140u, sA, zA);
+        const uint32_t a1 = deq2(wbv[k], 0x4140u, sB, zB);
+        const uint32_t a2 = deq2(wav[k], 0x4342u, sA, zA);
+        const uint32_t a3 = deq2(wbv[k], 0x4342u, sB, zB);
+        mma16816(acc, a0, a1, a2, a3, st.qf[hh][2 * k], st.qf[hh][2 * k + 1]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[u][c] = acc[c] * scale_log2;
+    if (boundary) {
+      const int pa = pos0 + ta, pb = pos0 + tb;
+      if (pa < t_lo || pa >= t_hi) s[u][0] = s[u][1] = -INFINITY;
+      if (pb < t_lo || pb >= t_hi) s[u][2] = s[u][3] = -INFINITY;
+    }
+  }
+
+  // ---- online softmax (heads 2*tig, 2*tig+1 live in this lane) ----
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
+    mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(st.m[0], mx0), mn1 = fmaxf(st.m[1], mx1);
+  const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
+  const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+  const float al0 = exp2f(st.m[0] - b0), al1 = exp2f(st.m[1] - b1);
+  st.m[0] = mn0;
+  st.m[1] = mn1;
+  float ps0 = 0.f, ps1 = 0.f;
+  uint32_t pb[4][2];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float p0 = exp2f(s[u][0] - b0), p1 = exp2f(s[u][1] - b1);
+    const float p2 = exp2f(s[u][2] - b0), p3 = exp2f(s[u][3] - b1);
+    ps0 += p0 + p2;
+    ps1 += p1 + p3;
+    pb[u][0] = movm_trans(f2h2(p0, p1));
+    pb[u][1] = movm_trans(f2h2(p2, p3));
+  }
+  st.l[0] = st.l[0] * al0 + ps0;
+  st.l[1] = st.l[1] * al1 + ps1;
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    st.o[mt][0] *= al0;
+    st.o[mt][1] *= al1;
+    st.o[mt][2] *= al0;
+    st.o[mt][3] *= al1;
+  }
+
+  // ---- V phase: Oᵀ += Vdeqᵀ · Pᵀ ----
+  const uint8_t* vt = sb + SG::VOFF;
+#pragma unroll
+  for (int grp = 0; grp < NG; ++grp) {
+    const uint4 s_lo = *reinterpret_cast<const uint4*>(sb + SG::meta(2, grp, 16 * tig));
+    const uint4 s_hi = *reinterpret_cast<const uint4*>(sb + SG::meta(2, grp, 16 * tig + 8));
+    const uint4 z_lo = *reinterpret_cast<const uint4*>(sb + SG::meta(3, grp, 16 * tig));
+    const uint4 z_hi = *reinterpret_cast<const uint4*>(sb + SG::meta(3, grp, 16 * tig + 8));
+    uint32_t vs[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
+    uint32_t vz[8] = {z_lo.x, z_lo.y, z_lo.z, z_lo.w, z_hi.x, z_hi.y, z_hi.z, z_hi.w};
+    if (boundary) {
+      // Invalid tokens get scale = zero = 0 so their (possibly stale) codes
+      // dequantize to exactly 0 and cannot inject non-finite values.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int p = pos0 + 16 * tig + 2 * i;
+        const uint32_t m = ((p >= t_lo && p < t_hi) ? 0x0000ffffu : 0u) |
+                           ((p + 1 >= t_lo && p + 1 < t_hi) ? 0xffff0000u : 0u);
+        vs[i] &= m;
+        vz[i] &= m;
+      }
+    }
+#pragma unroll
+    for (int mi = 0; mi < SG::G / 16; ++mi) {
+      const int mt = grp * (SG::G / 16) + mi;
+      const int d = 16 * mt + r;
+      const uint4 x = *reinterpret_cast<const uint4*>(vt + d * 64 + 16 * tig);
+      const uint4 y = *reinterpret_cast<const uint4*>(vt + (d + 8) * 64 + 16 * tig);
+      const uint32_t xv[4] = {x.x, x.y, x.z, x.w};
+      const uint32_t yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t a0 = deq2(xv[u], 0x4140u, vs[2 * u], vz[2 * u]);
+        const uint32_t a1 = deq2(yv[u], 0x4140u, vs[2 * u], vz[2 * u]);
+        const uint32_t a2 = deq2(xv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
+        const uint32_t a3 = deq2(yv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
+        mma16816(st.o[mt], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_out(void* out, int dtype, int64_t i, float v) {
+  if (dtype == 0)
+    reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+  else if (dtype == 1)
+    reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(out)[i] = v;
+}
+
+template <int D, int NG, int NCW, int NSTAGE>
+struct AttnSmem {
+  static constexpr int SB = SubGeom<D, NG>::SB;
+  static constexpr int STAGE_BYTES = NSTAGE * SB;
+  static constexpr int BAR_OFF = STAGE_BYTES;                      // 2*NSTAGE u64
+  static constexpr int CM_OFF = BAR_OFF + 2 * NSTAGE * 8;          // [NCW][8] f32
+  static constexpr int CL_OFF = CM_OFF + NCW * 8 * 4;              // [NCW][8] f32
+  static constexpr int CO_OFF = CL_OFF + NCW * 8 * 4;              // [NCW][8][D] f32
+  static constexpr int MISC_OFF = CO_OFF + NCW * 8 * D * 4;        // abort flag, last flag
+  static constexpr int TOTAL = MISC_OFF + 16;
+};
+
+template <int D, int NG, int NCW, int NSTAGE>
+__global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p) {
+  using SM = AttnSmem<D, NG, NCW, NSTAGE>;
+  constexpr int SB = SM::SB;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  const uint32_t bar_base = smem_u32(smem + SM::BAR_OFF);
+  float* cm = reinterpret_cast<float*>(smem + SM::CM_OFF);
+  float* cl = reinterpret_cast<float*>(smem + SM::CL_OFF);
+  float* cO = reinterpret_cast<float*>(smem + SM::CO_OFF);
+  volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(bar_base + 8 * s, 1);             // full: producer arrive + tx
+      mbar_init(bar_base + 8 * (NSTAGE + s), 1);  // empty: one consumer warp
+    }
+    *cta_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int it0 = p.cta_off[blockIdx.x], it1 = p.cta_off[blockIdx.x + 1];
+
+  if (warp == NCW) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t J = 0;
+      for (int it = it0; it < it1; ++it) {
+        const AttnItem item = p.items[it];
+        const AttnUnit un = p.units[item.unit];
+        const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
+        const uint8_t* head_base = p.pool + ((int64_t)un.layer * p.Hkv + un.h) * p.page_bytes;
+        const int64_t blk_stride = (int64_t)p.L * p.Hkv * p.page_bytes;
+        for (int j = item.sb_begin; j < item.sb_end; ++j, ++J) {
+          const uint32_t stage = J % NSTAGE;
+          if (J >= (uint32_t)NSTAGE)
+            mbar_wait(bar_base + 8 * (NSTAGE + stage), ((J / NSTAGE) - 1) & 1, cta_abort, p.err);
+          int bi = j >> 2;
+          if (p.ring > 0) bi %= p.ring;
+          const uint8_t* src = head_base + (int64_t)bt[bi] * blk_stride + (int64_t)(j & 3) * SB;
+          const uint32_t full = bar_base + 8 * stage;
+          mbar_expect_tx(full, SB);
+          bulk_g2s(smem_u32(stages + (size_t)stage * SB), src, SB, full);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  TCState<D> st;
+  uint32_t J = 0;
+  const int g = p.g;
+  for (int it = it0; it < it1; ++it) {
+    const AttnItem item = p.items[it];
+    const AttnUnit un = p.units[item.unit];
+    const int n_sb = item.sb_end - item.sb_begin;
+    reset_state(st);
+    const int64_t q_row = ((int64_t)un.qo_row * p.Hq + (int64_t)un.h * g) * D;
+    if (warp < n_sb) load_q<D>(st, p.q, p.q_dtype, q_row, g, lane);
+    for (int k = warp; k < n_sb; k += NCW) {
+      const uint32_t jj = J + k;
+      const uint32_t stage = jj % NSTAGE;
+      mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
+      const int j = item.sb_begin + k;
+      const int pos0 = j * 64;
+      const bool boundary = pos0 < un.t_lo || pos0 + 64 > un.t_hi;
+      tc_subblock<D, NG>(stages + (size_t)stage * SB, st, lane, p.scale_log2, boundary, pos0,
+                         un.t_lo, un.t_hi);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
+    }
+    J += n_sb;
+
+    // ---- combine the warps' states for this item ----
+    float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    named_bar(kConsumerBar, NCW * 32);  // previous item's combine reads are done
+    {
+      const int r = lane >> 2, tig = lane & 3;
+      if (r == 0) {
+        cm[warp * 8 + 2 * tig] = st.m[0];
+        cm[warp * 8 + 2 * tig + 1] = st.m[1];
+        cl[warp * 8 + 2 * tig] = l0;
+        cl[warp * 8 + 2 * tig + 1] = l1;
+      }
+      float* co = cO + (size_t)warp * 8 * D;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        const int d = 16 * mt + r;
+        co[(2 * tig) * D + d] = st.o[mt][0];
+        co[(2 * tig + 1) * D + d] = st.o[mt][1];
+        co[(2 * tig) * D + d + 8] = st.o[mt][2];
+        co[(2 * tig + 1) * D + d + 8] = st.o[mt][3];
+      }
+    }
+    named_bar(kConsumerBar, NCW * 32);
+    const bool split = un.n_items > 1;
+    float* part = p.partials + (int64_t)(un.first_item + item.idx) * partial_floats(D);
+    const int64_t out_row = ((int64_t)un.qo_row * p.Hq + (int64_t)un.h * g) * D;
+    for (int idx = tid; idx < g * D; idx += NCW * 32) {
+      const int h = idx / D, d = idx - h * D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) M = fmaxf(M, cm[w * 8 + h]);
+      float Ls = 0.f, Os = 0.f;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) {
+        const float mw = cm[w * 8 + h];
+        const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+        Ls += cl[w * 8 + h] * f;
+        Os += cO[((size_t)w * 8 + h) * D + d] * f;
+      }
+      if (!split) {
+        store_out(p.out, p.out_dtype, out_row + idx, Os / Ls);
+      } else {
+        part[16 + h * D + d] = Os;
+        if (d == 0) {
+          part[h] = M;
+          part[8 + h] = Ls;
+        }
+      }
+    }
+    if (split) {
+      __threadfence();
+      named_bar(kConsumerBar, NCW * 32);
+      if (tid == 0) {
+        const int old = atomicAdd(&p.counters[item.unit], 1);
+        *last_flag = (old == un.n_items - 1);
+      }
+      named_bar(kConsumerBar, NCW * 32);
+      if (*last_flag) {
+        __threadfence();
+        const float* pb = p.partials + (int64_t)un.first_item * partial_floats(D);
+        for (int idx = tid; idx < g * D; idx += NCW * 32) {
+          const int h = idx / D, d = idx - h * D;
+          float M = -INFINITY;
+          for (int i = 0; i < un.n_items; ++i) M = fmaxf(M, __ldcg(pb + i * partial_floats(D) + h));
+          float Ls = 0.f, Os = 0.f;
+          for (int i = 0; i < un.n_items; ++i) {
+            const float* pr = pb + i * partial_floats(D);
+            const float mi = __ldcg(pr + h);
+            const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
+            Ls += __ldcg(pr + 8 + h) * f;
+            Os += __ldcg(pr + 16 + h * D + d) * f;
+          }
+          store_out(p.out, p.out_dtype, out_row + idx, Os / Ls);
+        }
+        if (tid == 0) p.counters[item.unit] = 0;
+      }
+    }
+  }
+}
+
+template <int D, int NG, int NCW, int NSTAGE>
+cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
+  using SM = AttnSmem<D, NG, NCW, NSTAGE>;
+  static_assert(SM::TOTAL <= 232448, "shared memory budget");
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, NSTAGE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  attn_tc_kernel<D, NG, NCW, NSTAGE><<<grid, (NCW + 1) * 32, SM::TOTAL, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
+                             cudaStream_t stream) {
+  if (grid <= 0) return cudaSuccess;
+  (void)impl;
+  if (g.D == 64 && g.NG == 1) return launch_tc<64, 1, 8, 16>(p, grid, stream);
+  if (g.D == 128 && g.NG == 2) return launch_tc<128, 2, 8, 11>(p, grid, stream);
+  if (g.D == 128 && g.NG == 1) return launch_tc<128, 1, 8, 11>(p, grid, stream);
+  if (g.D == 256 && g.NG == 4) return launch_tc<256, 4, 4, 5>(p, grid, stream);
+  if (g.D == 256 && g.NG == 2) return launch_tc<256, 2, 4, 5>(p, grid, stream);
+  if (g.D == 256 && g.NG == 1) return launch_tc<256, 1, 4, 5>(p, grid, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace krill

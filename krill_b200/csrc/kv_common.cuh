@@ -1,0 +1,91 @@
+// kv_common.cuh — page geometry and device helpers shared by the kernels.
+//
+// HBM layout of one pool (one layer group on one GPU):
+//   pool = blocks[num_blocks]; block = pages[num_layers][num_kv_heads];
+//   page = 256 tokens = 4 sub-blocks of 64 tokens; each sub-block is one
+//   contiguous run of SB = 64 * (2*D + 8*NG) bytes:
+//     [0, 64*D)            K codes, token-major rows of D bytes; for D >= 128
+//                          the 16-byte chunks of odd rows are XOR-swizzled by 4
+//                          so the decode kernel's shared-memory reads are
+//                          bank-conflict free
+//     [64*D, 128*D)        V codes transposed: D rows of 64 token bytes, so the
+//                          tensor-core B/A fragments along the token axis are
+//                          contiguous bytes
+//     [128*D, +128*NG)     K scales  [NG][64] f16
+//     [+128*NG, +256*NG)   K zeros   [NG][64] f16
+//     [+256*NG, +384*NG)   V scales  [NG][64] f16
+//     [+384*NG, +512*NG)   V zeros   [NG][64] f16
+// A sub-block is the unit one bulk (TMA) copy moves into shared memory.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace krill {
+
+constexpr int kBlockTokens = 256;
+constexpr int kSubTokens = 64;
+constexpr int kSubPerBlock = kBlockTokens / kSubTokens;
+
+struct Geom {
+  int L;        // layers in the pool
+  int Hkv;      // kv heads
+  int Hq;       // query heads
+  int g;        // Hq / Hkv
+  int D;        // head dim
+  int G;        // group size
+  int NG;       // D / G
+  int ring;     // blocks in a windowed sequence's ring; 0 = full history
+  int window;   // sliding window (tokens); 0 = full history
+  int quant_variant;
+  int64_t sb_bytes;
+  int64_t page_bytes;
+  int64_t block_bytes;
+};
+
+inline Geom make_geom(int L, int Hkv, int Hq, int D, int G, int ring, int window, int qv) {
+  Geom g;
+  g.L = L; g.Hkv = Hkv; g.Hq = Hq; g.g = Hq / Hkv; g.D = D; g.G = G; g.NG = D / G;
+  g.ring = ring; g.window = window; g.quant_variant = qv;
+  g.sb_bytes = (int64_t)kSubTokens * (2 * D + 8 * g.NG);
+  g.page_bytes = g.sb_bytes * kSubPerBlock;
+  g.block_bytes = g.page_bytes * L * Hkv;
+  return g;
+}
+
+// Byte offsets inside a sub-block.
+__host__ __device__ inline int64_t sb_voff(int D) { return (int64_t)kSubTokens * D; }
+__host__ __device__ inline int64_t sb_meta_off(int D) { return (int64_t)2 * kSubTokens * D; }
+// meta array a (0 = K scale, 1 = K zero, 2 = V scale, 3 = V zero), group gi, token t
+__host__ __device__ inline int64_t sb_meta(int D, int NG, int a, int gi, int t) {
+  return sb_meta_off(D) + ((int64_t)(a * NG + gi) * kSubTokens + t) * 2;
+}
+// Physical byte offset of K code (token t in sub-block, element d).
+__host__ __device__ inline int64_t sb_kcode(int D, int t, int d) {
+  int chunk = d >> 4;
+  if (D >= 128) chunk ^= (t & 1) << 2;
+  return (int64_t)t * D + chunk * 16 + (d & 15);
+}
+__host__ __device__ inline int64_t sb_vcode(int D, int t, int d) {
+  return sb_voff(D) + (int64_t)d * kSubTokens + t;
+}
+
+// Error flag bits written by kernels (pool-owned int, read + cleared by host).
+constexpr int kErrTimeout = 1;
+constexpr int kErrBadArg = 2;
+
+#ifdef __CUDACC__
+__device__ inline float load_in(const void* p, int64_t i, int dtype) {
+  return dtype == 0 ? __half2float(reinterpret_cast<const __half*>(p)[i])
+                    : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+// Round a float to the input dtype (f16 or bf16), RN-even, back to float.
+__device__ inline float round_in(float v, int dtype) {
+  return dtype == 0 ? __half2float(__float2half_rn(v)) : __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ inline uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+#endif
+
+}  // namespace krill

@@ -1,0 +1,283 @@
+// kv_ops.cu — fused quantize+append, and the gather/scatter kernels behind
+// snapshots, restores and the continuous-batch stack/scatter glue.
+//
+// Quantizer: reference QuantizedKVCache.quantizePerHead
+// (Sources/KrillCache/QuantizedKVCache.swift:181-197), applied per
+// `group_size` slice of head_dim. Every rounding step is the reference's
+// (MLX CPU-device semantics), so codes, scales and zeros are bit-exact:
+//   mn/mx exact; d = rn_in(mx - mn); scale = max(d / 255f, 1e-8f) in f32
+//   (IEEE divide, __fdiv_rn); code = trunc(clip(rn_in(x - mn) / scale, 0, 255));
+//   stored scale f16_rn(scale), zero f16_rn(mn).
+// Dequantize (:200-204): f16_rn(f16_rn(f16(code) * scale) + zero).
+#include "internal.h"
+
+namespace krill {
+namespace {
+
+template <int EPL>
+struct VecIn;  // EPL 16-bit inputs per lane
+template <> struct VecIn<2> { using T = uint32_t; };
+template <> struct VecIn<4> { using T = uint2; };
+template <> struct VecIn<8> { using T = uint4; };
+
+__device__ inline float bits_to_float(uint16_t b, int dtype) {
+  return dtype == 0 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// Quantize EPL elements held by this lane; lanes [k*LPG, (k+1)*LPG) form one
+// group. Returns codes packed little-endian in `codes`, plus the group's f16
+// scale / zero bits.
+template <int EPL, int LPG>
+__device__ inline void quantize_lane(const float (&x)[EPL], int dtype, int variant,
+                                     uint8_t (&codes)[EPL], uint16_t& s16, uint16_t& z16) {
+  float mn = x[0], mx = x[0];
+#pragma unroll
+  for (int e = 1; e < EPL; ++e) { mn = fminf(mn, x[e]); mx = fmaxf(mx, x[e]); }
+#pragma unroll
+  for (int off = 1; off < LPG; off <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  }
+  float d = round_in(mx - mn, dtype);
+  float scale;
+  if (variant == 0) {
+    scale = fmaxf(__fdiv_rn(d, 255.0f), 1e-8f);
+  } else {
+    scale = fmaxf(round_in(__fdiv_rn(d, 255.0f), dtype), round_in(1e-8f, dtype));
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    float n = __fdiv_rn(round_in(x[e] - mn, dtype), scale);
+    if (variant != 0) n = round_in(n, dtype);
+    n = fminf(fmaxf(n, 0.0f), 255.0f);
+    codes[e] = (uint8_t)__float2int_rz(n);
+  }
+  s16 = __half_as_ushort(__float2half_rn(scale));
+  z16 = __half_as_ushort(__float2half_rn(mn));
+}
+
+template <int EPL>
+__device__ inline void load_row(const void* src, int64_t elem_off, int lane, int dtype,
+                                float (&x)[EPL]) {
+  using T = typename VecIn<EPL>::T;
+  const T* p = reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(src) + elem_off) + lane;
+  T v = *p;
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) x[e] = bits_to_float(h[e], dtype);
+}
+
+template <int EPL>
+__device__ inline void store_kcodes(uint8_t* sb, int D, int t, int lane, const uint8_t (&c)[EPL]) {
+  int64_t off = sb_kcode(D, t, lane * EPL);
+  if constexpr (EPL == 2) {
+    *reinterpret_cast<uint16_t*>(sb + off) = (uint16_t)(c[0] | (c[1] << 8));
+  } else if constexpr (EPL == 4) {
+    *reinterpret_cast<uint32_t*>(sb + off) =
+        (uint32_t)c[0] | ((uint32_t)c[1] << 8) | ((uint32_t)c[2] << 16) | ((uint32_t)c[3] << 24);
+  } else {
+    uint2 w;
+    w.x = (uint32_t)c[0] | ((uint32_t)c[1] << 8) | ((uint32_t)c[2] << 16) | ((uint32_t)c[3] << 24);
+    w.y = (uint32_t)c[4] | ((uint32_t)c[5] << 8) | ((uint32_t)c[6] << 16) | ((uint32_t)c[7] << 24);
+    *reinterpret_cast<uint2*>(sb + off) = w;
+  }
+}
+
+// One warp per (layer, seq, kv-head, new token): quantize its K row and V row
+// and write codes + meta straight into the destination sub-block.
+template <int EPL, int LPG>
+__global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restrict__ pool, Geom geom,
+                                                              const AppendDst* __restrict__ dst,
+                                                              int layer_begin, int layer_count,
+                                                              int n_seqs, int n_new,
+                                                              const void* __restrict__ k,
+                                                              const void* __restrict__ v, int dtype) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
+  if (w >= total) return;
+  const int D = geom.D;
+  const int tok = (int)(w % n_new);
+  const int64_t rest = w / n_new;
+  const int h = (int)(rest % geom.Hkv);
+  const int64_t ls = rest / geom.Hkv;  // li * n_seqs + si
+  const int li = (int)(ls / n_seqs);
+  const AppendDst d = dst[ls * n_new + tok];
+  const int slot = d.pos & (kBlockTokens - 1);
+  const int t = slot & (kSubTokens - 1);
+  uint8_t* sb = pool + (((int64_t)d.block * geom.L + (layer_begin + li)) * geom.Hkv + h) * geom.page_bytes +
+                (int64_t)(slot >> 6) * geom.sb_bytes;
+
+  const int64_t elem_off = w * D;
+  float xk[EPL], xv[EPL];
+  load_row<EPL>(k, elem_off, lane, dtype, xk);
+  load_row<EPL>(v, elem_off, lane, dtype, xv);
+  uint8_t ck[EPL], cv[EPL];
+  uint16_t sk, zk, sv, zv;
+  quantize_lane<EPL, LPG>(xk, dtype, geom.quant_variant, ck, sk, zk);
+  quantize_lane<EPL, LPG>(xv, dtype, geom.quant_variant, cv, sv, zv);
+
+  store_kcodes<EPL>(sb, D, t, lane, ck);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) sb[sb_vcode(D, t, lane * EPL + e)] = cv[e];
+  if ((lane % LPG) == 0) {
+    const int gi = lane / LPG;
+    const int NG = geom.NG;
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 0, gi, t)) = sk;
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 1, gi, t)) = zk;
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = sv;
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = zv;
+  }
+}
+
+// Gather rows [p0, p0+S) of one (seq, layer) into the reference snapshot
+// layout; one thread per (head, row, element-of-8). mode 0: raw codes + meta;
+// mode 1: dequantized f16 (keys/values are f16 outputs).
+__global__ void gather_kernel(const uint8_t* __restrict__ pool, Geom geom, int layer,
+                              const int32_t* __restrict__ bt, int64_t p0, int64_t S,
+                              GatherOut out) {
+  const int D = geom.D, NG = geom.NG, G = geom.G;
+  const int per_row = D / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)geom.Hkv * S * per_row;
+  if (idx >= total) return;
+  const int e8 = (int)(idx % per_row);
+  const int64_t hr = idx / per_row;
+  const int64_t i = hr % S;
+  const int h = (int)(hr / S);
+  const int64_t pos = p0 + i;
+  int64_t bidx = pos >> 8;
+  if (geom.ring > 0) bidx %= geom.ring;
+  const int blk = bt[bidx];
+  const int slot = (int)(pos & 255);
+  const int t = slot & 63;
+  const uint8_t* sb = pool + (((int64_t)blk * geom.L + layer) * geom.Hkv + h) * geom.page_bytes +
+                      (int64_t)(slot >> 6) * geom.sb_bytes;
+  const int64_t orow = (int64_t)h * out.rows_total + out.row_off + i;
+  const int d0 = e8 * 8;
+  uint8_t kc[8], vc[8];
+  // 8 consecutive K codes sit inside one 16-byte chunk.
+  const uint2 kw = *reinterpret_cast<const uint2*>(sb + sb_kcode(D, t, d0));
+  const uint8_t* kb = reinterpret_cast<const uint8_t*>(&kw);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) { kc[e] = kb[e]; vc[e] = sb[sb_vcode(D, t, d0 + e)]; }
+  const int gi = d0 / G;
+  const uint16_t ks = *reinterpret_cast<const uint16_t*>(sb + sb_meta(D, NG, 0, gi, t));
+  const uint16_t kz = *reinterpret_cast<const uint16_t*>(sb + sb_meta(D, NG, 1, gi, t));
+  const uint16_t vs = *reinterpret_cast<const uint16_t*>(sb + sb_meta(D, NG, 2, gi, t));
+  const uint16_t vz = *reinterpret_cast<const uint16_t*>(sb + sb_meta(D, NG, 3, gi, t));
+  if (out.mode == 0) {
+    if (out.keys) *reinterpret_cast<uint2*>(out.keys + orow * D + d0) = kw;
+    if (out.values) {
+      uint2 vw;
+      vw.x = vc[0] | (vc[1] << 8) | (vc[2] << 16) | ((uint32_t)vc[3] << 24);
+      vw.y = vc[4] | (vc[5] << 8) | (vc[6] << 16) | ((uint32_t)vc[7] << 24);
+      *reinterpret_cast<uint2*>(out.values + orow * D + d0) = vw;
+    }
+    if ((d0 % G) == 0) {
+      const int64_t m = orow * NG + gi;
+      if (out.key_scales) out.key_scales[m] = ks;
+      if (out.key_zeros) out.key_zeros[m] = kz;
+      if (out.value_scales) out.value_scales[m] = vs;
+      if (out.value_zeros) out.value_zeros[m] = vz;
+    }
+  } else {
+    const __half hks = __ushort_as_half(ks), hkz = __ushort_as_half(kz);
+    const __half hvs = __ushort_as_half(vs), hvz = __ushort_as_half(vz);
+    __half* ok = reinterpret_cast<__half*>(out.keys);
+    __half* ov = reinterpret_cast<__half*>(out.values);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (ok) ok[orow * D + d0 + e] = __hadd_rn(__hmul_rn(__ushort2half_rn(kc[e]), hks), hkz);
+      if (ov) ov[orow * D + d0 + e] = __hadd_rn(__hmul_rn(__ushort2half_rn(vc[e]), hvs), hvz);
+    }
+  }
+}
+
+// Scatter rows from the snapshot layout into a sequence's pages (restore,
+// scatter-back). Row i of the input (at in.row_off + i) lands at position p0+i.
+__global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
+                               const int32_t* __restrict__ bt, int64_t p0, int64_t S, ScatterIn in) {
+  const int D = geom.D, NG = geom.NG, G = geom.G;
+  const int per_row = D / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)geom.Hkv * S * per_row;
+  if (idx >= total) return;
+  const int e8 = (int)(idx % per_row);
+  const int64_t hr = idx / per_row;
+  const int64_t i = hr % S;
+  const int h = (int)(hr / S);
+  const int64_t pos = p0 + i;
+  int64_t bidx = pos >> 8;
+  if (geom.ring > 0) bidx %= geom.ring;
+  const int blk = bt[bidx];
+  const int slot = (int)(pos & 255);
+  const int t = slot & 63;
+  uint8_t* sb = pool + (((int64_t)blk * geom.L + layer) * geom.Hkv + h) * geom.page_bytes +
+                (int64_t)(slot >> 6) * geom.sb_bytes;
+  const int64_t irow = (int64_t)h * in.rows_total + in.row_off + i;
+  const int d0 = e8 * 8;
+  const uint2 kw = *reinterpret_cast<const uint2*>(in.keys + irow * D + d0);
+  const uint2 vw = *reinterpret_cast<const uint2*>(in.values + irow * D + d0);
+  *reinterpret_cast<uint2*>(sb + sb_kcode(D, t, d0)) = kw;
+  const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vw);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sb[sb_vcode(D, t, d0 + e)] = vb[e];
+  if ((d0 % G) == 0) {
+    const int gi = d0 / G;
+    const int64_t m = irow * NG + gi;
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 0, gi, t)) = in.key_scales[m];
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 1, gi, t)) = in.key_zeros[m];
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = in.value_scales[m];
+    *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = in.value_zeros[m];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
+                          int layer_count, int n_seqs, int n_new, const void* k, const void* v,
+                          int dtype, cudaStream_t stream) {
+  const int64_t warps = (int64_t)layer_count * n_seqs * g.Hkv * n_new;
+  if (warps == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  const int epl = g.D / 32;
+  const int lpg = g.G / epl;
+#define KRILL_APPEND(E, P)                                                                    \
+  if (epl == E && lpg == P) {                                                                  \
+    append_quantize_kernel<E, P><<<(unsigned)blocks, threads, 0, stream>>>(                    \
+        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype);                 \
+    return cudaGetLastError();                                                                 \
+  }
+  KRILL_APPEND(2, 32)   // D=64,  G=64
+  KRILL_APPEND(4, 16)   // D=128, G=64
+  KRILL_APPEND(4, 32)   // D=128, G=128
+  KRILL_APPEND(8, 8)    // D=256, G=64
+  KRILL_APPEND(8, 16)   // D=256, G=128
+  KRILL_APPEND(8, 32)   // D=256, G=256
+#undef KRILL_APPEND
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const int32_t* d_bt,
+                          int64_t p0, int64_t S, const GatherOut& out, cudaStream_t stream) {
+  const int64_t total = (int64_t)g.Hkv * S * (g.D / 8);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  gather_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, stream>>>(pool, g, layer,
+                                                                                     d_bt, p0, S, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
+                           int64_t S, const ScatterIn& in, cudaStream_t stream) {
+  const int64_t total = (int64_t)g.Hkv * S * (g.D / 8);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  scatter_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, stream>>>(pool, g, layer,
+                                                                                      d_bt, p0, S, in);
+  return cudaGetLastError();
+}
+
+}  // namespace krill

@@ -1,0 +1,139 @@
+"""Decode-attention parity: the fused int8 kernel vs the reference math
+(full-cache fp16 dequantize, QuantizedKVCache.swift:71-74 + :200-204, then
+SDPA with GQA, Gemma4Model.swift:516 / Attention.swift:95) evaluated in
+float64 by the oracle.
+
+Tolerance (written here, per the hot-path contract): max-abs 2e-3 on fp32
+outputs; for f16/bf16 outputs 2e-3 plus one half-ulp of the output dtype at
+the reference value (the rounding of the stored result itself).
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from tests._data import BF16, F16, kv_values, to_bits
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import krill_b200 as kb  # noqa: E402
+from tests._gpu import dev_bits, prefill  # noqa: E402
+
+ATOL = 2e-3
+
+
+def half_ulp(ref: np.ndarray, out_dtype) -> np.ndarray:
+    if out_dtype == torch.float32:
+        return np.zeros_like(ref)
+    mant = 10 if out_dtype == torch.float16 else 7
+    e = np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -14)))
+    return 0.5 * 2.0 ** (e - mant)
+
+
+def run_case(D, G, hq, hkv, dtype, lengths, scale, out_dtype=torch.float32, window=0, split=256,
+             outliers=False, layers=2, seed=0, impl=kb.ATTN_TENSOR_CORE, steps=2):
+    rng = np.random.default_rng(seed)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=64, group_size=G, window=window,
+                     split_tokens=split, attn_impl=impl)
+    seqs, kb_all, vb_all = [], [], []
+    for L in lengths:
+        s = pool.create_sequence()
+        k = to_bits(kv_values(rng, (layers, hkv, L, D), outliers), dtype)
+        v = to_bits(kv_values(rng, (layers, hkv, L, D), outliers), dtype)
+        if window:  # a windowed pool takes at most max_append tokens per call
+            prefill(pool, s, k, v, dtype, chunk=256)
+        else:
+            prefill(pool, s, k, v, dtype)
+        seqs.append(s)
+        kb_all.append(k)
+        vb_all.append(v)
+    n = len(seqs)
+    worst = 0.0
+    for _ in range(steps):
+        k1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D), outliers), dtype)
+        v1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D), outliers), dtype)
+        qb = to_bits(kv_values(rng, (layers, n, hq, D)), dtype)
+        out = torch.empty((layers, n, hq, D), dtype=out_dtype, device="cuda")
+        kb.decode_step(pool, seqs, 0, dev_bits(k1, dtype), dev_bits(v1, dtype), dev_bits(qb, dtype),
+                       out, scale)
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy().astype(np.float64)
+        for i in range(n):
+            kb_all[i] = np.concatenate([kb_all[i], k1[:, i]], axis=2)
+            vb_all[i] = np.concatenate([vb_all[i], v1[:, i]], axis=2)
+            for layer in range(layers):
+                kk = kb_all[i][layer]
+                vv = vb_all[i][layer]
+                if window:
+                    kk = kk[:, -window:]
+                    vv = vv[:, -window:]
+                ck, sk, zk = oracle.quantize(kk, dtype, G)
+                cv, sv, zv = oracle.quantize(vv, dtype, G)
+                ref = oracle.reference_attention(ck, sk, zk, cv, sv, zv, qb[layer, i], dtype, G, scale)
+                err = np.abs(got[layer, i] - ref)
+                tol = ATOL + half_ulp(ref, out_dtype)
+                assert np.all(err <= tol), (
+                    f"seq {i} (L={kk.shape[1]}) layer {layer}: max err {err.max():.3e}")
+                worst = max(worst, float(err.max()))
+    pool.close()
+    return worst
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,scale", [
+    (64, 64, 32, 8, F16, 1 / 8),          # Llama-3.2-1B shape (config 1)
+    (128, 64, 32, 8, BF16, 1 / math.sqrt(128)),  # Llama-3.1-8B shape (config 2)
+    (128, 64, 32, 4, BF16, 1 / math.sqrt(128)),  # Qwen3-30B-A3B KV shape (GQA 8, config 4)
+    (256, 64, 8, 4, F16, 1.0),            # Gemma-style D=256, GQA 2, scale 1 (config 5)
+    (128, 128, 16, 16, F16, 1 / math.sqrt(128)),  # G = D (strict reference scheme), MHA
+])
+def test_attention_ragged(D, G, hq, hkv, dtype, scale):
+    run_case(D, G, hq, hkv, dtype, [1, 5, 63, 64, 65, 200, 700], scale)
+
+
+def test_attention_long_split():
+    # several split-K items per unit, combined by the last CTA
+    run_case(128, 64, 32, 8, BF16, [3000, 1100], 1 / math.sqrt(128), split=512, layers=1)
+
+
+def test_attention_outliers_gqa8():
+    run_case(128, 64, 32, 4, BF16, [900, 33], 1 / math.sqrt(128), outliers=True, layers=1)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_attention_low_precision_out(out_dtype):
+    run_case(128, 64, 32, 8, BF16, [17, 300], 1 / math.sqrt(128), out_dtype=out_dtype, layers=1)
+
+
+def test_attention_windowed():
+    # RotatingKVCache semantics: attend the last `window` positions only
+    run_case(256, 64, 8, 4, F16, [10, 100, 300, 700], 1.0, window=128, layers=2, steps=3)
+
+
+def test_batch_invariance_bit_exact():
+    """BatchedDecodeLiveTests.swift:533-576: a row's output does not depend
+    on the other rows (R=1 batched == solo, cross-row isolation), bit for bit."""
+    rng = np.random.default_rng(5)
+    D, hq, hkv, layers = 128, 32, 8, 2
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=64, split_tokens=256)
+    lengths = [40, 900, 2000]
+    seqs = []
+    for L in lengths:
+        s = pool.create_sequence()
+        prefill(pool, s, to_bits(kv_values(rng, (layers, hkv, L, D)), BF16),
+                to_bits(kv_values(rng, (layers, hkv, L, D)), BF16), BF16)
+        seqs.append(s)
+    qb = to_bits(kv_values(rng, (layers, 3, hq, D)), BF16)
+    q = dev_bits(qb, BF16)
+    out_all = torch.empty((layers, 3, hq, D), dtype=torch.float32, device="cuda")
+    kb.decode_attention(pool, seqs, 0, q, out_all, 0.1)
+    for i in range(3):
+        out_one = torch.empty((layers, 1, hq, D), dtype=torch.float32, device="cuda")
+        kb.decode_attention(pool, [seqs[i]], 0, q[:, i:i + 1].contiguous(), out_one, 0.1)
+        torch.cuda.synchronize()
+        assert torch.equal(out_one[:, 0], out_all[:, i])
+    pool.close()
