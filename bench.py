@@ -213,10 +213,13 @@ def main():
     ap.add_argument("--attn-impl", default="tc", choices=["tc", "cuda"])
     ap.add_argument("--split-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-layer-sample", type=int, default=2)
+    ap.add_argument("--cpu-layer-sample", type=int, default=12)
+    ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.seqs:
+        cfg["seqs"] = args.seqs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -61,7 +61,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // timeout), records the error and returns false.
 __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t limit = *cta_abort ? 1000000ull : 2000000000ull;
+  const uint64_t limit = *cta_abort ? 20000ull : 2000000000ull;
   const uint64_t t0 = globaltimer();
   for (;;) {
     if (mbar_try_wait(bar, phase)) return true;
