@@ -103,9 +103,11 @@ const char* krill_version(void);
 /* ---- pool ----------------------------------------------------------------
  * Replaces makeQuantizedKVCaches(numLayers:) (QuantizedKVCache.swift:208-210)
  * and makeKVCaches(spec:numLayers:) for `.rotating(window:)` layers
- * (KVCache.swift:198-209). device < 0 creates a host-only pool: block
- * accounting, sequences and the prefix cache work, compute calls return
- * KRILL_ERR_NO_DEVICE. */
+ * (KVCache.swift:198-209). device < 0 creates a host-only dry-run pool: block
+ * accounting, copy-on-write decisions, lengths, planning and the prefix cache
+ * run exactly as on a device pool, while no device memory exists and no
+ * kernel or copy is issued (append / attention / restore update only the
+ * bookkeeping; snapshots, stacking and peer fetch return KRILL_ERR_NO_DEVICE). */
 krill_status_t krill_pool_create(const krill_pool_cfg* cfg, int32_t device, krill_pool_t* out);
 krill_status_t krill_pool_destroy(krill_pool_t pool);
 krill_status_t krill_pool_block_bytes(krill_pool_t pool, int64_t* bytes);
@@ -114,6 +116,15 @@ krill_status_t krill_pool_block_refcount(krill_pool_t pool, int32_t block, int32
 /* Device error flag set by a kernel whose bounded wait gave up (and cleared
  * by reading it). */
 krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
+
+/* Measurement hook (no reference counterpart): while enabled, every attention
+ * and append kernel the pool launches is bracketed by a CUDA event pair on its
+ * launching stream. krill_pool_kernel_times() waits for the recorded events,
+ * returns the accumulated device milliseconds and launch counts since the
+ * last call, and resets them. Any output pointer may be NULL. */
+krill_status_t krill_pool_set_profiling(krill_pool_t pool, int32_t enable);
+krill_status_t krill_pool_kernel_times(krill_pool_t pool, double* attn_ms, int32_t* attn_launches,
+                                       double* append_ms, int32_t* append_launches);
 
 /* ---- sequences (one request's per-layer caches) -------------------------- */
 /* New empty sequence: every layer at length 0 (QuantizedKVCache.init). */

@@ -109,6 +109,17 @@ class KVPool:
         check(L.lib.krill_pool_device_error(self.handle, C.byref(v)))
         return v.value
 
+    def set_profiling(self, enable: bool = True):
+        check(L.lib.krill_pool_set_profiling(self.handle, 1 if enable else 0))
+
+    def kernel_times(self):
+        """(attention ms, attention launches, append ms, append launches)
+        accumulated since the last call (profiling must be enabled)."""
+        am, an, pm, pn = C.c_double(), C.c_int32(), C.c_double(), C.c_int32()
+        check(L.lib.krill_pool_kernel_times(self.handle, C.byref(am), C.byref(an), C.byref(pm),
+                                            C.byref(pn)))
+        return am.value, an.value, pm.value, pn.value
+
     def create_sequence(self) -> "Sequence_":
         h = C.c_uint64()
         check(L.lib.krill_seq_create(self.handle, C.byref(h)))

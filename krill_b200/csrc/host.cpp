@@ -87,6 +87,17 @@ struct StageSlot {
 };
 constexpr int kStageSlots = 8;
 
+// Decode-attention planner buffers, reused across calls.
+struct Plan {
+  std::vector<Seq*> sv;
+  std::vector<AttnUnit> units;
+  std::vector<AttnItem> items;
+  std::vector<int64_t> bucket;
+  std::vector<int32_t> order, owner, count, fill;
+  std::vector<std::pair<int64_t, int32_t>> heap;
+  std::vector<uint8_t> dry;
+};
+
 }  // namespace
 
 struct krill_pool_s {
@@ -108,6 +119,15 @@ struct krill_pool_s {
   StageSlot stage[kStageSlots];
   int stage_next = 0;
   std::recursive_mutex mu;
+  // kernel timing (measurement hook): event pairs around each launch
+  bool profiling = false;
+  struct Timed {
+    cudaEvent_t a, b;
+    int kind;  // 0 = attention, 1 = append
+  };
+  std::vector<Timed> timed;
+  std::vector<cudaEvent_t> spare_events;
+  Plan plan;
 
   int64_t ring_tokens() const { return (int64_t)geom.ring * kBlockTokens; }
   bool windowed() const { return cfg.window > 0; }
@@ -226,7 +246,7 @@ krill_status_t stage_acquire(krill_pool_t p, size_t bytes, StageSlot** out) {
     if (s.d) cudaFree(s.d);
     s.h = nullptr;
     s.d = nullptr;
-    size_t cap = 64 * 1024;
+    size_t cap = 1 << 20;
     while (cap < bytes) cap *= 2;
     CUDA_TRY(cudaMallocHost(&s.h, cap));
     CUDA_TRY(cudaMalloc(&s.d, cap));
@@ -248,6 +268,29 @@ krill_status_t stage_release(StageSlot* s, cudaStream_t stream) {
 }
 
 size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+cudaEvent_t take_event(krill_pool_t p) {
+  if (!p->spare_events.empty()) {
+    cudaEvent_t e = p->spare_events.back();
+    p->spare_events.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Record an event pair around `launch` when profiling is on.
+template <typename F>
+cudaError_t timed_launch(krill_pool_t p, int kind, cudaStream_t stream, F&& launch) {
+  if (!p->profiling) return launch();
+  cudaEvent_t a = take_event(p), b = take_event(p);
+  cudaEventRecord(a, stream);
+  cudaError_t e = launch();
+  cudaEventRecord(b, stream);
+  p->timed.push_back({a, b, kind});
+  return e;
+}
 
 krill_status_t require_device(krill_pool_t p) {
   if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "compute call on a host-only pool");
@@ -272,15 +315,16 @@ krill_status_t check_layers(krill_pool_t p, int32_t lb, int32_t lc) {
 }
 
 // ---------------------------------------------------------------- append
+// On a host-only (dry-run) pool the block accounting, copy-on-write decisions
+// and length updates run, and the device work is skipped.
 krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                          int32_t lc, int32_t n_new, const void* k, const void* v, int32_t dtype,
                          cudaStream_t stream) {
-  TRY(require_device(p));
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(dtype, "k/v"));
   if (n_seqs < 0 || n_new < 0) return fail(KRILL_ERR_INVALID, "negative count");
   if (n_seqs == 0 || lc == 0 || n_new == 0) return KRILL_OK;
-  if (!k || !v || !seqs) return fail(KRILL_ERR_INVALID, "null k/v/seqs");
+  if (!seqs || (!p->host_only && (!k || !v))) return fail(KRILL_ERR_INVALID, "null k/v/seqs");
   if (p->windowed() && n_new > p->cfg.max_append)
     return fail(KRILL_ERR_INVALID, "n_new %d exceeds the windowed pool's max_append %d", n_new,
                 p->cfg.max_append);
@@ -290,9 +334,16 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
     for (int j = 0; j < i; ++j)
       if (sv[i] == sv[j]) return fail(KRILL_ERR_INVALID, "sequence listed twice in one call");
   const size_t n_dst = (size_t)lc * n_seqs * n_new;
-  StageSlot* slot;
-  TRY(stage_acquire(p, n_dst * sizeof(AppendDst), &slot));
-  AppendDst* dst = reinterpret_cast<AppendDst*>(slot->h);
+  StageSlot* slot = nullptr;
+  std::vector<AppendDst> dry;
+  AppendDst* dst;
+  if (p->host_only) {
+    dry.resize(n_dst);
+    dst = dry.data();
+  } else {
+    TRY(stage_acquire(p, n_dst * sizeof(AppendDst), &slot));
+    dst = reinterpret_cast<AppendDst*>(slot->h);
+  }
   for (int si = 0; si < n_seqs; ++si) {
     Seq& s = *sv[si];
     // make every touched block writable first (allocation / copy-on-write)
@@ -313,10 +364,14 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
       }
     }
   }
-  TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
-  CUDA_TRY(launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
-                         n_seqs, n_new, k, v, dtype, stream));
-  TRY(stage_release(slot, stream));
+  if (!p->host_only) {
+    TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
+    CUDA_TRY(timed_launch(p, 1, stream, [&] {
+      return launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
+                           n_seqs, n_new, k, v, dtype, stream);
+    }));
+    TRY(stage_release(slot, stream));
+  }
   for (int si = 0; si < n_seqs; ++si) {
     Seq& s = *sv[si];
     for (int li = 0; li < lc; ++li) {
@@ -335,6 +390,7 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
 krill_status_t ensure_scratch(krill_pool_t p, int64_t partial_count, int64_t units) {
   const int64_t pf = partial_floats(p->geom.D);
   if (partial_count * pf > p->partials_cap || units > p->counters_cap) {
+    // grows rarely (first launches); frees must not race kernels in flight
     CUDA_TRY(cudaDeviceSynchronize());
     if (partial_count * pf > p->partials_cap) {
       if (p->d_partials) cudaFree(p->d_partials);
@@ -358,33 +414,33 @@ krill_status_t ensure_scratch(krill_pool_t p, int64_t partial_count, int64_t uni
 krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                             int32_t lc, const void* q, int32_t q_dtype, void* out,
                             int32_t out_dtype, float scale, cudaStream_t stream) {
-  TRY(require_device(p));
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(q_dtype, "q"));
   if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
     return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
   if (n_seqs < 0) return fail(KRILL_ERR_INVALID, "negative n_seqs");
   if (n_seqs == 0 || lc == 0) return KRILL_OK;
-  if (!q || !out || !seqs) return fail(KRILL_ERR_INVALID, "null q/out/seqs");
+  if (!seqs || (!p->host_only && (!q || !out))) return fail(KRILL_ERR_INVALID, "null q/out/seqs");
   TRY(check_aligned(q, "q"));
   TRY(check_aligned(out, "out"));
   const Geom& g = p->geom;
-  std::vector<Seq*> sv(n_seqs);
+  Plan& pl = p->plan;
+  pl.sv.resize(n_seqs);
   int64_t bt_stride = 1;
   for (int i = 0; i < n_seqs; ++i) {
-    TRY(seq_get(p, seqs[i], &sv[i]));
-    bt_stride = std::max<int64_t>(bt_stride, (int64_t)sv[i]->blocks.size());
+    TRY(seq_get(p, seqs[i], &pl.sv[i]));
+    bt_stride = std::max<int64_t>(bt_stride, (int64_t)pl.sv[i]->blocks.size());
   }
-  const int64_t n_units = (int64_t)lc * n_seqs * g.Hkv;
+  // ---- units (layer, seq) and items (balanced split of each unit) ----
+  const int64_t n_units = (int64_t)lc * n_seqs;
   const int C = std::max(1, p->cfg.split_tokens / kSubTokens);
-  std::vector<AttnUnit> units((size_t)n_units);
-  std::vector<AttnItem> items;
-  items.reserve((size_t)n_units * 2);
-  int64_t partial_count = 0;
+  pl.units.resize((size_t)n_units);
+  pl.items.clear();
+  int64_t item_count = 0;
   for (int li = 0; li < lc; ++li) {
     const int L = lb + li;
     for (int si = 0; si < n_seqs; ++si) {
-      const Seq& s = *sv[si];
+      const Seq& s = *pl.sv[si];
       const int64_t len = s.len[L];
       if (len <= 0) return fail(KRILL_ERR_INVALID, "attention over an empty cache (layer %d)", L);
       const int64_t t_hi = len;
@@ -393,74 +449,90 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       const int64_t n_sb = sb1 - sb0;
       const int64_t n_it = (n_sb + C - 1) / C;
       const int64_t base = n_sb / n_it, extra = n_sb % n_it;
-      for (int h = 0; h < g.Hkv; ++h) {
-        const int64_t ui = ((int64_t)li * n_seqs + si) * g.Hkv + h;
-        AttnUnit& u = units[ui];
-        u.qo_row = li * n_seqs + si;
-        u.si = si;
-        u.layer = L;
-        u.h = h;
-        u.t_lo = (int32_t)t_lo;
-        u.t_hi = (int32_t)t_hi;
-        u.n_items = (int32_t)n_it;
-        u.first_item = n_it > 1 ? (int32_t)partial_count : 0;
-        if (n_it > 1) partial_count += n_it;
-        int64_t b = sb0;
-        for (int64_t i = 0; i < n_it; ++i) {
-          const int64_t sz = base + (i < extra ? 1 : 0);
-          items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int32_t)i});
-          b += sz;
-        }
+      const int64_t ui = (int64_t)li * n_seqs + si;
+      AttnUnit& u = pl.units[ui];
+      u.qo_row = (int32_t)ui;
+      u.si = si;
+      u.layer = L;
+      u.t_lo = (int32_t)t_lo;
+      u.t_hi = (int32_t)t_hi;
+      u.n_items = (int32_t)n_it;
+      u.first_item = (int32_t)item_count;
+      u.pad = 0;
+      int64_t b = sb0;
+      for (int64_t i = 0; i < n_it; ++i) {
+        const int64_t sz = base + (i < extra ? 1 : 0);
+        pl.items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int32_t)i});
+        b += sz;
       }
+      item_count += n_it;
     }
   }
-  TRY(ensure_scratch(p, partial_count, n_units));
-  // Longest-processing-time assignment of items to persistent CTAs.
-  const int64_t n_items = (int64_t)items.size();
+  if (!p->host_only) TRY(ensure_scratch(p, item_count * g.Hkv, n_units * g.Hkv));
+  // ---- longest-processing-time assignment of items to persistent CTAs ----
+  // Items are at most C sub-blocks, so a counting sort orders them by size.
+  const int64_t n_items = (int64_t)pl.items.size();
   const int grid = (int)std::min<int64_t>(p->num_sms, n_items);
-  std::vector<int32_t> order((size_t)n_items);
-  for (int64_t i = 0; i < n_items; ++i) order[i] = (int32_t)i;
-  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
-    return (items[a].sb_end - items[a].sb_begin) > (items[b].sb_end - items[b].sb_begin);
-  });
-  std::vector<int32_t> owner((size_t)n_items);
-  std::vector<int32_t> count((size_t)grid, 0);
-  {
-    using E = std::pair<int64_t, int32_t>;
-    std::priority_queue<E, std::vector<E>, std::greater<E>> heap;
-    for (int c = 0; c < grid; ++c) heap.push({0, c});
-    for (int32_t i : order) {
-      E e = heap.top();
-      heap.pop();
-      owner[i] = e.second;
-      count[e.second] += 1;
-      e.first += items[i].sb_end - items[i].sb_begin;
-      heap.push(e);
-    }
+  pl.bucket.assign((size_t)C + 2, 0);
+  for (const AttnItem& it : pl.items) pl.bucket[C - (it.sb_end - it.sb_begin)] += 1;
+  for (int i = 1; i <= C + 1; ++i) pl.bucket[i] += pl.bucket[i - 1];
+  pl.order.resize((size_t)n_items);
+  for (int64_t i = n_items - 1; i >= 0; --i) {
+    const AttnItem& it = pl.items[i];
+    pl.order[--pl.bucket[C - (it.sb_end - it.sb_begin)]] = (int32_t)i;
   }
-  const size_t units_bytes = align16(units.size() * sizeof(AttnUnit));
+  pl.owner.resize((size_t)n_items);
+  pl.count.assign((size_t)grid, 0);
+  pl.heap.resize((size_t)grid);
+  for (int c = 0; c < grid; ++c) pl.heap[c] = {0, c};  // already a min-heap
+  auto sift_down = [&](size_t i) {
+    const size_t n = pl.heap.size();
+    for (;;) {
+      size_t m = i, l = 2 * i + 1, r = l + 1;
+      if (l < n && pl.heap[l] < pl.heap[m]) m = l;
+      if (r < n && pl.heap[r] < pl.heap[m]) m = r;
+      if (m == i) return;
+      std::swap(pl.heap[i], pl.heap[m]);
+      i = m;
+    }
+  };
+  for (int32_t i : pl.order) {
+    auto& top = pl.heap[0];
+    pl.owner[i] = top.second;
+    pl.count[top.second] += 1;
+    top.first += pl.items[i].sb_end - pl.items[i].sb_begin;
+    sift_down(0);
+  }
+  // ---- metadata packet: units | items (grouped by CTA) | cta offsets | block tables ----
+  const size_t units_bytes = align16((size_t)n_units * sizeof(AttnUnit));
   const size_t items_bytes = align16((size_t)n_items * sizeof(AttnItem));
   const size_t off_bytes = align16((size_t)(grid + 1) * sizeof(int32_t));
   const size_t bt_bytes = align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
   const size_t total = units_bytes + items_bytes + off_bytes + bt_bytes;
-  StageSlot* slot;
-  TRY(stage_acquire(p, total, &slot));
-  uint8_t* h = slot->h;
-  std::memcpy(h, units.data(), units.size() * sizeof(AttnUnit));
+  StageSlot* slot = nullptr;
+  uint8_t* h;
+  if (p->host_only) {
+    pl.dry.resize(total);
+    h = pl.dry.data();
+  } else {
+    TRY(stage_acquire(p, total, &slot));
+    h = slot->h;
+  }
+  std::memcpy(h, pl.units.data(), (size_t)n_units * sizeof(AttnUnit));
   AttnItem* hi = reinterpret_cast<AttnItem*>(h + units_bytes);
   int32_t* off = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes);
   off[0] = 0;
-  for (int c = 0; c < grid; ++c) off[c + 1] = off[c] + count[c];
-  {
-    std::vector<int32_t> fill(off, off + grid);
-    for (int32_t i : order) hi[fill[owner[i]]++] = items[i];
-  }
+  for (int c = 0; c < grid; ++c) off[c + 1] = off[c] + pl.count[c];
+  pl.fill.assign(off, off + grid);
+  for (int32_t i : pl.order) hi[pl.fill[pl.owner[i]]++] = pl.items[i];
   int32_t* bt = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes + off_bytes);
   for (int si = 0; si < n_seqs; ++si) {
-    const Seq& s = *sv[si];
-    for (int64_t j = 0; j < bt_stride; ++j)
-      bt[si * bt_stride + j] = j < (int64_t)s.blocks.size() ? s.blocks[j] : -1;
+    const Seq& s = *pl.sv[si];
+    const size_t nb = s.blocks.size();
+    if (nb) std::memcpy(bt + si * bt_stride, s.blocks.data(), nb * sizeof(int32_t));
+    for (int64_t j = (int64_t)nb; j < bt_stride; ++j) bt[si * bt_stride + j] = -1;
   }
+  if (p->host_only) return KRILL_OK;  // dry run: planned, nothing launched
   TRY(stage_upload(slot, total, stream));
   AttnParams ap{};
   ap.pool = p->d_pool;
@@ -484,7 +556,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.partials = p->d_partials;
   ap.counters = p->d_counters;
   ap.err = p->d_err;
-  CUDA_TRY(launch_attention(g, ap, grid, p->cfg.attn_impl, stream));
+  CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
   TRY(stage_release(slot, stream));
   return KRILL_OK;
 }
@@ -520,19 +592,22 @@ krill_status_t do_restore(krill_pool_t p, Seq& s, int32_t layer, int64_t rows, i
   if (p->windowed() && rows > p->ring_tokens())
     return fail(KRILL_ERR_INVALID, "restore of %lld rows exceeds the ring (%lld)", (long long)rows,
                 (long long)p->ring_tokens());
-  if (rows > 0 && (!in.keys || !in.values || !in.key_scales || !in.key_zeros || !in.value_scales ||
-                   !in.value_zeros))
+  if (!p->host_only && rows > 0 &&
+      (!in.keys || !in.values || !in.key_scales || !in.key_zeros || !in.value_scales ||
+       !in.value_zeros))
     return fail(KRILL_ERR_INVALID, "restore needs all six tensors");
   const int64_t p0 = total_seen - rows;
   if (rows > 0) {
     int64_t b0 = p0 / kBlockTokens, b1 = (total_seen - 1) / kBlockTokens;
     for (int64_t bi = b0; bi <= b1; ++bi)
       TRY(seq_writable_block(p, s, p->windowed() ? bi % p->geom.ring : bi, stream));
-    StageSlot* slot;
-    TRY(upload_bt(p, s, stream, &slot));
-    CUDA_TRY(launch_scatter(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d),
-                            p0, rows, in, stream));
-    TRY(stage_release(slot, stream));
+    if (!p->host_only) {
+      StageSlot* slot;
+      TRY(upload_bt(p, s, stream, &slot));
+      CUDA_TRY(launch_scatter(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d),
+                              p0, rows, in, stream));
+      TRY(stage_release(slot, stream));
+    }
   }
   s.len[layer] = total_seen;
   s.ret[layer] = rows;
@@ -619,6 +694,11 @@ krill_status_t krill_pool_destroy(krill_pool_t p) {
       if (s.d) cudaFree(s.d);
       if (s.ev) cudaEventDestroy(s.ev);
     }
+    for (auto& e : p->timed) {
+      cudaEventDestroy(e.a);
+      cudaEventDestroy(e.b);
+    }
+    for (auto e : p->spare_events) cudaEventDestroy(e);
     if (p->d_pool) cudaFree(p->d_pool);
     if (p->d_partials) cudaFree(p->d_partials);
     if (p->d_counters) cudaFree(p->d_counters);
@@ -662,6 +742,37 @@ krill_status_t krill_pool_device_error(krill_pool_t p, int32_t* flag) {
     if (p->d_counters) CUDA_TRY(cudaMemset(p->d_counters, 0, (size_t)p->counters_cap * sizeof(int)));
   }
   *flag = v;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_set_profiling(krill_pool_t p, int32_t enable) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  p->profiling = enable != 0 && !p->host_only;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_kernel_times(krill_pool_t p, double* attn_ms, int32_t* attn_launches,
+                                       double* append_ms, int32_t* append_launches) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  double t[2] = {0.0, 0.0};
+  int32_t n[2] = {0, 0};
+  for (auto& e : p->timed) {
+    CUDA_TRY(cudaEventSynchronize(e.b));
+    float ms = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&ms, e.a, e.b));
+    t[e.kind] += ms;
+    n[e.kind] += 1;
+    p->spare_events.push_back(e.a);
+    p->spare_events.push_back(e.b);
+  }
+  p->timed.clear();
+  if (attn_ms) *attn_ms = t[0];
+  if (attn_launches) *attn_launches = n[0];
+  if (append_ms) *append_ms = t[1];
+  if (append_launches) *append_launches = n[1];
   return KRILL_OK;
 }
 
@@ -874,7 +985,6 @@ krill_status_t krill_seq_restore_quantized(krill_pool_t p, krill_seq_t h, int32_
                                            const void* value_zeros, void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
-  TRY(require_device(p));
   DeviceGuard dg(p->device);
   Seq* s = nullptr;
   TRY(seq_get(p, h, &s));

@@ -38,16 +38,17 @@ struct ScatterIn {
   int64_t rows_total;
 };
 
-// One decode-attention unit: (layer, sequence, kv-head) with its valid token
-// positions [t_lo, t_hi). Its sub-block range is split into n_items items.
+// One decode-attention unit: (layer, sequence) over all of its kv heads, with
+// the attended positions [t_lo, t_hi). Its sub-block range is split into
+// n_items items; each item is processed head by head by one CTA.
 struct AttnUnit {
   int32_t qo_row;      // li * n_seqs + si : row of q/out
   int32_t si;          // sequence index in the call (block-table row)
   int32_t layer;       // absolute layer in the pool
-  int32_t h;           // kv head
   int32_t t_lo, t_hi;  // attended positions
-  int32_t first_item;  // partial-slot base
+  int32_t first_item;  // partial record of (item idx, head h): (first_item + idx) * Hkv + h
   int32_t n_items;
+  int32_t pad;
 };
 
 struct AttnItem {
@@ -71,8 +72,8 @@ struct AttnParams {
   void* out;
   int out_dtype;
   float scale_log2;  // softmax scale * log2(e)
-  float* partials;   // [items][16 + 8*D]
-  int* counters;     // [units], zero between launches
+  float* partials;   // [items * Hkv][16 + 8*D]
+  int* counters;     // [units * Hkv], zero between launches
   int* err;
 };
 

@@ -110,6 +110,20 @@ __device__ __forceinline__ uint32_t deq2(uint32_t w, uint32_t sel, uint32_t s2, 
   return h2u(c);
 }
 
+// Same result with one operation less, exact whenever |s| < 64:
+// fma(1024 + c, s, -1024*s) rounds the exact product c*s once (-1024*s is
+// exact in f16, subnormal s included), then + z rounds again.
+__device__ __forceinline__ uint32_t deq2_fast(uint32_t w, uint32_t sel, uint32_t s2, uint32_t ns2,
+                                              uint32_t z2) {
+  __half2 c = u2h(__byte_perm(w, 0x64646464u, sel));
+  c = __hfma2(c, u2h(s2), u2h(ns2));
+  c = __hadd2_rn(c, u2h(z2));
+  return h2u(c);
+}
+__device__ __forceinline__ uint32_t neg1024(uint32_t s2) {
+  return h2u(__hmul2_rn(u2h(s2), u2h(0xE400E400u)));  // -1024 in f16
+}
+
 template <int D, int NG>
 struct SubGeom {
   static constexpr int G = D / NG;
@@ -121,6 +135,22 @@ struct SubGeom {
     return META + (a * NG + gi) * 128 + t * 2;
   }
 };
+
+// True when every K and V scale of the sub-block has |s| < 64 (and is finite),
+// i.e. the fast dequant is exact for the whole sub-block. Warp-uniform.
+template <int D, int NG>
+__device__ __forceinline__ bool scales_small(const uint8_t* __restrict__ sb, int lane) {
+  using SG = SubGeom<D, NG>;
+  constexpr int BYTES = NG * 128;  // one [NG][64] f16 array
+  bool big = false;
+  for (int off = lane * 16; off < 2 * BYTES; off += 512) {
+    const int a = off / BYTES;  // 0: K scales, 1: V scales (meta array 2)
+    const uint4 w = *reinterpret_cast<const uint4*>(sb + SG::META + a * 2 * BYTES + (off - a * BYTES));
+    big |= (__vcmpgeu2(w.x & 0x7fff7fffu, 0x54005400u) | __vcmpgeu2(w.y & 0x7fff7fffu, 0x54005400u) |
+            __vcmpgeu2(w.z & 0x7fff7fffu, 0x54005400u) | __vcmpgeu2(w.w & 0x7fff7fffu, 0x54005400u)) != 0;
+  }
+  return !__any_sync(0xffffffffu, big);
+}
 
 template <int D>
 struct TCState {
@@ -174,7 +204,7 @@ __device__ __forceinline__ void reset_state(TCState<D>& st) {
 // Process one 64-token sub-block resident in shared memory at `sb`.
 // pos0 = absolute position of its token 0; tokens outside [t_lo, t_hi) are
 // masked (only checked when `boundary`).
-template <int D, int NG>
+template <int D, int NG, bool FAST>
 __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCState<D>& st,
                                             int lane, float scale_log2, bool boundary, int pos0,
                                             int t_lo, int t_hi) {
@@ -204,12 +234,21 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
       const uint32_t zA = __byte_perm(kz4.x, 0, selh), zB = __byte_perm(kz4.y, 0, selh);
       const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
       const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+      const uint32_t nsA = neg1024(sA), nsB = neg1024(sB);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint32_t a0 = deq2(wav[k], 0x4140u, sA, zA);
-        const uint32_t a1 = deq2(wbv[k], 0x4140u, sB, zB);
-        const uint32_t a2 = deq2(wav[k], 0x4342u, sA, zA);
-        const uint32_t a3 = deq2(wbv[k], 0x4342u, sB, zB);
+        uint32_t a0, a1, a2, a3;
+        if constexpr (FAST) {
+          a0 = deq2_fast(wav[k], 0x4140u, sA, nsA, zA);
+          a1 = deq2_fast(wbv[k], 0x4140u, sB, nsB, zB);
+          a2 = deq2_fast(wav[k], 0x4342u, sA, nsA, zA);
+          a3 = deq2_fast(wbv[k], 0x4342u, sB, nsB, zB);
+        } else {
+          a0 = deq2(wav[k], 0x4140u, sA, zA);
+          a1 = deq2(wbv[k], 0x4140u, sB, zB);
+          a2 = deq2(wav[k], 0x4342u, sA, zA);
+          a3 = deq2(wbv[k], 0x4342u, sB, zB);
+        }
         mma16816(acc, a0, a1, a2, a3, st.qf[hh][2 * k], st.qf[hh][2 * k + 1]);
       }
     }
@@ -283,6 +322,9 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
         vz[i] &= m;
       }
     }
+    uint32_t nvs[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) nvs[i] = FAST ? neg1024(vs[i]) : 0u;
 #pragma unroll
     for (int mi = 0; mi < SG::G / 16; ++mi) {
       const int mt = grp * (SG::G / 16) + mi;
@@ -293,10 +335,18 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
       const uint32_t yv[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const uint32_t a0 = deq2(xv[u], 0x4140u, vs[2 * u], vz[2 * u]);
-        const uint32_t a1 = deq2(yv[u], 0x4140u, vs[2 * u], vz[2 * u]);
-        const uint32_t a2 = deq2(xv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
-        const uint32_t a3 = deq2(yv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
+        uint32_t a0, a1, a2, a3;
+        if constexpr (FAST) {
+          a0 = deq2_fast(xv[u], 0x4140u, vs[2 * u], nvs[2 * u], vz[2 * u]);
+          a1 = deq2_fast(yv[u], 0x4140u, vs[2 * u], nvs[2 * u], vz[2 * u]);
+          a2 = deq2_fast(xv[u], 0x4342u, vs[2 * u + 1], nvs[2 * u + 1], vz[2 * u + 1]);
+          a3 = deq2_fast(yv[u], 0x4342u, vs[2 * u + 1], nvs[2 * u + 1], vz[2 * u + 1]);
+        } else {
+          a0 = deq2(xv[u], 0x4140u, vs[2 * u], vz[2 * u]);
+          a1 = deq2(yv[u], 0x4140u, vs[2 * u], vz[2 * u]);
+          a2 = deq2(xv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
+          a3 = deq2(yv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
+        }
         mma16816(st.o[mt], a0, a1, a2, a3, pb[u][0], pb[u][1]);
       }
     }
@@ -319,13 +369,14 @@ struct AttnSmem {
   static constexpr int BAR_OFF = STAGE_BYTES;                      // 2*NSTAGE u64
   static constexpr int CM_OFF = BAR_OFF + 2 * NSTAGE * 8;          // [NCW][8] f32
   static constexpr int CL_OFF = CM_OFF + NCW * 8 * 4;              // [NCW][8] f32
-  static constexpr int CO_OFF = CL_OFF + NCW * 8 * 4;              // [NCW][8][D] f32
-  static constexpr int MISC_OFF = CO_OFF + NCW * 8 * D * 4;        // abort flag, last flag
+  static constexpr int CO_LD = D + 4;                              // padded: conflict-free stores
+  static constexpr int CO_OFF = CL_OFF + NCW * 8 * 4;              // [NCW][8][CO_LD] f32
+  static constexpr int MISC_OFF = CO_OFF + NCW * 8 * CO_LD * 4;    // abort flag, last flag
   static constexpr int TOTAL = MISC_OFF + 16;
 };
 
 template <int D, int NG, int NCW, int NSTAGE>
-__global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p) {
+__global__ void __maxnreg__(D >= 256 ? 255 : 224) attn_tc_kernel(AttnParams p) {
   using SM = AttnSmem<D, NG, NCW, NSTAGE>;
   constexpr int SB = SM::SB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -350,29 +401,47 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
   __syncthreads();
 
   const int it0 = p.cta_off[blockIdx.x], it1 = p.cta_off[blockIdx.x + 1];
+  const int Hkv = p.Hkv;
 
   if (warp == NCW) {
     // ---------------- producer ----------------
-    if (lane == 0) {
-      uint32_t J = 0;
-      for (int it = it0; it < it1; ++it) {
-        const AttnItem item = p.items[it];
-        const AttnUnit un = p.units[item.unit];
-        const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
-        const uint8_t* head_base = p.pool + ((int64_t)un.layer * p.Hkv + un.h) * p.page_bytes;
-        const int64_t blk_stride = (int64_t)p.L * p.Hkv * p.page_bytes;
-        for (int j = item.sb_begin; j < item.sb_end; ++j, ++J) {
-          const uint32_t stage = J % NSTAGE;
-          if (J >= (uint32_t)NSTAGE)
-            mbar_wait(bar_base + 8 * (NSTAGE + stage), ((J / NSTAGE) - 1) & 1, cta_abort, p.err);
-          int bi = j >> 2;
-          if (p.ring > 0) bi %= p.ring;
-          const uint8_t* src = head_base + (int64_t)bt[bi] * blk_stride + (int64_t)(j & 3) * SB;
-          const uint32_t full = bar_base + 8 * stage;
-          mbar_expect_tx(full, SB);
-          bulk_g2s(smem_u32(stages + (size_t)stage * SB), src, SB, full);
+    // The lanes fetch an item's block ids together (one coalesced load per 32
+    // blocks); lane 0 then issues one bulk copy per (head, sub-block) with no
+    // dependent global load in the issue loop.
+    const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
+    uint32_t J = 0;
+    for (int it = it0; it < it1; ++it) {
+      const AttnItem item = p.items[it];
+      const AttnUnit un = p.units[item.unit];
+      const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
+      const int b0 = item.sb_begin >> 2;
+      const int nblk = ((item.sb_end - 1) >> 2) - b0 + 1;
+      for (int c0 = 0; c0 < nblk; c0 += 32) {
+        int bi = b0 + c0 + lane;
+        if (p.ring > 0) bi %= p.ring;
+        const int blk = (c0 + lane < nblk) ? bt[bi] : 0;
+        const int jlo = max(item.sb_begin, (b0 + c0) * 4);
+        const int jhi = min(item.sb_end, (b0 + c0 + 32) * 4);
+        for (int h = 0; h < Hkv; ++h) {
+          const uint8_t* head_base = p.pool + ((int64_t)un.layer * Hkv + h) * p.page_bytes;
+          // sub-block order within the item: head-major, then position; the
+          // consumers use the same order (J advances identically)
+          for (int j = jlo; j < jhi; ++j) {
+            const int b = __shfl_sync(0xffffffffu, blk, (j >> 2) - b0 - c0);
+            if (lane == 0) {
+              const uint32_t Jh = J + (uint32_t)h * (item.sb_end - item.sb_begin) + (j - item.sb_begin);
+              const uint32_t stage = Jh % NSTAGE;
+              if (Jh >= (uint32_t)NSTAGE)
+                mbar_wait(bar_base + 8 * (NSTAGE + stage), ((Jh / NSTAGE) - 1) & 1, cta_abort, p.err);
+              const uint8_t* src = head_base + (int64_t)b * blk_stride + (int64_t)(j & 3) * SB;
+              const uint32_t full = bar_base + 8 * stage;
+              mbar_expect_tx(full, SB);
+              bulk_g2s(smem_u32(stages + (size_t)stage * SB), src, SB, full);
+            }
+          }
         }
       }
+      J += (uint32_t)Hkv * (item.sb_end - item.sb_begin);
     }
     return;
   }
@@ -381,106 +450,123 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
   TCState<D> st;
   uint32_t J = 0;
   const int g = p.g;
+  AttnItem item_next{};
+  AttnUnit un_next{};
+  if (it0 < it1) {
+    item_next = p.items[it0];
+    un_next = p.units[item_next.unit];
+  }
   for (int it = it0; it < it1; ++it) {
-    const AttnItem item = p.items[it];
-    const AttnUnit un = p.units[item.unit];
+    const AttnItem item = item_next;
+    const AttnUnit un = un_next;
+    if (it + 1 < it1) item_next = p.items[it + 1];
     const int n_sb = item.sb_end - item.sb_begin;
-    reset_state(st);
-    const int64_t q_row = ((int64_t)un.qo_row * p.Hq + (int64_t)un.h * g) * D;
-    if (warp < n_sb) load_q<D>(st, p.q, p.q_dtype, q_row, g, lane);
-    for (int k = warp; k < n_sb; k += NCW) {
-      const uint32_t jj = J + k;
-      const uint32_t stage = jj % NSTAGE;
-      mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
-      const int j = item.sb_begin + k;
-      const int pos0 = j * 64;
-      const bool boundary = pos0 < un.t_lo || pos0 + 64 > un.t_hi;
-      tc_subblock<D, NG>(stages + (size_t)stage * SB, st, lane, p.scale_log2, boundary, pos0,
-                         un.t_lo, un.t_hi);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
-    }
-    J += n_sb;
-
-    // ---- combine the warps' states for this item ----
-    float l0 = st.l[0], l1 = st.l[1];
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    named_bar(kConsumerBar, NCW * 32);  // previous item's combine reads are done
-    {
-      const int r = lane >> 2, tig = lane & 3;
-      if (r == 0) {
-        cm[warp * 8 + 2 * tig] = st.m[0];
-        cm[warp * 8 + 2 * tig + 1] = st.m[1];
-        cl[warp * 8 + 2 * tig] = l0;
-        cl[warp * 8 + 2 * tig + 1] = l1;
-      }
-      float* co = cO + (size_t)warp * 8 * D;
-#pragma unroll
-      for (int mt = 0; mt < D / 16; ++mt) {
-        const int d = 16 * mt + r;
-        co[(2 * tig) * D + d] = st.o[mt][0];
-        co[(2 * tig + 1) * D + d] = st.o[mt][1];
-        co[(2 * tig) * D + d + 8] = st.o[mt][2];
-        co[(2 * tig + 1) * D + d + 8] = st.o[mt][3];
-      }
-    }
-    named_bar(kConsumerBar, NCW * 32);
     const bool split = un.n_items > 1;
-    float* part = p.partials + (int64_t)(un.first_item + item.idx) * partial_floats(D);
-    const int64_t out_row = ((int64_t)un.qo_row * p.Hq + (int64_t)un.h * g) * D;
-    for (int idx = tid; idx < g * D; idx += NCW * 32) {
-      const int h = idx / D, d = idx - h * D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) M = fmaxf(M, cm[w * 8 + h]);
-      float Ls = 0.f, Os = 0.f;
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) {
-        const float mw = cm[w * 8 + h];
-        const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-        Ls += cl[w * 8 + h] * f;
-        Os += cO[((size_t)w * 8 + h) * D + d] * f;
+    for (int h = 0; h < Hkv; ++h) {
+      reset_state(st);
+      const int64_t qo_row = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
+      if (warp < n_sb) load_q<D>(st, p.q, p.q_dtype, qo_row, g, lane);
+      for (int k = warp; k < n_sb; k += NCW) {
+        const uint32_t jj = J + k;
+        const uint32_t stage = jj % NSTAGE;
+        mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
+        const int j = item.sb_begin + k;
+        const int pos0 = j * 64;
+        const bool boundary = pos0 < un.t_lo || pos0 + 64 > un.t_hi;
+        const uint8_t* sbp = stages + (size_t)stage * SB;
+        if (scales_small<D, NG>(sbp, lane))
+          tc_subblock<D, NG, true>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+        else
+          tc_subblock<D, NG, false>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
       }
-      if (!split) {
-        store_out(p.out, p.out_dtype, out_row + idx, Os / Ls);
-      } else {
-        part[16 + h * D + d] = Os;
-        if (d == 0) {
-          part[h] = M;
-          part[8 + h] = Ls;
+      J += n_sb;
+      if (h == Hkv - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
+
+      // ---- combine the warps' states for this (item, head) ----
+      float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+      }
+      named_bar(kConsumerBar, NCW * 32);  // previous combine's reads are done
+      {
+        const int r = lane >> 2, tig = lane & 3;
+        if (r == 0) {
+          cm[warp * 8 + 2 * tig] = st.m[0];
+          cm[warp * 8 + 2 * tig + 1] = st.m[1];
+          cl[warp * 8 + 2 * tig] = l0;
+          cl[warp * 8 + 2 * tig + 1] = l1;
+        }
+        constexpr int LD = SM::CO_LD;
+        float* co = cO + (size_t)warp * 8 * LD;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int d = 16 * mt + r;
+          co[(2 * tig) * LD + d] = st.o[mt][0];
+          co[(2 * tig + 1) * LD + d] = st.o[mt][1];
+          co[(2 * tig) * LD + d + 8] = st.o[mt][2];
+          co[(2 * tig + 1) * LD + d + 8] = st.o[mt][3];
         }
       }
-    }
-    if (split) {
-      __threadfence();
       named_bar(kConsumerBar, NCW * 32);
-      if (tid == 0) {
-        const int old = atomicAdd(&p.counters[item.unit], 1);
-        *last_flag = (old == un.n_items - 1);
-      }
-      named_bar(kConsumerBar, NCW * 32);
-      if (*last_flag) {
-        __threadfence();
-        const float* pb = p.partials + (int64_t)un.first_item * partial_floats(D);
-        for (int idx = tid; idx < g * D; idx += NCW * 32) {
-          const int h = idx / D, d = idx - h * D;
-          float M = -INFINITY;
-          for (int i = 0; i < un.n_items; ++i) M = fmaxf(M, __ldcg(pb + i * partial_floats(D) + h));
-          float Ls = 0.f, Os = 0.f;
-          for (int i = 0; i < un.n_items; ++i) {
-            const float* pr = pb + i * partial_floats(D);
-            const float mi = __ldcg(pr + h);
-            const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
-            Ls += __ldcg(pr + 8 + h) * f;
-            Os += __ldcg(pr + 16 + h * D + d) * f;
+      const int64_t rec = ((int64_t)un.first_item + item.idx) * Hkv + h;
+      float* part = p.partials + rec * partial_floats(D);
+      for (int idx = tid; idx < g * D; idx += NCW * 32) {
+        const int hq = idx / D, d = idx - hq * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) M = fmaxf(M, cm[w * 8 + hq]);
+        float Ls = 0.f, Os = 0.f;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+          const float mw = cm[w * 8 + hq];
+          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+          Ls += cl[w * 8 + hq] * f;
+          Os += cO[((size_t)w * 8 + hq) * SM::CO_LD + d] * f;
+        }
+        if (!split) {
+          store_out(p.out, p.out_dtype, qo_row + idx, Os / Ls);
+        } else {
+          part[16 + hq * D + d] = Os;
+          if (d == 0) {
+            part[hq] = M;
+            part[8 + hq] = Ls;
           }
-          store_out(p.out, p.out_dtype, out_row + idx, Os / Ls);
         }
-        if (tid == 0) p.counters[item.unit] = 0;
+      }
+      if (split) {
+        __threadfence();
+        named_bar(kConsumerBar, NCW * 32);
+        const int64_t ctr = (int64_t)item.unit * Hkv + h;
+        if (tid == 0) {
+          const int old = atomicAdd(&p.counters[ctr], 1);
+          *last_flag = (old == un.n_items - 1);
+        }
+        named_bar(kConsumerBar, NCW * 32);
+        if (*last_flag) {
+          __threadfence();
+          for (int idx = tid; idx < g * D; idx += NCW * 32) {
+            const int hq = idx / D, d = idx - hq * D;
+            float M = -INFINITY;
+            for (int i = 0; i < un.n_items; ++i) {
+              const float* pr = p.partials + (((int64_t)un.first_item + i) * Hkv + h) * partial_floats(D);
+              M = fmaxf(M, __ldcg(pr + hq));
+            }
+            float Ls = 0.f, Os = 0.f;
+            for (int i = 0; i < un.n_items; ++i) {
+              const float* pr = p.partials + (((int64_t)un.first_item + i) * Hkv + h) * partial_floats(D);
+              const float mi = __ldcg(pr + hq);
+              const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
+              Ls += __ldcg(pr + 8 + hq) * f;
+              Os += __ldcg(pr + 16 + hq * D + d) * f;
+            }
+            store_out(p.out, p.out_dtype, qo_row + idx, Os / Ls);
+          }
+          if (tid == 0) p.counters[ctr] = 0;
+        }
       }
     }
   }
