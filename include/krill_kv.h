@@ -90,9 +90,12 @@ typedef struct {
                              the ring: window - 1 + max_append tokens); 0 -> 256  */
   int32_t quant_variant;  /* KRILL_QUANT_*                                       */
   int32_t attn_impl;      /* KRILL_ATTN_*                                        */
-  int32_t split_tokens;   /* decode split-K chunk in tokens (multiple of 64);
-                             0 -> 2048. Fixed per pool, so a sequence's output
-                             does not depend on what else is in the batch.      */
+  int32_t split_tokens;   /* decode split-K piece in tokens (multiple of 64).
+                             0 = adaptive: pieces and head groups follow the
+                             batch shape (results depend on shapes, never on
+                             other sequences' contents). > 0 = fixed pieces and
+                             whole-layer head groups: a sequence's output is
+                             then bit-identical whatever else is batched.      */
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
 } krill_pool_cfg;
 
@@ -125,6 +128,12 @@ krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
 krill_status_t krill_pool_set_profiling(krill_pool_t pool, int32_t enable);
 krill_status_t krill_pool_kernel_times(krill_pool_t pool, double* attn_ms, int32_t* attn_launches,
                                        double* append_ms, int32_t* append_launches);
+
+/* Introspection (no reference counterpart): the decomposition chosen by the
+ * last krill_decode_attention on this pool — sequence piece length in 64-token
+ * sub-blocks, kv heads per work item, number of items and of persistent CTAs. */
+krill_status_t krill_pool_last_plan(krill_pool_t pool, int32_t* piece_subblocks,
+                                    int32_t* heads_per_item, int64_t* items, int32_t* ctas);
 
 /* ---- sequences (one request's per-layer caches) -------------------------- */
 /* New empty sequence: every layer at length 0 (QuantizedKVCache.init). */

@@ -120,6 +120,13 @@ class KVPool:
                                             C.byref(pn)))
         return am.value, an.value, pm.value, pn.value
 
+    def last_plan(self):
+        """(piece sub-blocks, kv heads per item, items, CTAs) of the last
+        decode-attention launch."""
+        c, hg, n, g = C.c_int32(), C.c_int32(), C.c_int64(), C.c_int32()
+        check(L.lib.krill_pool_last_plan(self.handle, C.byref(c), C.byref(hg), C.byref(n), C.byref(g)))
+        return c.value, hg.value, n.value, g.value
+
     def create_sequence(self) -> "Sequence_":
         h = C.c_uint64()
         check(L.lib.krill_seq_create(self.handle, C.byref(h)))

@@ -96,6 +96,10 @@ struct Plan {
   std::vector<int32_t> order, owner, count, fill;
   std::vector<std::pair<int64_t, int32_t>> heap;
   std::vector<uint8_t> dry;
+  std::vector<int64_t> nsb;
+  std::vector<int32_t> split_units;
+  int last_C = 0, last_HG = 0, last_grid = 0;
+  int64_t last_items = 0;
 };
 
 }  // namespace
@@ -113,8 +117,6 @@ struct krill_pool_s {
   int num_sms = 148;
   float* d_partials = nullptr;
   int64_t partials_cap = 0;
-  int* d_counters = nullptr;
-  int64_t counters_cap = 0;
   int* d_err = nullptr;
   StageSlot stage[kStageSlots];
   int stage_next = 0;
@@ -387,26 +389,16 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
 }
 
 // ---------------------------------------------------------------- attention
-krill_status_t ensure_scratch(krill_pool_t p, int64_t partial_count, int64_t units) {
+krill_status_t ensure_scratch(krill_pool_t p, int64_t records, int64_t /*unused*/) {
   const int64_t pf = partial_floats(p->geom.D);
-  if (partial_count * pf > p->partials_cap || units > p->counters_cap) {
-    // grows rarely (first launches); frees must not race kernels in flight
+  if (records * pf > p->partials_cap) {
+    // grows rarely (first launches); the free must not race kernels in flight
     CUDA_TRY(cudaDeviceSynchronize());
-    if (partial_count * pf > p->partials_cap) {
-      if (p->d_partials) cudaFree(p->d_partials);
-      p->d_partials = nullptr;
-      int64_t cap = std::max<int64_t>(partial_count * pf * 3 / 2, 1 << 20);
-      CUDA_TRY(cudaMalloc(&p->d_partials, (size_t)cap * sizeof(float)));
-      p->partials_cap = cap;
-    }
-    if (units > p->counters_cap) {
-      if (p->d_counters) cudaFree(p->d_counters);
-      p->d_counters = nullptr;
-      int64_t cap = std::max<int64_t>(units * 3 / 2, 4096);
-      CUDA_TRY(cudaMalloc(&p->d_counters, (size_t)cap * sizeof(int)));
-      CUDA_TRY(cudaMemset(p->d_counters, 0, (size_t)cap * sizeof(int)));
-      p->counters_cap = cap;
-    }
+    if (p->d_partials) cudaFree(p->d_partials);
+    p->d_partials = nullptr;
+    int64_t cap = std::max<int64_t>(records * pf * 3 / 2, 1 << 20);
+    CUDA_TRY(cudaMalloc(&p->d_partials, (size_t)cap * sizeof(float)));
+    p->partials_cap = cap;
   }
   return KRILL_OK;
 }
@@ -431,12 +423,11 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     TRY(seq_get(p, seqs[i], &pl.sv[i]));
     bt_stride = std::max<int64_t>(bt_stride, (int64_t)pl.sv[i]->blocks.size());
   }
-  // ---- units (layer, seq) and items (balanced split of each unit) ----
+  // ---- units (layer, seq) ----
   const int64_t n_units = (int64_t)lc * n_seqs;
-  const int C = std::max(1, p->cfg.split_tokens / kSubTokens);
   pl.units.resize((size_t)n_units);
-  pl.items.clear();
-  int64_t item_count = 0;
+  pl.nsb.resize((size_t)n_units);
+  int64_t total_sb = 0;
   for (int li = 0; li < lc; ++li) {
     const int L = lb + li;
     for (int si = 0; si < n_seqs; ++si) {
@@ -445,10 +436,6 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       if (len <= 0) return fail(KRILL_ERR_INVALID, "attention over an empty cache (layer %d)", L);
       const int64_t t_hi = len;
       const int64_t t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
-      const int64_t sb0 = t_lo / kSubTokens, sb1 = (t_hi + kSubTokens - 1) / kSubTokens;
-      const int64_t n_sb = sb1 - sb0;
-      const int64_t n_it = (n_sb + C - 1) / C;
-      const int64_t base = n_sb / n_it, extra = n_sb % n_it;
       const int64_t ui = (int64_t)li * n_seqs + si;
       AttnUnit& u = pl.units[ui];
       u.qo_row = (int32_t)ui;
@@ -456,19 +443,53 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       u.layer = L;
       u.t_lo = (int32_t)t_lo;
       u.t_hi = (int32_t)t_hi;
-      u.n_items = (int32_t)n_it;
-      u.first_item = (int32_t)item_count;
       u.pad = 0;
-      int64_t b = sb0;
-      for (int64_t i = 0; i < n_it; ++i) {
-        const int64_t sz = base + (i < extra ? 1 : 0);
-        pl.items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int32_t)i});
-        b += sz;
-      }
-      item_count += n_it;
+      pl.nsb[ui] = (t_hi + kSubTokens - 1) / kSubTokens - t_lo / kSubTokens;
+      total_sb += pl.nsb[ui];
     }
   }
-  if (!p->host_only) TRY(ensure_scratch(p, item_count * g.Hkv, n_units * g.Hkv));
+  // ---- decomposition: sequence piece length C (sub-blocks) and kv heads per
+  // item HG. A fixed split_tokens keeps C fixed and HG = Hkv, so a sequence's
+  // result does not depend on the batch; otherwise both follow the batch
+  // shape: the largest pieces such that one item is at most a quarter of a
+  // CTA's share, halving the head group when even 8-sub-block pieces are too
+  // coarse (small batches). Results depend only on shapes, never on contents.
+  int C, HG = g.Hkv;
+  if (p->cfg.split_tokens > 0) {
+    C = std::max(1, p->cfg.split_tokens / kSubTokens);
+  } else {
+    const int W = attn_warps(g.D);
+    const int64_t quarter = std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4);
+    while (HG > 1 && (int64_t)8 * HG > quarter && (HG % 2 == 0) &&
+           ((HG / 2) % W == 0 || W % (HG / 2) == 0))
+      HG /= 2;
+    C = 8;
+    while (C < 128 && (int64_t)(2 * C) * HG <= quarter) C *= 2;
+  }
+  // ---- items ----
+  pl.items.clear();
+  int64_t split_count = 0;
+  pl.split_units.clear();
+  for (int64_t ui = 0; ui < n_units; ++ui) {
+    AttnUnit& u = pl.units[ui];
+    const int64_t n_sb = pl.nsb[ui];
+    const int64_t n_it = (n_sb + C - 1) / C;
+    const int64_t base = n_sb / n_it, extra = n_sb % n_it;
+    u.n_split = (int32_t)n_it;
+    u.first_split = (int32_t)split_count;
+    if (n_it > 1) {
+      split_count += n_it;
+      pl.split_units.push_back((int32_t)ui);
+    }
+    int64_t b = u.t_lo / kSubTokens;
+    for (int64_t i = 0; i < n_it; ++i) {
+      const int64_t sz = base + (i < extra ? 1 : 0);
+      for (int h0 = 0; h0 < g.Hkv; h0 += HG)
+        pl.items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int16_t)i, (int16_t)h0});
+      b += sz;
+    }
+  }
+  if (!p->host_only) TRY(ensure_scratch(p, split_count * g.Hkv, 0));
   // ---- longest-processing-time assignment of items to persistent CTAs ----
   // Items are at most C sub-blocks, so a counting sort orders them by size.
   const int64_t n_items = (int64_t)pl.items.size();
@@ -508,7 +529,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   const size_t items_bytes = align16((size_t)n_items * sizeof(AttnItem));
   const size_t off_bytes = align16((size_t)(grid + 1) * sizeof(int32_t));
   const size_t bt_bytes = align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
-  const size_t total = units_bytes + items_bytes + off_bytes + bt_bytes;
+  const size_t su_bytes = align16((pl.split_units.size() + 1) * sizeof(int32_t));
+  const size_t total = units_bytes + items_bytes + off_bytes + bt_bytes + su_bytes;
   StageSlot* slot = nullptr;
   uint8_t* h;
   if (p->host_only) {
@@ -532,6 +554,13 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     if (nb) std::memcpy(bt + si * bt_stride, s.blocks.data(), nb * sizeof(int32_t));
     for (int64_t j = (int64_t)nb; j < bt_stride; ++j) bt[si * bt_stride + j] = -1;
   }
+  int32_t* su = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes + off_bytes + bt_bytes);
+  if (!pl.split_units.empty())
+    std::memcpy(su, pl.split_units.data(), pl.split_units.size() * sizeof(int32_t));
+  pl.last_C = C;
+  pl.last_HG = HG;
+  pl.last_items = n_items;
+  pl.last_grid = grid;
   if (p->host_only) return KRILL_OK;  // dry run: planned, nothing launched
   TRY(stage_upload(slot, total, stream));
   AttnParams ap{};
@@ -548,13 +577,15 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.cta_off = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes);
   ap.bt = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes);
   ap.bt_stride = (int)bt_stride;
+  ap.hg = HG;
+  ap.split_units = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes + bt_bytes);
+  ap.n_split_units = (int)pl.split_units.size();
   ap.q = q;
   ap.q_dtype = q_dtype;
   ap.out = out;
   ap.out_dtype = out_dtype;
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.partials = p->d_partials;
-  ap.counters = p->d_counters;
   ap.err = p->d_err;
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
   TRY(stage_release(slot, stream));
@@ -635,17 +666,24 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   if (cfg.head_dim != 64 && cfg.head_dim != 128 && cfg.head_dim != 256)
     return fail(KRILL_ERR_INVALID, "head_dim must be 64, 128 or 256");
   if (cfg.group_size == 0) cfg.group_size = 64;
-  if (cfg.group_size < 64 || cfg.head_dim % cfg.group_size != 0)
-    return fail(KRILL_ERR_INVALID, "group_size must divide head_dim and be >= 64");
+  if (cfg.group_size != 64 && cfg.group_size != cfg.head_dim)
+    return fail(KRILL_ERR_INVALID, "group_size must be 64 or head_dim");
+  {
+    // decode attention processes min(Hkv, W) kv heads at a time, W = 8 warps
+    // (4 for head_dim 256): Hkv must divide W or be a multiple of it
+    const int W = cfg.head_dim == 256 ? 4 : 8;
+    const int hpr = std::min(cfg.num_kv_heads, W);
+    if (W % hpr != 0 || cfg.num_kv_heads % hpr != 0)
+      return fail(KRILL_ERR_INVALID, "num_kv_heads must divide %d or be a multiple of it", W);
+  }
   if (cfg.window == 1 || cfg.window < 0) return fail(KRILL_ERR_INVALID, "window must be 0 or > 1");
   if (cfg.max_append <= 0) cfg.max_append = 256;
   if (cfg.quant_variant != KRILL_QUANT_F32 && cfg.quant_variant != KRILL_QUANT_INPUT_DTYPE)
     return fail(KRILL_ERR_INVALID, "bad quant_variant");
   if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE)
     return fail(KRILL_ERR_INVALID, "bad attn_impl");
-  if (cfg.split_tokens == 0) cfg.split_tokens = 2048;
-  if (cfg.split_tokens < 64 || cfg.split_tokens % 64 != 0)
-    return fail(KRILL_ERR_INVALID, "split_tokens must be a positive multiple of 64");
+  if (cfg.split_tokens < 0 || cfg.split_tokens % 64 != 0)
+    return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");
   if (cfg.num_blocks <= 0 || cfg.num_blocks > INT32_MAX)
     return fail(KRILL_ERR_INVALID, "num_blocks out of range");
   int ring = 0;
@@ -701,7 +739,6 @@ krill_status_t krill_pool_destroy(krill_pool_t p) {
     for (auto e : p->spare_events) cudaEventDestroy(e);
     if (p->d_pool) cudaFree(p->d_pool);
     if (p->d_partials) cudaFree(p->d_partials);
-    if (p->d_counters) cudaFree(p->d_counters);
     if (p->d_err) cudaFree(p->d_err);
   }
   delete p;
@@ -736,11 +773,7 @@ krill_status_t krill_pool_device_error(krill_pool_t p, int32_t* flag) {
   DeviceGuard dg(p->device);
   int v = 0;
   CUDA_TRY(cudaMemcpy(&v, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (v) {
-    CUDA_TRY(cudaMemset(p->d_err, 0, sizeof(int)));
-    // a bounded wait gave up mid-launch: split counters may be left non-zero
-    if (p->d_counters) CUDA_TRY(cudaMemset(p->d_counters, 0, (size_t)p->counters_cap * sizeof(int)));
-  }
+  if (v) CUDA_TRY(cudaMemset(p->d_err, 0, sizeof(int)));
   *flag = v;
   return KRILL_OK;
 }
@@ -773,6 +806,17 @@ krill_status_t krill_pool_kernel_times(krill_pool_t p, double* attn_ms, int32_t*
   if (attn_launches) *attn_launches = n[0];
   if (append_ms) *append_ms = t[1];
   if (append_launches) *append_launches = n[1];
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_last_plan(krill_pool_t p, int32_t* piece_subblocks, int32_t* heads_per_item,
+                                    int64_t* items, int32_t* ctas) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (piece_subblocks) *piece_subblocks = p->plan.last_C;
+  if (heads_per_item) *heads_per_item = p->plan.last_HG;
+  if (items) *items = p->plan.last_items;
+  if (ctas) *ctas = p->plan.last_grid;
   return KRILL_OK;
 }
 

@@ -40,14 +40,14 @@ struct ScatterIn {
 
 // One decode-attention unit: (layer, sequence) over all of its kv heads, with
 // the attended positions [t_lo, t_hi). Its sub-block range is split into
-// n_items items; each item is processed head by head by one CTA.
+// n_split sequence pieces; an item is one piece for one group of kv heads.
 struct AttnUnit {
-  int32_t qo_row;      // li * n_seqs + si : row of q/out
-  int32_t si;          // sequence index in the call (block-table row)
-  int32_t layer;       // absolute layer in the pool
-  int32_t t_lo, t_hi;  // attended positions
-  int32_t first_item;  // partial record of (item idx, head h): (first_item + idx) * Hkv + h
-  int32_t n_items;
+  int32_t qo_row;       // li * n_seqs + si : row of q/out
+  int32_t si;           // sequence index in the call (block-table row)
+  int32_t layer;        // absolute layer in the pool
+  int32_t t_lo, t_hi;   // attended positions
+  int32_t first_split;  // partial record of (piece i, head h): (first_split + i) * Hkv + h
+  int32_t n_split;
   int32_t pad;
 };
 
@@ -55,25 +55,28 @@ struct AttnItem {
   int32_t unit;
   int32_t sb_begin;  // logical sub-block range (positions 64*sb ...)
   int32_t sb_end;
-  int32_t idx;       // item index within its unit
+  int16_t idx;       // sequence piece within its unit
+  int16_t h0;        // first kv head of the item's head group
 };
 
 struct AttnParams {
   const uint8_t* pool;
   int64_t page_bytes, sb_bytes;
   int L, Hkv, Hq, g, ring;
+  int hg;                  // kv heads per item (divides Hkv)
   const AttnUnit* units;
   const AttnItem* items;
   const int32_t* cta_off;  // [grid + 1] item ranges per CTA
   const int32_t* bt;       // [n_seqs][bt_stride]
   int bt_stride;
+  const int32_t* split_units;  // units with n_split > 1 (merged by the combine kernel)
+  int n_split_units;
   const void* q;
   int q_dtype;
   void* out;
   int out_dtype;
   float scale_log2;  // softmax scale * log2(e)
-  float* partials;   // [items * Hkv][16 + 8*D]
-  int* counters;     // [units * Hkv], zero between launches
+  float* partials;   // [splits * Hkv][16 + 8*D]
   int* err;
 };
 
@@ -84,9 +87,12 @@ cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const i
                           int64_t p0, int64_t S, const GatherOut& out, cudaStream_t stream);
 cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
                            int64_t S, const ScatterIn& in, cudaStream_t stream);
-// grid = number of persistent CTAs (cta_off has grid + 1 entries).
+// grid = number of persistent CTAs (cta_off has grid + 1 entries). Launches
+// the attention kernel and, when some unit is split, the combine kernel.
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
+// Consumer warps per attention CTA for head_dim D.
+inline int attn_warps(int D) { return D >= 256 ? 4 : 8; }
 // Floats per partial record for head_dim D.
 __host__ __device__ inline int64_t partial_floats(int D) { return 16 + 8 * (int64_t)D; }
 

@@ -29,8 +29,6 @@
 namespace krill {
 namespace {
 
-constexpr int kConsumerBar = 1;  // named barrier id for consumer warps
-
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
@@ -79,9 +77,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
           dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
-}
-__device__ __forceinline__ void named_bar(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -362,38 +357,129 @@ __device__ __forceinline__ void store_out(void* out, int dtype, int64_t i, float
     reinterpret_cast<float*>(out)[i] = v;
 }
 
-template <int D, int NG, int NCW, int NSTAGE>
+template <int D, int NG, int NCW, int R, int NSTAGE>
 struct AttnSmem {
   static constexpr int SB = SubGeom<D, NG>::SB;
   static constexpr int STAGE_BYTES = NSTAGE * SB;
-  static constexpr int BAR_OFF = STAGE_BYTES;                      // 2*NSTAGE u64
-  static constexpr int CM_OFF = BAR_OFF + 2 * NSTAGE * 8;          // [NCW][8] f32
-  static constexpr int CL_OFF = CM_OFF + NCW * 8 * 4;              // [NCW][8] f32
-  static constexpr int CO_LD = D + 4;                              // padded: conflict-free stores
-  static constexpr int CO_OFF = CL_OFF + NCW * 8 * 4;              // [NCW][8][CO_LD] f32
-  static constexpr int MISC_OFF = CO_OFF + NCW * 8 * CO_LD * 4;    // abort flag, last flag
+  static constexpr int BAR_OFF = STAGE_BYTES;                 // 2*NSTAGE u64
+  static constexpr int NV = D / 16 * 4 + 4;                   // per-lane state floats
+  static constexpr int CB_OFF = BAR_OFF + 2 * NSTAGE * 8;     // [NCW][NV][32] f32 (R > 1)
+  static constexpr int CB_BYTES = R > 1 ? NCW * NV * 32 * 4 : 0;
+  static constexpr int MISC_OFF = CB_OFF + CB_BYTES;          // abort flag
   static constexpr int TOTAL = MISC_OFF + 16;
 };
 
-template <int D, int NG, int NCW, int NSTAGE>
-__global__ void __maxnreg__(D >= 256 ? 255 : 224) attn_tc_kernel(AttnParams p) {
-  using SM = AttnSmem<D, NG, NCW, NSTAGE>;
+// Number of 64-token stages that fit next to the rest of the shared memory.
+template <int D, int NG, int NCW, int R>
+constexpr int stages_for() {
+  constexpr int fixed = AttnSmem<D, NG, NCW, R, 0>::TOTAL;
+  constexpr int n = (232448 - fixed - 2 * 16 * 8) / SubGeom<D, NG>::SB;
+  return n > 16 ? 16 : n;
+}
+
+// Finish one (item, head) in the warp that holds the merged state: write the
+// normalized output, or a partial record plus the last-arriver merge when the
+// unit is split over several items.
+template <int D>
+__device__ __forceinline__ void finish_head(const AttnParams& p, const TCState<D>& st, float l0,
+                                            float l1, const AttnUnit& un, const AttnItem& item,
+                                            int h, int lane) {
+  const int r = lane >> 2, tig = lane & 3;
+  const int g = p.g;
+  const int Hkv = p.Hkv;
+  const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
+  const int h0 = 2 * tig, h1 = 2 * tig + 1;
+  if (un.n_split == 1) {
+    const float i0 = 1.f / l0, i1 = 1.f / l1;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int d = 16 * mt + r;
+      if (h0 < g) {
+        store_out(p.out, p.out_dtype, orow + h0 * D + d, st.o[mt][0] * i0);
+        store_out(p.out, p.out_dtype, orow + h0 * D + d + 8, st.o[mt][2] * i0);
+      }
+      if (h1 < g) {
+        store_out(p.out, p.out_dtype, orow + h1 * D + d, st.o[mt][1] * i1);
+        store_out(p.out, p.out_dtype, orow + h1 * D + d + 8, st.o[mt][3] * i1);
+      }
+    }
+    return;
+  }
+  const int64_t rec = ((int64_t)un.first_split + item.idx) * Hkv + h;
+  float* part = p.partials + rec * partial_floats(D);
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d = 16 * mt + r;
+    part[16 + h0 * D + d] = st.o[mt][0];
+    part[16 + h0 * D + d + 8] = st.o[mt][2];
+    part[16 + h1 * D + d] = st.o[mt][1];
+    part[16 + h1 * D + d + 8] = st.o[mt][3];
+  }
+  if (r == 0) {
+    part[h0] = st.m[0];
+    part[h1] = st.m[1];
+    part[8 + h0] = l0;
+    part[8 + h1] = l1;
+  }
+}
+
+// Merge the partial records of split units: one CTA per (split unit, kv head).
+template <int D>
+__global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
+  const int Hkv = p.Hkv, g = p.g;
+  const int u = p.split_units[blockIdx.x / Hkv];
+  const int h = blockIdx.x % Hkv;
+  const AttnUnit un = p.units[u];
+  const float* base = p.partials + ((int64_t)un.first_split * Hkv + h) * partial_floats(D);
+  const int64_t stride = (int64_t)Hkv * partial_floats(D);
+  __shared__ float sm[8], sinv[8];
+  if (threadIdx.x < g) {
+    const int hq = threadIdx.x;
+    float M = -INFINITY;
+    for (int i = 0; i < un.n_split; ++i) M = fmaxf(M, base[i * stride + hq]);
+    float Ls = 0.f;
+    for (int i = 0; i < un.n_split; ++i) {
+      const float mi = base[i * stride + hq];
+      Ls += (mi == -INFINITY) ? 0.f : base[i * stride + 8 + hq] * exp2f(mi - M);
+    }
+    sm[hq] = M;
+    sinv[hq] = 1.f / Ls;
+  }
+  __syncthreads();
+  const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
+  for (int idx = threadIdx.x; idx < g * D; idx += blockDim.x) {
+    const int hq = idx / D, d = idx - hq * D;
+    const float M = sm[hq];
+    float Os = 0.f;
+    for (int i = 0; i < un.n_split; ++i) {
+      const float mi = base[i * stride + hq];
+      if (mi != -INFINITY) Os += base[i * stride + 16 + hq * D + d] * exp2f(mi - M);
+    }
+    store_out(p.out, p.out_dtype, orow + idx, Os * sinv[hq]);
+  }
+}
+
+// Work split inside a CTA: an item covers hg kv heads; HPR = NCW / R of them
+// are processed at once, each by R warps (R = 1 when hg >= NCW), in hg / HPR
+// rounds. For an item of n_sb sub-blocks the
+// producer issues, per round, sub-block k of head hr as stage J0 + k*HPR + hr;
+// warp (hr, r) takes the sub-blocks k = r, r + R, ...
+template <int D, int NG, int NCW, int R, int NSTAGE>
+__global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p) {
+  using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
   constexpr int SB = SM::SB;
+  constexpr int HPR = NCW / R;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
   const uint32_t bar_base = smem_u32(smem + SM::BAR_OFF);
-  float* cm = reinterpret_cast<float*>(smem + SM::CM_OFF);
-  float* cl = reinterpret_cast<float*>(smem + SM::CL_OFF);
-  float* cO = reinterpret_cast<float*>(smem + SM::CO_OFF);
   volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF + 4);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(bar_base + 8 * s, 1);             // full: producer arrive + tx
-      mbar_init(bar_base + 8 * (NSTAGE + s), 1);  // empty: one consumer warp
+      mbar_init(bar_base + 8 * (NSTAGE + s), 1);  // empty: the consuming warp
     }
     *cta_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -402,54 +488,59 @@ __global__ void __maxnreg__(D >= 256 ? 255 : 224) attn_tc_kernel(AttnParams p) {
 
   const int it0 = p.cta_off[blockIdx.x], it1 = p.cta_off[blockIdx.x + 1];
   const int Hkv = p.Hkv;
+  const int rounds = p.hg / HPR;
 
   if (warp == NCW) {
     // ---------------- producer ----------------
     // The lanes fetch an item's block ids together (one coalesced load per 32
-    // blocks); lane 0 then issues one bulk copy per (head, sub-block) with no
-    // dependent global load in the issue loop.
+    // blocks); lane 0 issues the bulk copies with no dependent global load in
+    // the issue loop.
     const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
     uint32_t J = 0;
     for (int it = it0; it < it1; ++it) {
       const AttnItem item = p.items[it];
       const AttnUnit un = p.units[item.unit];
       const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
+      const int n_sb = item.sb_end - item.sb_begin;
       const int b0 = item.sb_begin >> 2;
       const int nblk = ((item.sb_end - 1) >> 2) - b0 + 1;
-      for (int c0 = 0; c0 < nblk; c0 += 32) {
-        int bi = b0 + c0 + lane;
-        if (p.ring > 0) bi %= p.ring;
-        const int blk = (c0 + lane < nblk) ? bt[bi] : 0;
-        const int jlo = max(item.sb_begin, (b0 + c0) * 4);
-        const int jhi = min(item.sb_end, (b0 + c0 + 32) * 4);
-        for (int h = 0; h < Hkv; ++h) {
-          const uint8_t* head_base = p.pool + ((int64_t)un.layer * Hkv + h) * p.page_bytes;
-          // sub-block order within the item: head-major, then position; the
-          // consumers use the same order (J advances identically)
+      for (int rd = 0; rd < rounds; ++rd) {
+        const uint8_t* layer_base =
+            p.pool + ((int64_t)un.layer * Hkv + item.h0 + rd * HPR) * p.page_bytes;
+        for (int c0 = 0; c0 < nblk; c0 += 32) {
+          int bi = b0 + c0 + lane;
+          if (p.ring > 0) bi %= p.ring;
+          const int blk = (c0 + lane < nblk) ? bt[bi] : 0;
+          const int jlo = max(item.sb_begin, (b0 + c0) * 4);
+          const int jhi = min(item.sb_end, (b0 + c0 + 32) * 4);
           for (int j = jlo; j < jhi; ++j) {
             const int b = __shfl_sync(0xffffffffu, blk, (j >> 2) - b0 - c0);
             if (lane == 0) {
-              const uint32_t Jh = J + (uint32_t)h * (item.sb_end - item.sb_begin) + (j - item.sb_begin);
-              const uint32_t stage = Jh % NSTAGE;
-              if (Jh >= (uint32_t)NSTAGE)
-                mbar_wait(bar_base + 8 * (NSTAGE + stage), ((Jh / NSTAGE) - 1) & 1, cta_abort, p.err);
-              const uint8_t* src = head_base + (int64_t)b * blk_stride + (int64_t)(j & 3) * SB;
-              const uint32_t full = bar_base + 8 * stage;
-              mbar_expect_tx(full, SB);
-              bulk_g2s(smem_u32(stages + (size_t)stage * SB), src, SB, full);
+              const uint8_t* sb_src = layer_base + (int64_t)b * blk_stride + (int64_t)(j & 3) * SB;
+              for (int hr = 0; hr < HPR; ++hr) {
+                const uint32_t Jh = J + (uint32_t)(j - item.sb_begin) * HPR + hr;
+                const uint32_t stage = Jh % NSTAGE;
+                if (Jh >= (uint32_t)NSTAGE)
+                  mbar_wait(bar_base + 8 * (NSTAGE + stage), ((Jh / NSTAGE) - 1) & 1, cta_abort,
+                            p.err);
+                const uint32_t full = bar_base + 8 * stage;
+                mbar_expect_tx(full, SB);
+                bulk_g2s(smem_u32(stages + (size_t)stage * SB), sb_src + (int64_t)hr * p.page_bytes,
+                         SB, full);
+              }
             }
           }
         }
+        J += (uint32_t)n_sb * HPR;
       }
-      J += (uint32_t)Hkv * (item.sb_end - item.sb_begin);
     }
     return;
   }
 
   // ---------------- consumers ----------------
+  const int hr = warp / R, rr = warp % R;
   TCState<D> st;
   uint32_t J = 0;
-  const int g = p.g;
   AttnItem item_next{};
   AttnUnit un_next{};
   if (it0 < it1) {
@@ -461,13 +552,13 @@ __global__ void __maxnreg__(D >= 256 ? 255 : 224) attn_tc_kernel(AttnParams p) {
     const AttnUnit un = un_next;
     if (it + 1 < it1) item_next = p.items[it + 1];
     const int n_sb = item.sb_end - item.sb_begin;
-    const bool split = un.n_items > 1;
-    for (int h = 0; h < Hkv; ++h) {
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int h = item.h0 + rd * HPR + hr;
       reset_state(st);
-      const int64_t qo_row = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
-      if (warp < n_sb) load_q<D>(st, p.q, p.q_dtype, qo_row, g, lane);
-      for (int k = warp; k < n_sb; k += NCW) {
-        const uint32_t jj = J + k;
+      if (rr < n_sb)
+        load_q<D>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g, lane);
+      for (int k = rr; k < n_sb; k += R) {
+        const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
         mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
         const int j = item.sb_begin + k;
@@ -481,109 +572,94 @@ __global__ void __maxnreg__(D >= 256 ? 255 : 224) attn_tc_kernel(AttnParams p) {
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
       }
-      J += n_sb;
-      if (h == Hkv - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
+      J += (uint32_t)n_sb * HPR;
+      if (rd == rounds - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
 
-      // ---- combine the warps' states for this (item, head) ----
       float l0 = st.l[0], l1 = st.l[1];
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
         l1 += __shfl_xor_sync(0xffffffffu, l1, off);
       }
-      named_bar(kConsumerBar, NCW * 32);  // previous combine's reads are done
-      {
-        const int r = lane >> 2, tig = lane & 3;
-        if (r == 0) {
-          cm[warp * 8 + 2 * tig] = st.m[0];
-          cm[warp * 8 + 2 * tig + 1] = st.m[1];
-          cl[warp * 8 + 2 * tig] = l0;
-          cl[warp * 8 + 2 * tig + 1] = l1;
-        }
-        constexpr int LD = SM::CO_LD;
-        float* co = cO + (size_t)warp * 8 * LD;
+      if constexpr (R > 1) {
+        // merge the R warps of this head through a lane-major buffer
+        float* cb = reinterpret_cast<float*>(smem + SM::CB_OFF);
+        const int nbar = 1 + hr;
+        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");  // buffer free
+        if (rr != 0) {
+          float* mine = cb + (size_t)warp * SM::NV * 32;
 #pragma unroll
-        for (int mt = 0; mt < D / 16; ++mt) {
-          const int d = 16 * mt + r;
-          co[(2 * tig) * LD + d] = st.o[mt][0];
-          co[(2 * tig + 1) * LD + d] = st.o[mt][1];
-          co[(2 * tig) * LD + d + 8] = st.o[mt][2];
-          co[(2 * tig + 1) * LD + d + 8] = st.o[mt][3];
-        }
-      }
-      named_bar(kConsumerBar, NCW * 32);
-      const int64_t rec = ((int64_t)un.first_item + item.idx) * Hkv + h;
-      float* part = p.partials + rec * partial_floats(D);
-      for (int idx = tid; idx < g * D; idx += NCW * 32) {
-        const int hq = idx / D, d = idx - hq * D;
-        float M = -INFINITY;
+          for (int mt = 0; mt < D / 16; ++mt)
 #pragma unroll
-        for (int w = 0; w < NCW; ++w) M = fmaxf(M, cm[w * 8 + hq]);
-        float Ls = 0.f, Os = 0.f;
-#pragma unroll
-        for (int w = 0; w < NCW; ++w) {
-          const float mw = cm[w * 8 + hq];
-          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-          Ls += cl[w * 8 + hq] * f;
-          Os += cO[((size_t)w * 8 + hq) * SM::CO_LD + d] * f;
+            for (int c = 0; c < 4; ++c) mine[(mt * 4 + c) * 32 + lane] = st.o[mt][c];
+          mine[(D / 4 + 0) * 32 + lane] = st.m[0];
+          mine[(D / 4 + 1) * 32 + lane] = st.m[1];
+          mine[(D / 4 + 2) * 32 + lane] = l0;
+          mine[(D / 4 + 3) * 32 + lane] = l1;
         }
-        if (!split) {
-          store_out(p.out, p.out_dtype, qo_row + idx, Os / Ls);
-        } else {
-          part[16 + hq * D + d] = Os;
-          if (d == 0) {
-            part[hq] = M;
-            part[8 + hq] = Ls;
+        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");
+        if (rr == 0) {
+#pragma unroll
+          for (int w = 1; w < R; ++w) {
+            const float* o = cb + (size_t)(warp + w) * SM::NV * 32;
+            const float m0 = o[(D / 4 + 0) * 32 + lane], m1 = o[(D / 4 + 1) * 32 + lane];
+            const float M0 = fmaxf(st.m[0], m0), M1 = fmaxf(st.m[1], m1);
+            const float a0 = (st.m[0] == -INFINITY) ? 0.f : exp2f(st.m[0] - M0);
+            const float a1 = (st.m[1] == -INFINITY) ? 0.f : exp2f(st.m[1] - M1);
+            const float b0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+            const float b1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+            l0 = l0 * a0 + o[(D / 4 + 2) * 32 + lane] * b0;
+            l1 = l1 * a1 + o[(D / 4 + 3) * 32 + lane] * b1;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+              st.o[mt][0] = st.o[mt][0] * a0 + o[(mt * 4 + 0) * 32 + lane] * b0;
+              st.o[mt][1] = st.o[mt][1] * a1 + o[(mt * 4 + 1) * 32 + lane] * b1;
+              st.o[mt][2] = st.o[mt][2] * a0 + o[(mt * 4 + 2) * 32 + lane] * b0;
+              st.o[mt][3] = st.o[mt][3] * a1 + o[(mt * 4 + 3) * 32 + lane] * b1;
+            }
+            st.m[0] = M0;
+            st.m[1] = M1;
           }
         }
       }
-      if (split) {
-        __threadfence();
-        named_bar(kConsumerBar, NCW * 32);
-        const int64_t ctr = (int64_t)item.unit * Hkv + h;
-        if (tid == 0) {
-          const int old = atomicAdd(&p.counters[ctr], 1);
-          *last_flag = (old == un.n_items - 1);
-        }
-        named_bar(kConsumerBar, NCW * 32);
-        if (*last_flag) {
-          __threadfence();
-          for (int idx = tid; idx < g * D; idx += NCW * 32) {
-            const int hq = idx / D, d = idx - hq * D;
-            float M = -INFINITY;
-            for (int i = 0; i < un.n_items; ++i) {
-              const float* pr = p.partials + (((int64_t)un.first_item + i) * Hkv + h) * partial_floats(D);
-              M = fmaxf(M, __ldcg(pr + hq));
-            }
-            float Ls = 0.f, Os = 0.f;
-            for (int i = 0; i < un.n_items; ++i) {
-              const float* pr = p.partials + (((int64_t)un.first_item + i) * Hkv + h) * partial_floats(D);
-              const float mi = __ldcg(pr + hq);
-              const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
-              Ls += __ldcg(pr + 8 + hq) * f;
-              Os += __ldcg(pr + 16 + hq * D + d) * f;
-            }
-            store_out(p.out, p.out_dtype, qo_row + idx, Os / Ls);
-          }
-          if (tid == 0) p.counters[ctr] = 0;
-        }
-      }
+      if (rr == 0) finish_head<D>(p, st, l0, l1, un, item, h, lane);
     }
   }
 }
 
-template <int D, int NG, int NCW, int NSTAGE>
+template <int D, int NG, int NCW, int R>
 cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
-  using SM = AttnSmem<D, NG, NCW, NSTAGE>;
+  constexpr int NSTAGE = stages_for<D, NG, NCW, R>();
+  using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
+  static_assert(NSTAGE >= 4, "too few stages");
   static_assert(SM::TOTAL <= 232448, "shared memory budget");
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, NSTAGE>,
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  attn_tc_kernel<D, NG, NCW, NSTAGE><<<grid, (NCW + 1) * 32, SM::TOTAL, stream>>>(p);
+  attn_tc_kernel<D, NG, NCW, R, NSTAGE><<<grid, (NCW + 1) * 32, SM::TOTAL, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D, int NG, int NCW>
+cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
+  const int hpr = p.hg < NCW ? p.hg : NCW;
+  if (NCW % hpr != 0 || p.hg % hpr != 0) return cudaErrorInvalidValue;
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (NCW / hpr) {
+    case 1: e = launch_tc<D, NG, NCW, 1>(p, grid, stream); break;
+    case 2: e = launch_tc<D, NG, NCW, 2>(p, grid, stream); break;
+    case 4: e = launch_tc<D, NG, NCW, 4>(p, grid, stream); break;
+    case 8:
+      if constexpr (NCW == 8) e = launch_tc<D, NG, NCW, 8>(p, grid, stream);
+      break;
+    default: break;
+  }
+  if (e != cudaSuccess || p.n_split_units == 0) return e;
+  attn_combine_kernel<D><<<p.n_split_units * p.Hkv, 128, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -593,12 +669,11 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
                              cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
   (void)impl;
-  if (g.D == 64 && g.NG == 1) return launch_tc<64, 1, 8, 16>(p, grid, stream);
-  if (g.D == 128 && g.NG == 2) return launch_tc<128, 2, 8, 11>(p, grid, stream);
-  if (g.D == 128 && g.NG == 1) return launch_tc<128, 1, 8, 11>(p, grid, stream);
-  if (g.D == 256 && g.NG == 4) return launch_tc<256, 4, 4, 5>(p, grid, stream);
-  if (g.D == 256 && g.NG == 2) return launch_tc<256, 2, 4, 5>(p, grid, stream);
-  if (g.D == 256 && g.NG == 1) return launch_tc<256, 1, 4, 5>(p, grid, stream);
+  if (g.D == 64 && g.NG == 1) return launch_tc_r<64, 1, 8>(p, grid, stream);
+  if (g.D == 128 && g.NG == 2) return launch_tc_r<128, 2, 8>(p, grid, stream);
+  if (g.D == 128 && g.NG == 1) return launch_tc_r<128, 1, 8>(p, grid, stream);
+  if (g.D == 256 && g.NG == 4) return launch_tc_r<256, 4, 4>(p, grid, stream);
+  if (g.D == 256 && g.NG == 1) return launch_tc_r<256, 1, 4>(p, grid, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -89,7 +89,10 @@ def run_case(D, G, hq, hkv, dtype, lengths, scale, out_dtype=torch.float32, wind
     (128, 64, 32, 8, BF16, 1 / math.sqrt(128)),  # Llama-3.1-8B shape (config 2)
     (128, 64, 32, 4, BF16, 1 / math.sqrt(128)),  # Qwen3-30B-A3B KV shape (GQA 8, config 4)
     (256, 64, 8, 4, F16, 1.0),            # Gemma-style D=256, GQA 2, scale 1 (config 5)
-    (128, 128, 16, 16, F16, 1 / math.sqrt(128)),  # G = D (strict reference scheme), MHA
+    (128, 128, 16, 16, F16, 1 / math.sqrt(128)),  # G = D (strict reference scheme), MHA, 2 rounds
+    (128, 64, 8, 2, BF16, 1 / math.sqrt(128)),   # 2 kv heads: 4 warps merge per head
+    (64, 64, 8, 1, F16, 1 / 8),                  # MQA: 8 warps merge on one head
+    (256, 256, 16, 2, BF16, 1.0),                # D=256, G=D, 2 kv heads
 ])
 def test_attention_ragged(D, G, hq, hkv, dtype, scale):
     run_case(D, G, hq, hkv, dtype, [1, 5, 63, 64, 65, 200, 700], scale)
@@ -137,3 +140,32 @@ def test_batch_invariance_bit_exact():
         torch.cuda.synchronize()
         assert torch.equal(out_one[:, 0], out_all[:, i])
     pool.close()
+
+
+def test_neighbor_content_isolation_bit_exact():
+    """BatchedDecodeLiveTests.swift:533-546 (cross-row isolation at a fixed
+    batch width): with the adaptive decomposition, a row's output is
+    bit-identical when only its neighbors' K/V/q contents change."""
+    D, hq, hkv, layers = 128, 32, 8, 2
+    lengths = [700, 1500, 333]
+    outs = []
+    for neighbor_seed in (11, 12):
+        rng_row = np.random.default_rng(3)
+        rng_nb = np.random.default_rng(neighbor_seed)
+        pool = kb.KVPool(layers, hkv, hq, D, num_blocks=64)  # adaptive split
+        seqs = []
+        for i, L in enumerate(lengths):
+            rng = rng_row if i == 0 else rng_nb
+            s = pool.create_sequence()
+            prefill(pool, s, to_bits(kv_values(rng, (layers, hkv, L, D)), BF16),
+                    to_bits(kv_values(rng, (layers, hkv, L, D)), BF16), BF16)
+            seqs.append(s)
+        qrow = to_bits(kv_values(np.random.default_rng(4), (layers, 1, hq, D)), BF16)
+        qnb = to_bits(kv_values(rng_nb, (layers, 2, hq, D)), BF16)
+        q = dev_bits(np.ascontiguousarray(np.concatenate([qrow, qnb], axis=1)), BF16)
+        out = torch.empty((layers, 3, hq, D), dtype=torch.float32, device="cuda")
+        kb.decode_attention(pool, seqs, 0, q, out, 0.1)
+        torch.cuda.synchronize()
+        outs.append(out[:, 0].clone())
+        pool.close()
+    assert torch.equal(outs[0], outs[1])
