@@ -183,6 +183,34 @@ krill_status_t krill_decode_attention(krill_pool_t pool, int32_t n_seqs, const k
                                       int32_t q_dtype, void* out, int32_t out_dtype, float scale,
                                       void* stream);
 
+/* Allocation-free decode attention. No counterpart in the reference: it
+ * exists for callers that cannot have the library allocate memory while they
+ * decode — an engine that has reserved all device memory for its own
+ * allocator, a serving loop that must not take the driver's allocation locks
+ * mid-step, a host that accounts for every device byte. Same arguments,
+ * layouts and results (within the attention tolerance) as
+ * krill_decode_attention, which grows its staging and split scratch with
+ * cudaMalloc / cudaMallocHost; this variant calls no allocating routine on
+ * success and instead uses a fixed scratch array of
+ * KRILL_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that
+ * loads the library holds until the process exits, plus a fixed host buffer.
+ *   - Limit: a call whose metadata plus split partials exceed the scratch
+ *     (roughly: many sequences longer than 4096 tokens at once) is rejected
+ *     with KRILL_ERR_INVALID and a message giving the bytes it would need.
+ *   - The first call on a device looks up the scratch's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one scratch and every call writes all of the scratch
+ *     it reads (nothing has to start zeroed), so calls serialise on the host,
+ *     and calls whose GPU work overlaps (different streams, no ordering
+ *     between them) race on the scratch: order them on one stream or
+ *     synchronise between them. */
+#define KRILL_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int32_t n_seqs,
+                                              const krill_seq_t* seqs, int32_t layer_begin,
+                                              int32_t layer_count, const void* q, int32_t q_dtype,
+                                              void* out, int32_t out_dtype, float scale,
+                                              void* stream);
+
 /* One decode step: krill_append_quantize (n_new = 1) then
  * krill_decode_attention over the same layers. */
 krill_status_t krill_decode_step(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,

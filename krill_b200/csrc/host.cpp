@@ -1478,3 +1478,165 @@ krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
 }
 
 }  // extern "C"
+
+// =====================================================================
+// Metadata for the allocation-free decode attention (kv_noalloc.cu)
+// =====================================================================
+namespace krill {
+
+krill_status_t set_error(krill_status_t code, const char* msg) { return fail(code, "%s", msg); }
+
+// Plans a decode-attention launch for krill_decode_attention_noalloc without
+// touching the pool's staging buffers or scratch, and without any heap
+// allocation on the success path: the metadata packet is written straight
+// into `buf` (host memory owned by the caller) using only fixed-size stack
+// state. Decomposition: every item covers all kv heads of a (layer,
+// sequence) and at most 64 sub-blocks (4096 tokens); items are dealt to CTAs
+// in serpentine order of decreasing size. On return `np->ap` holds every
+// launch parameter except the device pointers into the scratch, whose byte
+// offsets are in `np`.
+krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
+                            int32_t lc, const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                            float scale, uint8_t* buf, size_t buf_cap, NoAllocPlan* np) {
+  constexpr int C = 64;
+  constexpr int kMaxCtas = 1024;
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "compute call on a host-only pool");
+  TRY(check_layers(p, lb, lc));
+  TRY(check_dtype16(q_dtype, "q"));
+  if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
+    return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
+  if (n_seqs <= 0 || lc <= 0) return fail(KRILL_ERR_INVALID, "nothing to attend");
+  if (!seqs || !q || !out) return fail(KRILL_ERR_INVALID, "null q/out/seqs");
+  TRY(check_aligned(q, "q"));
+  TRY(check_aligned(out, "out"));
+  const Geom& g = p->geom;
+  // pass 1: sizes
+  int64_t bt_stride = 1, n_items = 0, splits = 0, n_split_units = 0;
+  for (int i = 0; i < n_seqs; ++i) {
+    Seq* s = nullptr;
+    TRY(seq_get(p, seqs[i], &s));
+    bt_stride = std::max<int64_t>(bt_stride, (int64_t)s->blocks.size());
+  }
+  auto span = [&](const Seq& s, int L, int64_t* t_lo, int64_t* sb0, int64_t* n_sb) {
+    const int64_t len = s.len[L];
+    *t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
+    *sb0 = *t_lo / kSubTokens;
+    *n_sb = (len + kSubTokens - 1) / kSubTokens - *sb0;
+  };
+  for (int li = 0; li < lc; ++li)
+    for (int si = 0; si < n_seqs; ++si) {
+      Seq* s = nullptr;
+      TRY(seq_get(p, seqs[si], &s));
+      if (s->len[lb + li] <= 0)
+        return fail(KRILL_ERR_INVALID, "attention over an empty cache (layer %d)", lb + li);
+      int64_t t_lo, sb0, n_sb;
+      span(*s, lb + li, &t_lo, &sb0, &n_sb);
+      const int64_t n_it = (n_sb + C - 1) / C;
+      n_items += n_it;
+      if (n_it > 1) {
+        splits += n_it;
+        n_split_units += 1;
+      }
+    }
+  const int64_t n_units = (int64_t)lc * n_seqs;
+  const int grid = (int)std::min<int64_t>(std::min(p->num_sms, kMaxCtas), n_items);
+  NoAllocPlan& o = *np;
+  o.units_off = 0;
+  o.items_off = align16((size_t)n_units * sizeof(AttnUnit));
+  o.cta_off_off = o.items_off + align16((size_t)n_items * sizeof(AttnItem));
+  o.bt_off = o.cta_off_off + align16((size_t)(grid + 1) * sizeof(int32_t));
+  o.su_off = o.bt_off + align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
+  o.packet_bytes = o.su_off + align16((size_t)(n_split_units + 1) * sizeof(int32_t));
+  o.partials_off = (o.packet_bytes + 255) & ~(size_t)255;
+  o.total_bytes = o.partials_off + (size_t)splits * g.Hkv * partial_floats(g.D) * sizeof(float);
+  if (o.total_bytes > buf_cap)
+    return fail(KRILL_ERR_INVALID,
+                "decode attention needs %zu bytes of scratch, above the %zu-byte limit of the "
+                "allocation-free entry point (use krill_decode_attention, or fewer/shorter "
+                "sequences per call)",
+                o.total_bytes, buf_cap);
+  // pass 2: units, split list, block tables
+  AttnUnit* units = reinterpret_cast<AttnUnit*>(buf + o.units_off);
+  int32_t* su = reinterpret_cast<int32_t*>(buf + o.su_off);
+  int64_t split_base = 0, n_su = 0;
+  for (int li = 0; li < lc; ++li)
+    for (int si = 0; si < n_seqs; ++si) {
+      Seq* s = nullptr;
+      TRY(seq_get(p, seqs[si], &s));
+      int64_t t_lo, sb0, n_sb;
+      span(*s, lb + li, &t_lo, &sb0, &n_sb);
+      const int64_t n_it = (n_sb + C - 1) / C;
+      const int64_t ui = (int64_t)li * n_seqs + si;
+      units[ui] = AttnUnit{(int32_t)ui, si, lb + li, (int32_t)t_lo, (int32_t)s->len[lb + li],
+                           (int32_t)split_base, (int32_t)n_it, 0};
+      if (n_it > 1) {
+        split_base += n_it;
+        su[n_su++] = (int32_t)ui;
+      }
+    }
+  int32_t* bt = reinterpret_cast<int32_t*>(buf + o.bt_off);
+  for (int si = 0; si < n_seqs; ++si) {
+    Seq* s = nullptr;
+    TRY(seq_get(p, seqs[si], &s));
+    for (int64_t j = 0; j < bt_stride; ++j)
+      bt[si * bt_stride + j] = j < (int64_t)s->blocks.size() ? s->blocks[j] : -1;
+  }
+  // pass 3: items in decreasing size, dealt serpentine to CTAs. CTA c gets
+  // items i with serp(i) = c; count them first to lay the CTA ranges out.
+  int32_t* off = reinterpret_cast<int32_t*>(buf + o.cta_off_off);
+  int32_t fill[kMaxCtas];
+  auto serp = [&](int64_t i) {
+    const int64_t round = i / grid, pos = i % grid;
+    return (int)((round & 1) ? grid - 1 - pos : pos);
+  };
+  for (int c = 0; c < grid; ++c) fill[c] = 0;
+  for (int64_t i = 0; i < n_items; ++i) fill[serp(i)] += 1;
+  off[0] = 0;
+  for (int c = 0; c < grid; ++c) {
+    off[c + 1] = off[c] + fill[c];
+    fill[c] = off[c];
+  }
+  AttnItem* hi = reinterpret_cast<AttnItem*>(buf + o.items_off);
+  int64_t rank = 0;
+  for (int sz = C; sz >= 1; --sz)
+    for (int64_t ui = 0; ui < n_units; ++ui) {
+      const AttnUnit& u = units[ui];
+      const int64_t sb0 = u.t_lo / kSubTokens;
+      const int64_t n_sb = (u.t_hi + kSubTokens - 1) / kSubTokens - sb0;
+      const int64_t n_it = u.n_split, base = n_sb / n_it, extra = n_sb % n_it;
+      int64_t b = sb0;
+      for (int64_t i = 0; i < n_it; ++i) {
+        const int64_t piece = base + (i < extra ? 1 : 0);
+        if (piece == sz)
+          hi[fill[serp(rank++)]++] = AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + piece), (int16_t)i, 0};
+        b += piece;
+      }
+    }
+  AttnParams& ap = o.ap;
+  ap = AttnParams{};
+  ap.pool = p->d_pool;
+  ap.page_bytes = g.page_bytes;
+  ap.sb_bytes = g.sb_bytes;
+  ap.L = g.L;
+  ap.Hkv = g.Hkv;
+  ap.Hq = g.Hq;
+  ap.g = g.g;
+  ap.ring = g.ring;
+  ap.hg = g.Hkv;
+  ap.bt_stride = (int)bt_stride;
+  ap.n_split_units = (int)n_su;
+  ap.q = q;
+  ap.q_dtype = q_dtype;
+  ap.out = out;
+  ap.out_dtype = out_dtype;
+  ap.scale_log2 = scale * 1.4426950408889634f;
+  ap.err = p->d_err;
+  o.geom = g;
+  o.grid = grid;
+  o.impl = p->cfg.attn_impl;
+  o.device = p->device;
+  return KRILL_OK;
+}
+
+}  // namespace krill

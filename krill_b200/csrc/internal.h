@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/krill_kv.h"
 #include "kv_common.cuh"
 
 namespace krill {
@@ -91,6 +92,24 @@ cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_
 // the attention kernel and, when some unit is split, the combine kernel.
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
+// Launch description produced for the allocation-free decode attention:
+// byte offsets of the metadata and partial records inside the caller's
+// scratch, plus the launch parameters (pointers into the scratch unset).
+struct NoAllocPlan {
+  size_t units_off, items_off, cta_off_off, bt_off, su_off;
+  size_t packet_bytes, partials_off, total_bytes;
+  AttnParams ap;
+  Geom geom;
+  int grid, impl, device;
+};
+
+// Plans a launch of the allocation-free decode attention into `buf` (host).
+krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
+                            int32_t lc, const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                            float scale, uint8_t* buf, size_t buf_cap, NoAllocPlan* np);
+// Sets the thread-local message returned by krill_last_error_string().
+krill_status_t set_error(krill_status_t code, const char* msg);
+
 // Consumer warps per attention CTA for head_dim D.
 inline int attn_warps(int D) { return D >= 256 ? 4 : 8; }
 // Floats per partial record for head_dim D.

@@ -1,0 +1,87 @@
+// kv_noalloc.cu — decode attention that allocates no memory.
+//
+// krill_decode_attention grows two kinds of memory on demand: pinned host +
+// device staging for each launch's metadata (work items, block tables) and a
+// device buffer for the per-piece partial results of long sequences. Some
+// callers cannot let the library allocate at decode time: an engine that
+// reserves all device memory up front for its own allocator (so a cudaMalloc
+// from the library would fail or fragment its arena), a serving loop that
+// must not take the driver's allocation locks in the middle of a step, or a
+// host that accounts for every device byte itself. This entry point serves
+// them: it does the same decode attention with its scratch in a fixed array
+// compiled into the library (KRILL_NOALLOC_SCRATCH_BYTES, present on every
+// GPU that loads the library until the process exits) and a fixed host
+// buffer for the metadata, and it calls no cudaMalloc, cudaFree,
+// cudaMallocHost or other allocating routine.
+//
+// The array's name in host code is only a stand-in for the device symbol, not
+// a device address, so the address kernels receive comes from
+// cudaGetSymbolAddress, looked up once per device with that device current
+// (on the first call that uses the device).
+#include <mutex>
+
+#include "internal.h"
+
+namespace {
+
+// The scratch every call shares: metadata packet, then partial records.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[KRILL_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;                        // one call at a time through the shared buffers
+void* g_scratch_addr[kMaxDevices];      // device address of g_noalloc_scratch per device
+alignas(64) uint8_t g_host_packet[KRILL_NOALLOC_SCRATCH_BYTES];  // host side of the metadata
+
+}  // namespace
+
+extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int32_t n_seqs,
+                                                         const krill_seq_t* seqs,
+                                                         int32_t layer_begin, int32_t layer_count,
+                                                         const void* q, int32_t q_dtype, void* out,
+                                                         int32_t out_dtype, float scale,
+                                                         void* stream) {
+  using namespace krill;
+  if (!pool) return set_error(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::mutex> lk(g_mu);
+  NoAllocPlan np;
+  krill_status_t st = noalloc_plan(pool, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out,
+                                   out_dtype, scale, g_host_packet, sizeof(g_host_packet), &np);
+  if (st != KRILL_OK) return st;
+  if (np.device < 0 || np.device >= kMaxDevices)
+    return set_error(KRILL_ERR_INVALID, "device index out of range for the no-alloc scratch");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != np.device) cudaSetDevice(np.device);
+  krill_status_t rc = KRILL_OK;
+  do {
+    if (!g_scratch_addr[np.device]) {
+      void* addr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+      if (e != cudaSuccess || !addr) {
+        rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+        break;
+      }
+      g_scratch_addr[np.device] = addr;
+    }
+    uint8_t* base = static_cast<uint8_t*>(g_scratch_addr[np.device]);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Pageable source: the call returns once g_host_packet has been read, so
+    // the next call may overwrite it.
+    cudaError_t e = cudaMemcpyAsync(base, g_host_packet, np.packet_bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+      rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+      break;
+    }
+    AttnParams ap = np.ap;
+    ap.units = reinterpret_cast<const AttnUnit*>(base + np.units_off);
+    ap.items = reinterpret_cast<const AttnItem*>(base + np.items_off);
+    ap.cta_off = reinterpret_cast<const int32_t*>(base + np.cta_off_off);
+    ap.bt = reinterpret_cast<const int32_t*>(base + np.bt_off);
+    ap.split_units = reinterpret_cast<const int32_t*>(base + np.su_off);
+    ap.partials = reinterpret_cast<float*>(base + np.partials_off);
+    e = launch_attention(np.geom, ap, np.grid, np.impl, s);
+    if (e != cudaSuccess) rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+  } while (false);
+  if (prev >= 0 && prev != np.device) cudaSetDevice(prev);
+  return rc;
+}
