@@ -72,18 +72,6 @@ def sample_lengths(cfg, n, seed_offset=0):
     return [int(x) for x in rng.integers(lo, hi + 1, size=n)]
 
 
-def lpt_partition(lengths, n_parts):
-    """Longest-processing-time partition of sequence indices by length."""
-    order = sorted(range(len(lengths)), key=lambda i: -lengths[i])
-    loads = [0] * n_parts
-    parts = [[] for _ in range(n_parts)]
-    for i in order:
-        r = min(range(n_parts), key=lambda j: (loads[j], j))
-        parts[r].append(i)
-        loads[r] += lengths[i]
-    return [sorted(p) for p in parts]
-
-
 class ClockSampler:
     """nvidia-smi clocks/throttle sampling during the timed region."""
 
@@ -242,6 +230,7 @@ def main():
     # ---- workload: global batch partitioned over ranks ----
     n_total = cfg["seqs"] * world
     lengths_all = sample_lengths(cfg, n_total)
+    from krill_b200.shard import lpt_partition
     parts = lpt_partition(lengths_all, world)
     mine = [lengths_all[i] for i in parts[rank]]
     layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
