@@ -134,6 +134,20 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def profiled_traffic(workload, algo_bytes):
+    """DRAM traffic of one attention launch, from the committed ncu summary of
+    this workload (dram bytes read + written per algorithmic byte on a
+    smaller capture of the same kernel, scaled to the full launch)."""
+    path = os.path.join(ROOT, "profiles", f"attn_tc_kernel_{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_per_algorithmic_byte:"):
+                return float(line.split(":")[1]) * algo_bytes
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline(cfg, lengths, steps, threads, layer_sample):
     """Time the oracle's reference-dataflow restatement on a bounded sample:
     all sequences, `layer_sample` of the layers, `steps` steps; scaled to the
@@ -371,7 +385,8 @@ def main():
                        "l2": f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)",
                        "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": profiled_traffic(args.config, attn_bytes),
                          "kernel": "attn_tc_kernel", "peak_kind": peak_kind,
                          "attn_ms": attn_mean_ms, "append_ms": float(np.mean(app_ms)),
                          "step_gbs": step_gbs, "algo_bytes_attn": attn_bytes,
