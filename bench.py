@@ -217,6 +217,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layer-sample", type=int, default=12)
     ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (profiling)")
+    ap.add_argument("--diag", action="store_true",
+                    help="per-rank, per-step kernel times and device error flags on stderr")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(CONFIGS[args.config])
@@ -238,6 +240,10 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+        # first collective up front, so NCCL's lazy setup never overlaps our kernels
+        warm = torch.ones(1, device=torch.device("cuda", local_rank))
+        dist.all_reduce(warm)
+        torch.cuda.synchronize()
 
     import krill_b200 as kb
 
@@ -289,6 +295,18 @@ def main():
         return float(t.item())
 
     # ---- device-timed region: inputs resident in HBM ----
+    if args.diag:
+        pool.set_profiling(True)
+        pool.kernel_times()
+        for i in range(args.warmup + args.steps):
+            kb.append_quantize(pool, seqs, 0, k_new, v_new, stream=stream)
+            kb.decode_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+            torch.cuda.synchronize()
+            am, an, pm, pn = pool.kernel_times()
+            print(f"[rank {rank} dev {torch.cuda.current_device()}] step {i}: attn {am:.3f} ms "
+                  f"append {pm:.3f} ms err {pool.device_error()} plan {pool.last_plan()}",
+                  file=sys.stderr, flush=True)
+        pool.set_profiling(False)
     for _ in range(args.warmup):
         kb.append_quantize(pool, seqs, 0, k_new, v_new, stream=stream)
         kb.decode_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
@@ -351,6 +369,9 @@ def main():
         stream.synchronize()
     e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
     barrier()
+    if args.diag:
+        print(f"[rank {rank}] timed {total_ms / args.steps:.3f} ms/step attn {attn_ms[0]:.3f} ms "
+              f"e2e {e2e_s * 1e3:.3f} ms/step err {pool.device_error()}", file=sys.stderr, flush=True)
     h2d = (h_k.numel() + h_v.numel() + h_q.numel()) * h_k.element_size()
     d2h = h_out.numel() * h_out.element_size()
     err_flag = pool.device_error()

@@ -12,7 +12,7 @@
 //   - the host plans work items = (layer, seq, kv-head, range of 64-token
 //     sub-blocks) and assigns them to CTAs by longest-processing-time;
 //   - a producer warp streams each item's sub-blocks HBM -> shared memory with
-//     bulk async copies (cp.async.bulk, no multicast) into an NSTAGE ring
+//     plain bulk async copies (cp.async.bulk, one CTA each) into an NSTAGE ring
 //     guarded by mbarriers;
 //   - NCW consumer warps take the item's sub-blocks round-robin. Tensor-core
 //     path (mma.sync m16n8k16, f16 in / f32 accumulate):
@@ -55,11 +55,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: gives up after ~2 s (or ~1 ms once the CTA has already seen a
-// timeout), records the error and returns false.
+// Bounded wait: gives up after ~10 s (20 us once the CTA has already seen a
+// timeout), records the error and returns false. The bound is far above any
+// legitimate wait (a 17 KB copy) yet short enough that a fault ends the
+// launch instead of hanging the GPU.
 __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t limit = *cta_abort ? 20000ull : 2000000000ull;
+  const uint64_t limit = *cta_abort ? 20000ull : 10000000000ull;
   const uint64_t t0 = globaltimer();
   for (;;) {
     if (mbar_try_wait(bar, phase)) return true;
