@@ -24,6 +24,8 @@
 //     fp32 partials and the last CTA to finish (atomic counter) merges them.
 // Every mbarrier wait is bounded; on timeout the kernel raises an error flag
 // and runs to completion instead of hanging.
+#include <atomic>
+
 #include "internal.h"
 
 namespace krill {
@@ -635,12 +637,17 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
   static_assert(NSTAGE >= 4, "too few stages");
   static_assert(SM::TOTAL <= 232448, "shared memory budget");
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
+  // the shared-memory opt-in is a per-device attribute: set it once per device
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.fetch_or(bit);
   }
   attn_tc_kernel<D, NG, NCW, R, NSTAGE><<<grid, (NCW + 1) * 32, SM::TOTAL, stream>>>(p);
   return cudaGetLastError();
