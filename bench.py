@@ -46,6 +46,14 @@ CONFIGS = {
                               lens=("fixed", 2048, 2048, 0), scale=1 / 8.0),
     "qwen3_30b_longctx": dict(layers=48, hq=32, hkv=4, D=128, G=64, dtype="bf16", seqs=16,
                               lens=("fixed", 32768, 32768, 3), scale=1 / math.sqrt(128)),
+    # 64 requests = one shared 4096-token prefix + a unique 256-token suffix
+    # 26 layers = 22 sliding (window 1024) + 4 global, D=256, 256 ragged seqs
+    "gemma_mixed_256": dict(layers=26, layers_global=4, layers_sliding=22, window=1024, hq=8, hkv=4,
+                            D=256, G=64, dtype="f16", seqs=256, lens=("uniform", 1024, 16384, 5),
+                            scale=1.0, shared_prefix=2048, shared_frac=0.3),
+    "llama31_8b_prefix64": dict(layers=32, hq=32, hkv=8, D=128, G=64, dtype="bf16", seqs=64,
+                                lens=("fixed", 4352, 4352, 2), scale=1 / math.sqrt(128),
+                                prefix=4096, suffix=256),
 }
 DEFAULT_CONFIG = "llama31_8b_batch32"
 
@@ -205,6 +213,262 @@ def run_reference_arm(args, cfg, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
+    """shared-prefix reuse. Every rank builds one 4096-token prefix
+    (bf16 N(0,1) K/V quantized by the append kernel) and stores it in its
+    prefix cache; its requests then look the prefix up (exact-key scan), fork
+    its blocks (reference-counted, nothing copied, no prefill of the prefix),
+    prefill only their unique 256-token suffix, and run decode steps (append 1
+    token + attention per request). Reports decode tokens/s, the logical bytes
+    (every request reads its whole cache) and the unique bytes (shared prefix
+    blocks counted once per layer per step)."""
+    layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
+    P, S, n = cfg["prefix"], cfg["suffix"], cfg["seqs"]
+    tdt = torch.bfloat16
+    dev = torch.device("cuda", local_rank)
+    steps_total = args.warmup + args.steps + 2
+    blocks = P // 256 + n * ((P + S + steps_total + 255) // 256 - P // 256 + 1) + 4
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, device=local_rank)
+    pc = kb.PrefixCache(pool)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    base = pool.create_sequence()
+    k = torch.randn((layers, 1, hkv, P, D), generator=gen, device=dev).to(tdt)
+    v = torch.randn((layers, 1, hkv, P, D), generator=gen, device=dev).to(tdt)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    kb.append_quantize(pool, [base], 0, k, v)
+    torch.cuda.synchronize()
+    prefix_prefill_s = time.perf_counter() - t0
+    prefix_tokens = list(range(P))
+    pc.store_quantized(prefix_tokens, "llama-3.1-8b", base)
+    # lookup + fork per request (host), then the suffix prefill (device)
+    t0 = time.perf_counter()
+    seqs, hits = [], 0
+    for r in range(n):
+        prompt = prefix_tokens + [1_000_000 + r * S + i for i in range(S)]
+        hit = pc.lookup_quantized(prompt, "llama-3.1-8b")
+        if hit is None:
+            hit = pc.lookup_longest_prefix_quantized(prompt, "llama-3.1-8b")
+        hits += hit is not None and hit.prefix_length == P
+        seqs.append(hit.fork(min(hit.prefix_length, len(prompt) - 1)))
+        hit.release()
+    lookup_fork_us = (time.perf_counter() - t0) / n * 1e6
+    refcount = pool.refcount(base.blocks()[0])
+    ks = torch.randn((layers, n, hkv, S, D), generator=gen, device=dev).to(tdt)
+    vs = torch.randn((layers, n, hkv, S, D), generator=gen, device=dev).to(tdt)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    kb.append_quantize(pool, seqs, 0, ks, vs)
+    torch.cuda.synchronize()
+    suffix_prefill_s = time.perf_counter() - t0
+    del k, v, ks, vs
+    k1 = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
+    v1 = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
+    q = torch.randn((layers, n, hq, D), generator=gen, device=dev).to(tdt)
+    out = torch.empty((layers, n, hq, D), dtype=tdt, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    len0 = seqs[0].length(0)
+    pool.set_profiling(True)
+    pool.kernel_times()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = start.elapsed_time(stop)
+    am, an, pm, pn = pool.kernel_times()
+    ms = total_ms / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_tok = hkv * (2 * D + 8 * D // G)
+    mean_len = len0 + (args.steps + 1) / 2
+    logical = n * layers * mean_len * per_tok + n * layers * 2 * hq * D * 2
+    unique = layers * (P + n * (mean_len - P)) * per_tok + n * layers * 2 * hq * D * 2
+    attn_ms = am / max(1, an)
+    peak, peak_kind = measured_peak()
+    if rank == 0:
+        line = {
+            "metric": "int8-KV decode-attn+append tokens/s (shared-prefix batch)",
+            "value": n * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic",
+            "config": {"workload": args.config, "requests_per_gpu": n, "prefix": P, "suffix": S,
+                       "layers": layers, "kv_heads": hkv, "head_dim": D, "group_size": G},
+            "prefix": {"hits": hits, "requests": n, "lookup_fork_us_per_request": lookup_fork_us,
+                       "prefix_block_refcount": refcount, "prefix_prefill_s": prefix_prefill_s,
+                       "suffix_prefill_s": suffix_prefill_s,
+                       "prefill_tokens_skipped_per_request": P,
+                       "gather_bytes_copied": 0,
+                       "reference_style_copy_bytes_per_request": layers * P * per_tok},
+            "roofline": {"bound": "hbm", "kernel": "attn_tc_kernel", "attn_ms": attn_ms,
+                         "append_ms": pm / max(1, pn),
+                         "achieved_logical": logical / (attn_ms / 1e3) / 1e9,
+                         "achieved_unique": unique / (attn_ms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                         "frac_unique": unique / (attn_ms / 1e3) / 1e9 / peak,
+                         "algo_bytes_logical": logical, "algo_bytes_unique": unique},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(),
+            "device_error_flag": pool.device_error(),
+        }
+        print(json.dumps(line), flush=True)
+    pc.close()
+    pool.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
+    """mixed local/global cache. Two pools per GPU: the 4 global
+    layers (full history) and the 22 sliding layers (window 1024, ring of
+    blocks, RotatingKVCache semantics). 256 sequences per GPU with lengths
+    U[1024, 16384]; 30% of them fork a shared 2048-token prefix in the global
+    pool (in the sliding layers the prefix's window is overwritten once a
+    sequence is 1024 tokens past it). One step = append + attention in both
+    pools. The cache is filled with f16 N(0,1) K/V through the append kernel
+    (sliding layers receive only their last window of tokens)."""
+    from krill_b200.shard import lpt_partition
+    Lg, Ls, W = cfg["layers_global"], cfg["layers_sliding"], cfg["window"]
+    hq, hkv, D, G = cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
+    n_total = cfg["seqs"] * world
+    lengths_all = sample_lengths(cfg, n_total)
+    mine = [lengths_all[i] for i in lpt_partition(lengths_all, world)[rank]]
+    n = len(mine)
+    rng = np.random.default_rng(17)
+    shared = set(i for i in range(n) if rng.random() < cfg["shared_frac"] and mine[i] > cfg["shared_prefix"])
+    P = cfg["shared_prefix"]
+    dev = torch.device("cuda", local_rank)
+    steps_total = args.warmup + args.steps + 2
+    blocks_g = sum((L + steps_total + 255) // 256 for L in mine) + 8
+    glob = kb.KVPool(Lg, hkv, hq, D, num_blocks=blocks_g, group_size=G, device=local_rank)
+    slid = kb.KVPool(Ls, hkv, hq, D, num_blocks=n * 5 + 8, group_size=G, window=W, max_append=256,
+                     device=local_rank)
+    pc = kb.PrefixCache(glob)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(999 + rank)
+    maxL = max(mine)
+    bufk = torch.randn((Lg * hkv * maxL * D,), generator=gen, device=dev).to(torch.float16)
+    bufv = torch.randn((Lg * hkv * maxL * D,), generator=gen, device=dev).to(torch.float16)
+
+    def chunk(buf, lc, L):
+        return buf[: lc * hkv * L * D].view(lc, 1, hkv, L, D)
+
+    t_fill = time.perf_counter()
+    base = glob.create_sequence()
+    kb.append_quantize(glob, [base], 0, chunk(bufk, Lg, P), chunk(bufv, Lg, P))
+    pc.store_quantized(list(range(P)), "gemma", base)
+    gseqs, sseqs = [], []
+    for i, L in enumerate(mine):
+        if i in shared:
+            prompt = list(range(P)) + [7_000_000 + i]
+            hit = pc.lookup_quantized(prompt, "gemma") or pc.lookup_longest_prefix_quantized(prompt, "gemma")
+            s = hit.fork(P)
+            hit.release()
+            kb.append_quantize(glob, [s], 0, chunk(bufk, Lg, L - P), chunk(bufv, Lg, L - P))
+        else:
+            s = glob.create_sequence()
+            kb.append_quantize(glob, [s], 0, chunk(bufk, Lg, L), chunk(bufv, Lg, L))
+        gseqs.append(s)
+    sk = torch.randn((Ls * hkv * 256 * D,), generator=gen, device=dev).to(torch.float16)
+    sv = torch.randn((Ls * hkv * 256 * D,), generator=gen, device=dev).to(torch.float16)
+    for L in mine:
+        s = slid.create_sequence()
+        for _ in range(min(L, W) // 256):
+            kb.append_quantize(slid, [s], 0, chunk(sk, Ls, 256), chunk(sv, Ls, 256))
+        sseqs.append(s)
+    del bufk, bufv
+    torch.cuda.synchronize()
+    t_fill = time.perf_counter() - t_fill
+    kg = torch.randn((Lg, n, hkv, 1, D), generator=gen, device=dev).to(torch.float16)
+    ks = torch.randn((Ls, n, hkv, 1, D), generator=gen, device=dev).to(torch.float16)
+    qg = torch.randn((Lg, n, hq, D), generator=gen, device=dev).to(torch.float16)
+    qs = torch.randn((Ls, n, hq, D), generator=gen, device=dev).to(torch.float16)
+    og, os_ = torch.empty_like(qg), torch.empty_like(qs)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        kb.decode_step(glob, gseqs, 0, kg, kg, qg, og, cfg["scale"], stream=stream)
+        kb.decode_step(slid, sseqs, 0, ks, ks, qs, os_, cfg["scale"], stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    lg0 = [s.length(0) for s in gseqs]
+    glob.set_profiling(True)
+    slid.set_profiling(True)
+    glob.kernel_times()
+    slid.kernel_times()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    ag, _, pg, _ = glob.kernel_times()
+    as_, _, ps, _ = slid.kernel_times()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_tok = hkv * (2 * D + 8 * D // G)
+    mid = (args.steps + 1) / 2
+    glob_b = sum(L + mid for L in lg0) * Lg * per_tok
+    glob_unique = glob_b - len(shared) * P * Lg * per_tok + P * Lg * per_tok
+    slid_b = n * min(W, W) * Ls * per_tok
+    qo = n * (Lg + Ls) * 2 * hq * D * 2
+    attn_ms = (ag + as_) / args.steps
+    peak, peak_kind = measured_peak()
+    if rank == 0:
+        line = {
+            "metric": "int8-KV decode-attn+append tokens/s (mixed sliding/global)",
+            "value": n_total / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic",
+            "config": {"workload": args.config, "seqs_per_gpu": n, "global_layers": Lg,
+                       "sliding_layers": Ls, "window": W, "head_dim": D, "kv_heads": hkv,
+                       "q_heads": hq, "shared_prefix_seqs": len(shared),
+                       "mean_len": float(np.mean(lengths_all))},
+            "roofline": {"bound": "hbm", "kernel": "attn_tc_kernel", "attn_ms": attn_ms,
+                         "attn_ms_global": ag / args.steps, "attn_ms_sliding": as_ / args.steps,
+                         "append_ms": (pg + ps) / args.steps,
+                         "achieved": (glob_b + slid_b + qo) / (attn_ms / 1e3) / 1e9,
+                         "achieved_unique": (glob_unique + slid_b + qo) / (attn_ms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                         "frac": (glob_b + slid_b + qo) / (attn_ms / 1e3) / 1e9 / peak,
+                         "algo_bytes": glob_b + slid_b + qo},
+            "gpu_launches": 4 * args.steps, "fill_s": t_fill, "clocks": clocks.summary(),
+            "device_error_flag": glob.device_error() | slid.device_error(),
+        }
+        print(json.dumps(line), flush=True)
+    pc.close()
+    glob.close()
+    slid.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -246,6 +510,13 @@ def main():
         torch.cuda.synchronize()
 
     import krill_b200 as kb
+
+    if "prefix" in cfg:
+        run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank)
+        return
+    if "window" in cfg:
+        run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank)
+        return
 
     # ---- workload: global batch partitioned over ranks ----
     n_total = cfg["seqs"] * world
