@@ -444,7 +444,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       u.t_lo = (int32_t)t_lo;
       u.t_hi = (int32_t)t_hi;
       u.pad = 0;
-      pl.nsb[ui] = (t_hi + kSubTokens - 1) / kSubTokens - t_lo / kSubTokens;
+      pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - t_lo / g.subt;
       total_sb += pl.nsb[ui];
     }
   }
@@ -456,7 +456,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   // coarse (small batches). Results depend only on shapes, never on contents.
   int C, HG = g.Hkv;
   if (p->cfg.split_tokens > 0) {
-    C = std::max(1, p->cfg.split_tokens / kSubTokens);
+    C = std::max(1, p->cfg.split_tokens / g.subt);
   } else {
     const int W = attn_warps(g.D);
     const int64_t quarter = std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4);
@@ -481,7 +481,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       split_count += n_it;
       pl.split_units.push_back((int32_t)ui);
     }
-    int64_t b = u.t_lo / kSubTokens;
+    int64_t b = u.t_lo / g.subt;
     for (int64_t i = 0; i < n_it; ++i) {
       const int64_t sz = base + (i < extra ? 1 : 0);
       for (int h0 = 0; h0 < g.Hkv; h0 += HG)
@@ -669,9 +669,9 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   if (cfg.group_size != 64 && cfg.group_size != cfg.head_dim)
     return fail(KRILL_ERR_INVALID, "group_size must be 64 or head_dim");
   {
-    // decode attention processes min(Hkv, W) kv heads at a time, W = 8 warps
-    // (4 for head_dim 256): Hkv must divide W or be a multiple of it
-    const int W = cfg.head_dim == 256 ? 4 : 8;
+    // decode attention processes min(Hkv, W) kv heads at a time, W = 8 warps:
+    // Hkv must divide W or be a multiple of it
+    const int W = 8;
     const int hpr = std::min(cfg.num_kv_heads, W);
     if (W % hpr != 0 || cfg.num_kv_heads % hpr != 0)
       return fail(KRILL_ERR_INVALID, "num_kv_heads must divide %d or be a multiple of it", W);
@@ -1521,8 +1521,8 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   auto span = [&](const Seq& s, int L, int64_t* t_lo, int64_t* sb0, int64_t* n_sb) {
     const int64_t len = s.len[L];
     *t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
-    *sb0 = *t_lo / kSubTokens;
-    *n_sb = (len + kSubTokens - 1) / kSubTokens - *sb0;
+    *sb0 = *t_lo / g.subt;
+    *n_sb = (len + g.subt - 1) / g.subt - *sb0;
   };
   for (int li = 0; li < lc; ++li)
     for (int si = 0; si < n_seqs; ++si) {
@@ -1602,8 +1602,8 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   for (int sz = C; sz >= 1; --sz)
     for (int64_t ui = 0; ui < n_units; ++ui) {
       const AttnUnit& u = units[ui];
-      const int64_t sb0 = u.t_lo / kSubTokens;
-      const int64_t n_sb = (u.t_hi + kSubTokens - 1) / kSubTokens - sb0;
+      const int64_t sb0 = u.t_lo / g.subt;
+      const int64_t n_sb = (u.t_hi + g.subt - 1) / g.subt - sb0;
       const int64_t n_it = u.n_split, base = n_sb / n_it, extra = n_sb % n_it;
       int64_t b = sb0;
       for (int64_t i = 0; i < n_it; ++i) {

@@ -111,7 +111,7 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
 krill_status_t set_error(krill_status_t code, const char* msg);
 
 // Consumer warps per attention CTA for head_dim D.
-inline int attn_warps(int D) { return D >= 256 ? 4 : 8; }
+inline int attn_warps(int /*D*/) { return 8; }
 // Floats per partial record for head_dim D.
 __host__ __device__ inline int64_t partial_floats(int D) { return 16 + 8 * (int64_t)D; }
 

@@ -74,6 +74,25 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort,
     }
   }
 }
+// A consumer may reach a stage several uses ahead of the producer (its
+// stages are HPR*R apart and it may skip items), and a parity wait cannot
+// tell phase u+1 from phase u-1. The producer therefore tags each stage with
+// the sequence number it is filling before arming the barrier; a consumer
+// first waits (bounded) for its own tag, after which the parity wait is exact.
+__device__ bool wait_tag(volatile uint32_t* tag, uint32_t want, volatile int* cta_abort, int* err) {
+  if (*tag == want) return true;
+  const uint64_t limit = *cta_abort ? 20000ull : 10000000000ull;
+  const uint64_t t0 = globaltimer();
+  while (*tag != want) {
+    if (globaltimer() - t0 > limit) {
+      *cta_abort = 1;
+      atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                          uint32_t bar) {
   asm volatile(
@@ -126,12 +145,16 @@ __device__ __forceinline__ uint32_t neg1024(uint32_t s2) {
 template <int D, int NG>
 struct SubGeom {
   static constexpr int G = D / NG;
-  static constexpr int SB = 64 * (2 * D + 8 * NG);
-  static constexpr int VOFF = 64 * D;
-  static constexpr int META = 128 * D;
+  static constexpr int T = sub_tokens(D);   // tokens per sub-block
+  static constexpr int SPB = kBlockTokens / T;
+  static constexpr int NU = T / 16;          // 16-token m-tiles per sub-block
+  static constexpr int TPT = T / 4;          // tokens per lane chunk (V rows)
+  static constexpr int SB = T * (2 * D + 8 * NG);
+  static constexpr int VOFF = T * D;
+  static constexpr int META = 2 * T * D;
   // meta array a, group gi, token t -> byte offset
   static __device__ __forceinline__ int meta(int a, int gi, int t) {
-    return META + (a * NG + gi) * 128 + t * 2;
+    return META + ((a * NG + gi) * T + t) * 2;
   }
 };
 
@@ -140,7 +163,7 @@ struct SubGeom {
 template <int D, int NG>
 __device__ __forceinline__ bool scales_small(const uint8_t* __restrict__ sb, int lane) {
   using SG = SubGeom<D, NG>;
-  constexpr int BYTES = NG * 128;  // one [NG][64] f16 array
+  constexpr int BYTES = NG * SG::T * 2;  // one [NG][T] f16 array
   bool big = false;
   for (int off = lane * 16; off < 2 * BYTES; off += 512) {
     const int a = off / BYTES;  // 0: K scales, 1: V scales (meta array 2)
@@ -212,11 +235,15 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
   const int r = lane >> 2, tig = lane & 3;
   const uint32_t selh = (r & 1) ? 0x3232u : 0x1010u;
 
-  // ---- K phase: Sᵀ = Kdeq · Qᵀ for 4 m-tiles of 16 tokens ----
-  float s[4][4];
+  // ---- K phase: Sᵀ = Kdeq · Qᵀ for NU m-tiles of 16 tokens ----
+  // Rows r and r + 8 of m-tile u hold tokens TPT*(r>>1) + 4u + (r&1) and that
+  // plus 2: after movmatrix.trans this is exactly the token order of the V
+  // fragments, where lane tig holds tokens TPT*tig + 4u + 0..3.
+  constexpr int NU = SG::NU, TPT = SG::TPT;
+  float s[NU][4];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int tbase = 16 * (r >> 1) + 4 * u;
+  for (int u = 0; u < NU; ++u) {
+    const int tbase = TPT * (r >> 1) + 4 * u;
     const int ta = tbase + (r & 1);
     const int tb = ta + 2;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -263,7 +290,7 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
   // ---- online softmax (heads 2*tig, 2*tig+1 live in this lane) ----
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
+  for (int u = 0; u < NU; ++u) {
     mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
     mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
   }
@@ -279,9 +306,9 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
   st.m[0] = mn0;
   st.m[1] = mn1;
   float ps0 = 0.f, ps1 = 0.f;
-  uint32_t pb[4][2];
+  uint32_t pb[NU][2];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
+  for (int u = 0; u < NU; ++u) {
     const float p0 = exp2f(s[u][0] - b0), p1 = exp2f(s[u][1] - b1);
     const float p2 = exp2f(s[u][2] - b0), p3 = exp2f(s[u][3] - b1);
     ps0 += p0 + p2;
@@ -303,37 +330,49 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
   const uint8_t* vt = sb + SG::VOFF;
 #pragma unroll
   for (int grp = 0; grp < NG; ++grp) {
-    const uint4 s_lo = *reinterpret_cast<const uint4*>(sb + SG::meta(2, grp, 16 * tig));
-    const uint4 s_hi = *reinterpret_cast<const uint4*>(sb + SG::meta(2, grp, 16 * tig + 8));
-    const uint4 z_lo = *reinterpret_cast<const uint4*>(sb + SG::meta(3, grp, 16 * tig));
-    const uint4 z_hi = *reinterpret_cast<const uint4*>(sb + SG::meta(3, grp, 16 * tig + 8));
-    uint32_t vs[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
-    uint32_t vz[8] = {z_lo.x, z_lo.y, z_lo.z, z_lo.w, z_hi.x, z_hi.y, z_hi.z, z_hi.w};
+    // this lane's TPT tokens: TPT*tig .. TPT*tig + TPT - 1 (TPT/2 words of two)
+    constexpr int NW = TPT / 2;
+    uint32_t vs[NW], vz[NW];
+#pragma unroll
+    for (int c = 0; c < NW / 4; ++c) {
+      const uint4 sw = *reinterpret_cast<const uint4*>(sb + SG::meta(2, grp, TPT * tig + 8 * c));
+      const uint4 zw = *reinterpret_cast<const uint4*>(sb + SG::meta(3, grp, TPT * tig + 8 * c));
+      vs[4 * c] = sw.x; vs[4 * c + 1] = sw.y; vs[4 * c + 2] = sw.z; vs[4 * c + 3] = sw.w;
+      vz[4 * c] = zw.x; vz[4 * c + 1] = zw.y; vz[4 * c + 2] = zw.z; vz[4 * c + 3] = zw.w;
+    }
     if (boundary) {
       // Invalid tokens get scale = zero = 0 so their (possibly stale) codes
       // dequantize to exactly 0 and cannot inject non-finite values.
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int p = pos0 + 16 * tig + 2 * i;
+      for (int i = 0; i < NW; ++i) {
+        const int p = pos0 + TPT * tig + 2 * i;
         const uint32_t m = ((p >= t_lo && p < t_hi) ? 0x0000ffffu : 0u) |
                            ((p + 1 >= t_lo && p + 1 < t_hi) ? 0xffff0000u : 0u);
         vs[i] &= m;
         vz[i] &= m;
       }
     }
-    uint32_t nvs[8];
+    uint32_t nvs[NW];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) nvs[i] = FAST ? neg1024(vs[i]) : 0u;
+    for (int i = 0; i < NW; ++i) nvs[i] = FAST ? neg1024(vs[i]) : 0u;
 #pragma unroll
     for (int mi = 0; mi < SG::G / 16; ++mi) {
       const int mt = grp * (SG::G / 16) + mi;
       const int d = 16 * mt + r;
-      const uint4 x = *reinterpret_cast<const uint4*>(vt + d * 64 + 16 * tig);
-      const uint4 y = *reinterpret_cast<const uint4*>(vt + (d + 8) * 64 + 16 * tig);
-      const uint32_t xv[4] = {x.x, x.y, x.z, x.w};
-      const uint32_t yv[4] = {y.x, y.y, y.z, y.w};
+      uint32_t xv[NU], yv[NU];
+      if constexpr (NU == 4) {
+        const uint4 x = *reinterpret_cast<const uint4*>(vt + d * SG::T + TPT * tig);
+        const uint4 y = *reinterpret_cast<const uint4*>(vt + (d + 8) * SG::T + TPT * tig);
+        xv[0] = x.x; xv[1] = x.y; xv[2] = x.z; xv[3] = x.w;
+        yv[0] = y.x; yv[1] = y.y; yv[2] = y.z; yv[3] = y.w;
+      } else {
+        const uint2 x = *reinterpret_cast<const uint2*>(vt + d * SG::T + TPT * tig);
+        const uint2 y = *reinterpret_cast<const uint2*>(vt + (d + 8) * SG::T + TPT * tig);
+        xv[0] = x.x; xv[1] = x.y;
+        yv[0] = y.x; yv[1] = y.y;
+      }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < NU; ++u) {
         uint32_t a0, a1, a2, a3;
         if constexpr (FAST) {
           a0 = deq2_fast(xv[u], 0x4140u, vs[2 * u], nvs[2 * u], vz[2 * u]);
@@ -367,9 +406,10 @@ struct AttnSmem {
   static constexpr int STAGE_BYTES = NSTAGE * SB;
   static constexpr int BAR_OFF = STAGE_BYTES;                 // 2*NSTAGE u64
   static constexpr int NV = D / 16 * 4 + 4;                   // per-lane state floats
-  static constexpr int CB_OFF = BAR_OFF + 2 * NSTAGE * 8;     // [NCW][NV][32] f32 (R > 1)
-  static constexpr int CB_BYTES = R > 1 ? NCW * NV * 32 * 4 : 0;
-  static constexpr int MISC_OFF = CB_OFF + CB_BYTES;          // abort flag
+  static constexpr int CB_OFF = BAR_OFF + 2 * NSTAGE * 8;     // [NCW - NCW/R][NV][32] f32
+  static constexpr int CB_BYTES = R > 1 ? (NCW - NCW / R) * NV * 32 * 4 : 0;
+  static constexpr int TAG_OFF = CB_OFF + CB_BYTES;           // [NSTAGE] u32 stage tags
+  static constexpr int MISC_OFF = TAG_OFF + ((NSTAGE * 4 + 15) / 16) * 16;  // abort flag
   static constexpr int TOTAL = MISC_OFF + 16;
 };
 
@@ -468,8 +508,16 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 // rounds. For an item of n_sb sub-blocks the
 // producer issues, per round, sub-block k of head hr as stage J0 + k*HPR + hr;
 // warp (hr, r) takes the sub-blocks k = r, r + R, ...
+// Threads: NCW consumer warps (two warpgroups) + one producer warpgroup, of
+// which one warp issues the copies. At start the producer warpgroup gives its
+// registers back (setmaxnreg.dec to 40) and the consumers take them
+// (setmaxnreg.inc to 232): 128*40 + 256*232 = 384*168, the launch budget.
+constexpr int kProducerRegs = 40;
+constexpr int kConsumerRegs = 232;
+
 template <int D, int NG, int NCW, int R, int NSTAGE>
-__global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p) {
+__global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
+  static_assert(NCW == 8, "two consumer warpgroups");
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
   constexpr int SB = SM::SB;
   constexpr int HPR = NCW / R;
@@ -477,6 +525,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
   uint8_t* stages = smem;
   const uint32_t bar_base = smem_u32(smem + SM::BAR_OFF);
   volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF);
+  volatile uint32_t* tags = reinterpret_cast<volatile uint32_t*>(smem + SM::TAG_OFF);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -485,6 +534,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
       mbar_init(bar_base + 8 * s, 1);             // full: producer arrive + tx
       mbar_init(bar_base + 8 * (NSTAGE + s), 1);  // empty: the consuming warp
     }
+    for (int s = 0; s < NSTAGE; ++s) tags[s] = 0xffffffffu;
     *cta_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -494,7 +544,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
   const int Hkv = p.Hkv;
   const int rounds = p.hg / HPR;
 
-  if (warp == NCW) {
+  if (warp >= NCW) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp != NCW) return;
     // ---------------- producer ----------------
     // The lanes fetch an item's block ids together (one coalesced load per 32
     // blocks); lane 0 issues the bulk copies with no dependent global load in
@@ -506,8 +558,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
       const AttnUnit un = p.units[item.unit];
       const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
       const int n_sb = item.sb_end - item.sb_begin;
-      const int b0 = item.sb_begin >> 2;
-      const int nblk = ((item.sb_end - 1) >> 2) - b0 + 1;
+      constexpr int SPB = SubGeom<D, NG>::SPB;
+      const int b0 = item.sb_begin / SPB;
+      const int nblk = (item.sb_end - 1) / SPB - b0 + 1;
       for (int rd = 0; rd < rounds; ++rd) {
         const uint8_t* layer_base =
             p.pool + ((int64_t)un.layer * Hkv + item.h0 + rd * HPR) * p.page_bytes;
@@ -515,12 +568,12 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
           int bi = b0 + c0 + lane;
           if (p.ring > 0) bi %= p.ring;
           const int blk = (c0 + lane < nblk) ? bt[bi] : 0;
-          const int jlo = max(item.sb_begin, (b0 + c0) * 4);
-          const int jhi = min(item.sb_end, (b0 + c0 + 32) * 4);
+          const int jlo = max(item.sb_begin, (b0 + c0) * SPB);
+          const int jhi = min(item.sb_end, (b0 + c0 + 32) * SPB);
           for (int j = jlo; j < jhi; ++j) {
-            const int b = __shfl_sync(0xffffffffu, blk, (j >> 2) - b0 - c0);
+            const int b = __shfl_sync(0xffffffffu, blk, j / SPB - b0 - c0);
             if (lane == 0) {
-              const uint8_t* sb_src = layer_base + (int64_t)b * blk_stride + (int64_t)(j & 3) * SB;
+              const uint8_t* sb_src = layer_base + (int64_t)b * blk_stride + (int64_t)(j % SPB) * SB;
               for (int hr = 0; hr < HPR; ++hr) {
                 const uint32_t Jh = J + (uint32_t)(j - item.sb_begin) * HPR + hr;
                 const uint32_t stage = Jh % NSTAGE;
@@ -528,6 +581,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
                   mbar_wait(bar_base + 8 * (NSTAGE + stage), ((Jh / NSTAGE) - 1) & 1, cta_abort,
                             p.err);
                 const uint32_t full = bar_base + 8 * stage;
+                tags[stage] = Jh;  // released by the arrive below
                 mbar_expect_tx(full, SB);
                 bulk_g2s(smem_u32(stages + (size_t)stage * SB), sb_src + (int64_t)hr * p.page_bytes,
                          SB, full);
@@ -542,6 +596,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
   }
 
   // ---------------- consumers ----------------
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   const int hr = warp / R, rr = warp % R;
   TCState<D> st;
   uint32_t J = 0;
@@ -564,10 +619,12 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
       for (int k = rr; k < n_sb; k += R) {
         const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
+        wait_tag(tags + stage, jj, cta_abort, p.err);
         mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
         const int j = item.sb_begin + k;
-        const int pos0 = j * 64;
-        const bool boundary = pos0 < un.t_lo || pos0 + 64 > un.t_hi;
+        constexpr int T = SubGeom<D, NG>::T;
+        const int pos0 = j * T;
+        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
         const uint8_t* sbp = stages + (size_t)stage * SB;
         if (scales_small<D, NG>(sbp, lane))
           tc_subblock<D, NG, true>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
@@ -591,7 +648,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
         const int nbar = 1 + hr;
         asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");  // buffer free
         if (rr != 0) {
-          float* mine = cb + (size_t)warp * SM::NV * 32;
+          float* mine = cb + (size_t)(hr * (R - 1) + rr - 1) * SM::NV * 32;
 #pragma unroll
           for (int mt = 0; mt < D / 16; ++mt)
 #pragma unroll
@@ -605,7 +662,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) attn_tc_kernel(AttnParams p
         if (rr == 0) {
 #pragma unroll
           for (int w = 1; w < R; ++w) {
-            const float* o = cb + (size_t)(warp + w) * SM::NV * 32;
+            const float* o = cb + (size_t)(hr * (R - 1) + w - 1) * SM::NV * 32;
             const float m0 = o[(D / 4 + 0) * 32 + lane], m1 = o[(D / 4 + 1) * 32 + lane];
             const float M0 = fmaxf(st.m[0], m0), M1 = fmaxf(st.m[1], m1);
             const float a0 = (st.m[0] == -INFINITY) ? 0.f : exp2f(st.m[0] - M0);
@@ -644,12 +701,19 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
+    // setmaxnreg.inc waits until the producer's released registers cover it:
+    // refuse to launch a build whose register count would not balance
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs * (NCW + 4) * 32 < 128 * kProducerRegs + NCW * 32 * kConsumerRegs)
+      return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
-  attn_tc_kernel<D, NG, NCW, R, NSTAGE><<<grid, (NCW + 1) * 32, SM::TOTAL, stream>>>(p);
+  attn_tc_kernel<D, NG, NCW, R, NSTAGE><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -681,8 +745,8 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
   if (g.D == 64 && g.NG == 1) return launch_tc_r<64, 1, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 2) return launch_tc_r<128, 2, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 1) return launch_tc_r<128, 1, 8>(p, grid, stream);
-  if (g.D == 256 && g.NG == 4) return launch_tc_r<256, 4, 4>(p, grid, stream);
-  if (g.D == 256 && g.NG == 1) return launch_tc_r<256, 1, 4>(p, grid, stream);
+  if (g.D == 256 && g.NG == 4) return launch_tc_r<256, 4, 8>(p, grid, stream);
+  if (g.D == 256 && g.NG == 1) return launch_tc_r<256, 1, 8>(p, grid, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -2,19 +2,17 @@
 //
 // HBM layout of one pool (one layer group on one GPU):
 //   pool = blocks[num_blocks]; block = pages[num_layers][num_kv_heads];
-//   page = 256 tokens = 4 sub-blocks of 64 tokens; each sub-block is one
-//   contiguous run of SB = 64 * (2*D + 8*NG) bytes:
-//     [0, 64*D)            K codes, token-major rows of D bytes; for D >= 128
+//   page = 256 tokens = sub-blocks of T tokens (T = 64, or 32 for D = 256 so
+//   that every sub-block is about 17 KB); each sub-block is one contiguous run
+//   of SB = T * (2*D + 8*NG) bytes:
+//     [0, T*D)             K codes, token-major rows of D bytes; for D >= 128
 //                          the 16-byte chunks of odd rows are XOR-swizzled by 4
 //                          so the decode kernel's shared-memory reads are
 //                          bank-conflict free
-//     [64*D, 128*D)        V codes transposed: D rows of 64 token bytes, so the
-//                          tensor-core B/A fragments along the token axis are
+//     [T*D, 2*T*D)         V codes transposed: D rows of T token bytes, so the
+//                          tensor-core fragments along the token axis are
 //                          contiguous bytes
-//     [128*D, +128*NG)     K scales  [NG][64] f16
-//     [+128*NG, +256*NG)   K zeros   [NG][64] f16
-//     [+256*NG, +384*NG)   V scales  [NG][64] f16
-//     [+384*NG, +512*NG)   V zeros   [NG][64] f16
+//     [2*T*D, ...)         K scales, K zeros, V scales, V zeros: [NG][T] f16 each
 // A sub-block is the unit one bulk (TMA) copy moves into shared memory.
 #pragma once
 #include <cuda_bf16.h>
@@ -24,8 +22,8 @@
 namespace krill {
 
 constexpr int kBlockTokens = 256;
-constexpr int kSubTokens = 64;
-constexpr int kSubPerBlock = kBlockTokens / kSubTokens;
+// Tokens per sub-block for head dim D.
+__host__ __device__ constexpr int sub_tokens(int D) { return D >= 256 ? 32 : 64; }
 
 struct Geom {
   int L;        // layers in the pool
@@ -38,6 +36,8 @@ struct Geom {
   int ring;     // blocks in a windowed sequence's ring; 0 = full history
   int window;   // sliding window (tokens); 0 = full history
   int quant_variant;
+  int subt;     // tokens per sub-block
+  int spb;      // sub-blocks per 256-token block
   int64_t sb_bytes;
   int64_t page_bytes;
   int64_t block_bytes;
@@ -47,18 +47,20 @@ inline Geom make_geom(int L, int Hkv, int Hq, int D, int G, int ring, int window
   Geom g;
   g.L = L; g.Hkv = Hkv; g.Hq = Hq; g.g = Hq / Hkv; g.D = D; g.G = G; g.NG = D / G;
   g.ring = ring; g.window = window; g.quant_variant = qv;
-  g.sb_bytes = (int64_t)kSubTokens * (2 * D + 8 * g.NG);
-  g.page_bytes = g.sb_bytes * kSubPerBlock;
+  g.subt = sub_tokens(D);
+  g.spb = kBlockTokens / g.subt;
+  g.sb_bytes = (int64_t)g.subt * (2 * D + 8 * g.NG);
+  g.page_bytes = g.sb_bytes * g.spb;
   g.block_bytes = g.page_bytes * L * Hkv;
   return g;
 }
 
 // Byte offsets inside a sub-block.
-__host__ __device__ inline int64_t sb_voff(int D) { return (int64_t)kSubTokens * D; }
-__host__ __device__ inline int64_t sb_meta_off(int D) { return (int64_t)2 * kSubTokens * D; }
+__host__ __device__ inline int64_t sb_voff(int D) { return (int64_t)sub_tokens(D) * D; }
+__host__ __device__ inline int64_t sb_meta_off(int D) { return (int64_t)2 * sub_tokens(D) * D; }
 // meta array a (0 = K scale, 1 = K zero, 2 = V scale, 3 = V zero), group gi, token t
 __host__ __device__ inline int64_t sb_meta(int D, int NG, int a, int gi, int t) {
-  return sb_meta_off(D) + ((int64_t)(a * NG + gi) * kSubTokens + t) * 2;
+  return sb_meta_off(D) + ((int64_t)(a * NG + gi) * sub_tokens(D) + t) * 2;
 }
 // Physical byte offset of K code (token t in sub-block, element d).
 __host__ __device__ inline int64_t sb_kcode(int D, int t, int d) {
@@ -67,7 +69,7 @@ __host__ __device__ inline int64_t sb_kcode(int D, int t, int d) {
   return (int64_t)t * D + chunk * 16 + (d & 15);
 }
 __host__ __device__ inline int64_t sb_vcode(int D, int t, int d) {
-  return sb_voff(D) + (int64_t)d * kSubTokens + t;
+  return sb_voff(D) + (int64_t)d * sub_tokens(D) + t;
 }
 
 // Error flag bits written by kernels (pool-owned int, read + cleared by host).

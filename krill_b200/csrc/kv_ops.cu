@@ -104,9 +104,9 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
   const int li = (int)(ls / n_seqs);
   const AppendDst d = dst[ls * n_new + tok];
   const int slot = d.pos & (kBlockTokens - 1);
-  const int t = slot & (kSubTokens - 1);
+  const int t = slot % geom.subt;
   uint8_t* sb = pool + (((int64_t)d.block * geom.L + (layer_begin + li)) * geom.Hkv + h) * geom.page_bytes +
-                (int64_t)(slot >> 6) * geom.sb_bytes;
+                (int64_t)(slot / geom.subt) * geom.sb_bytes;
 
   const int64_t elem_off = w * D;
   float xk[EPL], xv[EPL];
@@ -150,9 +150,9 @@ __global__ void gather_kernel(const uint8_t* __restrict__ pool, Geom geom, int l
   if (geom.ring > 0) bidx %= geom.ring;
   const int blk = bt[bidx];
   const int slot = (int)(pos & 255);
-  const int t = slot & 63;
+  const int t = slot % geom.subt;
   const uint8_t* sb = pool + (((int64_t)blk * geom.L + layer) * geom.Hkv + h) * geom.page_bytes +
-                      (int64_t)(slot >> 6) * geom.sb_bytes;
+                      (int64_t)(slot / geom.subt) * geom.sb_bytes;
   const int64_t orow = (int64_t)h * out.rows_total + out.row_off + i;
   const int d0 = e8 * 8;
   uint8_t kc[8], vc[8];
@@ -212,9 +212,9 @@ __global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
   if (geom.ring > 0) bidx %= geom.ring;
   const int blk = bt[bidx];
   const int slot = (int)(pos & 255);
-  const int t = slot & 63;
+  const int t = slot % geom.subt;
   uint8_t* sb = pool + (((int64_t)blk * geom.L + layer) * geom.Hkv + h) * geom.page_bytes +
-                (int64_t)(slot >> 6) * geom.sb_bytes;
+                (int64_t)(slot / geom.subt) * geom.sb_bytes;
   const int64_t irow = (int64_t)h * in.rows_total + in.row_off + i;
   const int d0 = e8 * 8;
   const uint2 kw = *reinterpret_cast<const uint2*>(in.keys + irow * D + d0);
