@@ -493,7 +493,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   // ---- longest-processing-time assignment of items to persistent CTAs ----
   // Items are at most C sub-blocks, so a counting sort orders them by size.
   const int64_t n_items = (int64_t)pl.items.size();
-  const int grid = (int)std::min<int64_t>(p->num_sms, n_items);
+  const int grid =
+      (int)std::min<int64_t>((int64_t)p->num_sms * attn_ctas_per_sm(p->cfg.attn_impl), n_items);
   pl.bucket.assign((size_t)C + 2, 0);
   for (const AttnItem& it : pl.items) pl.bucket[C - (it.sb_end - it.sb_begin)] += 1;
   for (int i = 1; i <= C + 1; ++i) pl.bucket[i] += pl.bucket[i - 1];

@@ -112,6 +112,9 @@ krill_status_t set_error(krill_status_t code, const char* msg);
 
 // Consumer warps per attention CTA for head_dim D.
 inline int attn_warps(int /*D*/) { return 8; }
+// Resident CTAs per SM the planner targets: one persistent tensor-core CTA
+// (it fills the shared memory), four of the lighter CUDA-core variant.
+inline int attn_ctas_per_sm(int impl) { return impl == 1 ? 4 : 1; }
 // Floats per partial record for head_dim D.
 __host__ __device__ inline int64_t partial_floats(int D) { return 16 + 8 * (int64_t)D; }
 

@@ -736,12 +736,186 @@ cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// CUDA-core variant (attn_impl = KRILL_ATTN_CUDA_CORE), kept as the
+// measured alternative to the tensor-core path. Same planner, partial records
+// and combine kernel; reads the pages straight from global memory (no staging).
+// One warp per kv head of an item; lane l owns head-dim slice
+// [l*EPD, (l+1)*EPD). Tokens go in batches of TB = 32/GQ: each lane forms
+// partial q.k dot products for TB tokens x GQ query heads over its slice, a
+// 31-shuffle reduce-scatter leaves lane L with the full score of
+// (token L / GQ, head L % GQ), the scores are broadcast back, and every lane
+// accumulates p.v for its slice with FMAs. Dequantization is the reference's
+// (two fp16 roundings), as on the tensor-core path.
+template <int D, int NG, int GQ>
+__global__ void __launch_bounds__(256) attn_cc_kernel(AttnParams p) {
+  using SG = SubGeom<D, NG>;
+  constexpr int T = SG::T, SPB = SG::SPB, EPD = D / 32, G = D / NG;
+  constexpr int TB = 32 / GQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int it0 = p.cta_off[blockIdx.x], it1 = p.cta_off[blockIdx.x + 1];
+  const int Hkv = p.Hkv;
+  const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
+  const int d0 = lane * EPD;
+  const int grp = d0 / G;
+  for (int it = it0; it < it1; ++it) {
+    const AttnItem item = p.items[it];
+    const AttnUnit un = p.units[item.unit];
+    const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
+    for (int h = item.h0 + warp; h < item.h0 + p.hg; h += 8) {
+      const int64_t qrow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * GQ) * D;
+      float qv[GQ][EPD];
+#pragma unroll
+      for (int hq = 0; hq < GQ; ++hq)
+#pragma unroll
+        for (int e = 0; e < EPD; ++e) qv[hq][e] = load_in(p.q, qrow + hq * D + d0 + e, p.q_dtype);
+      float o[GQ][EPD], m[GQ], l[GQ];
+#pragma unroll
+      for (int hq = 0; hq < GQ; ++hq) {
+        m[hq] = -INFINITY;
+        l[hq] = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPD; ++e) o[hq][e] = 0.f;
+      }
+      const uint8_t* head_base = p.pool + ((int64_t)un.layer * Hkv + h) * p.page_bytes;
+      for (int j = item.sb_begin; j < item.sb_end; ++j) {
+        int bi = j / SPB;
+        if (p.ring > 0) bi %= p.ring;
+        const uint8_t* sb = head_base + (int64_t)__ldg(bt + bi) * blk_stride + (int64_t)(j % SPB) * SG::SB;
+        const int pos0 = j * T;
+        for (int t0 = 0; t0 < T; t0 += TB) {
+          // ---- partial q.k over this lane's slice ----
+          float part[32];
+#pragma unroll
+          for (int tt = 0; tt < TB; ++tt) {
+            const int t = t0 + tt;
+            const __half s = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sb + SG::meta(0, grp, t)));
+            const __half z = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sb + SG::meta(1, grp, t)));
+            const uint8_t* kr = sb + sb_kcode(D, t, d0);
+            float kf[EPD];
+#pragma unroll
+            for (int e = 0; e < EPD; ++e)
+              kf[e] = __half2float(__hadd_rn(__hmul_rn(__ushort2half_rn(kr[e]), s), z));
+#pragma unroll
+            for (int hq = 0; hq < GQ; ++hq) {
+              float a = 0.f;
+#pragma unroll
+              for (int e = 0; e < EPD; ++e) a = fmaf(qv[hq][e], kf[e], a);
+              part[tt * GQ + hq] = a;
+            }
+          }
+          // ---- reduce-scatter: lane L ends with the sum of part[L] ----
+#pragma unroll
+          for (int off = 16, n = 32; off >= 1; off >>= 1, n >>= 1) {
+            const bool up = lane & off;
+#pragma unroll
+            for (int i = 0; i < n / 2; ++i) {
+              const float send = up ? part[i] : part[i + n / 2];
+              const float keep = up ? part[i + n / 2] : part[i];
+              part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+          }
+          const int my_t = pos0 + t0 + lane / GQ;
+          float sc = part[0] * p.scale_log2;
+          if (my_t < un.t_lo || my_t >= un.t_hi) sc = -INFINITY;
+          // ---- online softmax per head (lanes with the same lane % GQ) ----
+          float mx = sc;
+#pragma unroll
+          for (int off = GQ; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          float pv[32];
+          float alpha[GQ];
+#pragma unroll
+          for (int hq = 0; hq < GQ; ++hq) {
+            const float mb = __shfl_sync(0xffffffffu, mx, hq);
+            const float mn = fmaxf(m[hq], mb);
+            const float base = (mn == -INFINITY) ? 0.f : mn;
+            alpha[hq] = exp2f(m[hq] - base);
+            m[hq] = mn;
+          }
+          const float my_base = (m[lane % GQ] == -INFINITY) ? 0.f : m[lane % GQ];
+          const float my_p = exp2f(sc - my_base);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pv[i] = __shfl_sync(0xffffffffu, my_p, i);
+#pragma unroll
+          for (int hq = 0; hq < GQ; ++hq) {
+            float ls = 0.f;
+#pragma unroll
+            for (int tt = 0; tt < TB; ++tt) ls += pv[tt * GQ + hq];
+            l[hq] = l[hq] * alpha[hq] + ls;
+#pragma unroll
+            for (int e = 0; e < EPD; ++e) o[hq][e] *= alpha[hq];
+          }
+          // ---- p.v over this lane's slice ----
+#pragma unroll
+          for (int tt = 0; tt < TB; ++tt) {
+            const int t = t0 + tt;
+            const int pt = pos0 + t;
+            const bool valid = pt >= un.t_lo && pt < un.t_hi;
+            const __half s = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sb + SG::meta(2, grp, t)));
+            const __half z = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sb + SG::meta(3, grp, t)));
+#pragma unroll
+            for (int e = 0; e < EPD; ++e) {
+              const uint8_t c = sb[sb_vcode(D, t, d0 + e)];
+              const float vf = valid ? __half2float(__hadd_rn(__hmul_rn(__ushort2half_rn(c), s), z)) : 0.f;
+#pragma unroll
+              for (int hq = 0; hq < GQ; ++hq) o[hq][e] = fmaf(pv[tt * GQ + hq], vf, o[hq][e]);
+            }
+          }
+        }
+      }
+      // ---- finish: output, or a partial record of a split unit ----
+      if (un.n_split == 1) {
+#pragma unroll
+        for (int hq = 0; hq < GQ; ++hq) {
+          const float inv = 1.f / l[hq];
+#pragma unroll
+          for (int e = 0; e < EPD; ++e) store_out(p.out, p.out_dtype, qrow + hq * D + d0 + e, o[hq][e] * inv);
+        }
+      } else {
+        const int64_t rec = ((int64_t)un.first_split + item.idx) * Hkv + h;
+        float* part = p.partials + rec * partial_floats(D);
+#pragma unroll
+        for (int hq = 0; hq < GQ; ++hq) {
+#pragma unroll
+          for (int e = 0; e < EPD; ++e) part[16 + hq * D + d0 + e] = o[hq][e];
+          if (lane == 0) {
+            part[hq] = m[hq];
+            part[8 + hq] = l[hq];
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int D, int NG>
+cudaError_t launch_cc(const AttnParams& p, int grid, cudaStream_t stream) {
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (p.g) {
+    case 1: attn_cc_kernel<D, NG, 1><<<grid, 256, 0, stream>>>(p); e = cudaGetLastError(); break;
+    case 2: attn_cc_kernel<D, NG, 2><<<grid, 256, 0, stream>>>(p); e = cudaGetLastError(); break;
+    case 4: attn_cc_kernel<D, NG, 4><<<grid, 256, 0, stream>>>(p); e = cudaGetLastError(); break;
+    case 8: attn_cc_kernel<D, NG, 8><<<grid, 256, 0, stream>>>(p); e = cudaGetLastError(); break;
+    default: break;
+  }
+  if (e != cudaSuccess || p.n_split_units == 0) return e;
+  attn_combine_kernel<D><<<p.n_split_units * p.Hkv, 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
 }  // namespace
 
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
-  (void)impl;
+  if (impl == 1) {  // KRILL_ATTN_CUDA_CORE
+    if (g.D == 64 && g.NG == 1) return launch_cc<64, 1>(p, grid, stream);
+    if (g.D == 128 && g.NG == 2) return launch_cc<128, 2>(p, grid, stream);
+    if (g.D == 128 && g.NG == 1) return launch_cc<128, 1>(p, grid, stream);
+    if (g.D == 256 && g.NG == 4) return launch_cc<256, 4>(p, grid, stream);
+    if (g.D == 256 && g.NG == 1) return launch_cc<256, 1>(p, grid, stream);
+    return cudaErrorInvalidValue;
+  }
   if (g.D == 64 && g.NG == 1) return launch_tc_r<64, 1, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 2) return launch_tc_r<128, 2, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 1) return launch_tc_r<128, 1, 8>(p, grid, stream);

@@ -169,3 +169,19 @@ def test_neighbor_content_isolation_bit_exact():
         outs.append(out[:, 0].clone())
         pool.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,scale", [
+    (64, 64, 32, 8, F16, 1 / 8),
+    (128, 64, 32, 8, BF16, 1 / math.sqrt(128)),
+    (128, 64, 32, 4, BF16, 1 / math.sqrt(128)),
+    (256, 64, 8, 4, F16, 1.0),
+    (64, 64, 8, 8, F16, 1 / 8),
+])
+def test_attention_cuda_core_variant(D, G, hq, hkv, dtype, scale):
+    """The CUDA-core variant (attn_impl = CUDA_CORE) meets the same tolerance."""
+    run_case(D, G, hq, hkv, dtype, [1, 63, 65, 300, 1100], scale, impl=kb.ATTN_CUDA_CORE, split=512)
+
+
+def test_attention_cuda_core_windowed():
+    run_case(256, 64, 8, 4, F16, [10, 300, 700], 1.0, window=128, impl=kb.ATTN_CUDA_CORE, steps=2)
