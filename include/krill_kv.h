@@ -96,6 +96,13 @@ typedef struct {
                              other sequences' contents). > 0 = fixed pieces and
                              whole-layer head groups: a sequence's output is
                              then bit-identical whatever else is batched.      */
+  int32_t cascade_min_tokens; /* shared-prefix (cascade) attention: sequences of
+                             one call whose block tables begin with the same
+                             blocks (forks of one prefix entry) attend at least
+                             this many common tokens together, read and
+                             dequantized once. 0 -> 256; < 0 -> off. Applies
+                             to full-history pools with the tensor-core
+                             implementation and split_tokens = 0.           */
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
 } krill_pool_cfg;
 
@@ -134,6 +141,12 @@ krill_status_t krill_pool_kernel_times(krill_pool_t pool, double* attn_ms, int32
  * sub-blocks, kv heads per work item, number of items and of persistent CTAs. */
 krill_status_t krill_pool_last_plan(krill_pool_t pool, int32_t* piece_subblocks,
                                     int32_t* heads_per_item, int64_t* items, int32_t* ctas);
+/* Introspection (no reference counterpart): the shared-prefix part of the last
+ * krill_decode_attention — number of sequence groups attended together, their
+ * cascade work items, partial-record slots per member and persistent CTAs
+ * (0 everywhere when no group qualified). */
+krill_status_t krill_pool_last_cascade(krill_pool_t pool, int32_t* groups, int64_t* shared_items,
+                                       int32_t* prefix_slots, int32_t* ctas);
 
 /* ---- sequences (one request's per-layer caches) -------------------------- */
 /* New empty sequence: every layer at length 0 (QuantizedKVCache.init). */

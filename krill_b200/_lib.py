@@ -49,6 +49,7 @@ class PoolCfg(C.Structure):
         ("quant_variant", C.c_int32),
         ("attn_impl", C.c_int32),
         ("split_tokens", C.c_int32),
+        ("cascade_min_tokens", C.c_int32),
         ("num_blocks", C.c_int64),
     ]
 
@@ -78,6 +79,7 @@ _SIGS = {
     "krill_pool_set_profiling": (i32, [vp, i32]),
     "krill_pool_kernel_times": (i32, [vp, C.POINTER(C.c_double), P_i32, C.POINTER(C.c_double), P_i32]),
     "krill_pool_last_plan": (i32, [vp, P_i32, P_i32, P_i64, P_i32]),
+    "krill_pool_last_cascade": (i32, [vp, P_i32, P_i64, P_i32, P_i32]),
     "krill_seq_create": (i32, [vp, P_u64]),
     "krill_seq_release": (i32, [vp, u64]),
     "krill_seq_reset": (i32, [vp, u64]),

@@ -64,9 +64,10 @@ class KVPool:
     def __init__(self, num_layers: int, num_kv_heads: int, num_q_heads: int, head_dim: int,
                  num_blocks: int, group_size: int = 64, window: int = 0, max_append: int = 0,
                  quant_variant: int = L.QUANT_F32, attn_impl: int = L.ATTN_TENSOR_CORE,
-                 split_tokens: int = 0, device: int = 0):
+                 split_tokens: int = 0, cascade_min_tokens: int = 0, device: int = 0):
         cfg = L.PoolCfg(num_layers, num_kv_heads, num_q_heads, head_dim, group_size, window,
-                        max_append, quant_variant, attn_impl, split_tokens, num_blocks)
+                        max_append, quant_variant, attn_impl, split_tokens, cascade_min_tokens,
+                        num_blocks)
         h = C.c_void_p()
         check(L.lib.krill_pool_create(C.byref(cfg), device, C.byref(h)))
         self.handle = h
@@ -126,6 +127,13 @@ class KVPool:
         c, hg, n, g = C.c_int32(), C.c_int32(), C.c_int64(), C.c_int32()
         check(L.lib.krill_pool_last_plan(self.handle, C.byref(c), C.byref(hg), C.byref(n), C.byref(g)))
         return c.value, hg.value, n.value, g.value
+
+    def last_cascade(self):
+        """(sequence groups attended together, cascade items, prefix record
+        slots per member, cascade CTAs) of the last decode-attention launch."""
+        g, n, s, c = C.c_int32(), C.c_int64(), C.c_int32(), C.c_int32()
+        check(L.lib.krill_pool_last_cascade(self.handle, C.byref(g), C.byref(n), C.byref(s), C.byref(c)))
+        return g.value, n.value, s.value, c.value
 
     def create_sequence(self) -> "Sequence_":
         h = C.c_uint64()

@@ -98,8 +98,15 @@ struct Plan {
   std::vector<uint8_t> dry;
   std::vector<int64_t> nsb;
   std::vector<int32_t> split_units;
+  // cascade (shared-prefix) planning
+  std::vector<int32_t> gorder, gstart, gmembers, seq_sh;
+  std::vector<int64_t> gshared;
+  std::vector<ShItem> sh_items;
+  std::vector<int32_t> sh_members, sh_cta;
   int last_C = 0, last_HG = 0, last_grid = 0;
   int64_t last_items = 0;
+  int last_groups = 0, last_pslots = 0, last_sh_grid = 0;
+  int64_t last_sh_items = 0;
 };
 
 }  // namespace
@@ -423,6 +430,67 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     TRY(seq_get(p, seqs[i], &pl.sv[i]));
     bt_stride = std::max<int64_t>(bt_stride, (int64_t)pl.sv[i]->blocks.size());
   }
+  // ---- shared-prefix groups (cascade) ----
+  // Sequences whose block tables begin with the same physical blocks (forks of
+  // one prefix-cache entry) attend that common prefix through cascade items
+  // that read and dequantize it once for all of them; each member's decode
+  // items then start where the shared part ends. Only on full-history pools
+  // with the tensor-core implementation and adaptive splitting: a fixed
+  // split_tokens promises results that do not depend on the rest of the batch.
+  pl.gstart.clear();
+  pl.gmembers.clear();
+  pl.gshared.clear();
+  pl.seq_sh.assign((size_t)n_seqs, 0);
+  const int64_t min_tok = p->cfg.cascade_min_tokens == 0 ? 256 : p->cfg.cascade_min_tokens;
+  if (!p->windowed() && p->cfg.attn_impl == KRILL_ATTN_TENSOR_CORE && p->cfg.split_tokens == 0 &&
+      p->cfg.cascade_min_tokens >= 0 && n_seqs >= 2) {
+    const size_t min_blocks = (size_t)std::max<int64_t>(1, (min_tok + kBlockTokens - 1) / kBlockTokens);
+    pl.gorder.clear();
+    for (int si = 0; si < n_seqs; ++si)
+      if (pl.sv[si]->blocks.size() >= min_blocks) pl.gorder.push_back(si);
+    std::sort(pl.gorder.begin(), pl.gorder.end(), [&](int32_t a, int32_t b) {
+      const auto& x = pl.sv[a]->blocks;
+      const auto& y = pl.sv[b]->blocks;
+      return std::lexicographical_compare(x.begin(), x.end(), y.begin(), y.end()) ||
+             (x == y && a < b);
+    });
+    auto lcp = [&](int32_t a, int32_t b) {
+      const auto& x = pl.sv[a]->blocks;
+      const auto& y = pl.sv[b]->blocks;
+      const size_t n = std::min(x.size(), y.size());
+      size_t i = 0;
+      while (i < n && x[i] == y[i]) ++i;
+      return i;
+    };
+    for (size_t i = 0; i < pl.gorder.size();) {
+      size_t j = i + 1, common = SIZE_MAX;
+      while (j < pl.gorder.size()) {
+        const size_t c = lcp(pl.gorder[j - 1], pl.gorder[j]);
+        if (c < min_blocks) break;
+        common = std::min(common, c);
+        ++j;
+      }
+      if (j - i >= 2) {
+        // whole common blocks, strictly below every member's length at every
+        // layer of the call (each member keeps at least one own token)
+        int64_t S = (int64_t)common * kBlockTokens;
+        for (size_t k = i; k < j; ++k)
+          for (int li = 0; li < lc; ++li) S = std::min<int64_t>(S, pl.sv[pl.gorder[k]]->len[lb + li] - 1);
+        S -= S % g.subt;
+        if (S >= min_tok) {
+          pl.gstart.push_back((int32_t)pl.gmembers.size());
+          pl.gshared.push_back(S);
+          for (size_t k = i; k < j; ++k) {
+            pl.gmembers.push_back(pl.gorder[k]);
+            pl.seq_sh[pl.gorder[k]] = (int32_t)(S / g.subt);
+          }
+        }
+      }
+      i = j;
+    }
+  }
+  const int n_groups = (int)pl.gshared.size();
+  pl.gstart.push_back((int32_t)pl.gmembers.size());
   // ---- units (layer, seq) ----
   const int64_t n_units = (int64_t)lc * n_seqs;
   pl.units.resize((size_t)n_units);
@@ -444,7 +512,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       u.t_lo = (int32_t)t_lo;
       u.t_hi = (int32_t)t_hi;
       u.pad = 0;
-      pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - t_lo / g.subt;
+      pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
       total_sb += pl.nsb[ui];
     }
   }
@@ -466,6 +534,62 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     C = 8;
     while (C < 128 && (int64_t)(2 * C) * HG <= quarter) C *= 2;
   }
+  // ---- cascade items: (group, layer, row block, kv head) pairs cut into
+  // fragments. The pairs' sub-blocks are laid end to end and split into
+  // equal contiguous ranges, one per CTA; the fragment index within a pair is
+  // its partial-record slot. Pairs that read the same blocks are adjacent, so
+  // the CTAs working on them run side by side and share L2.
+  pl.sh_items.clear();
+  pl.sh_members.clear();
+  pl.sh_cta.clear();
+  int n_pslots = 0, sh_grid = 0;
+  if (n_groups > 0) {
+    const int mem_cap = std::max(1, sh_rows(g.D) / g.g);
+    int64_t W = 0;
+    for (int gi = 0; gi < n_groups; ++gi) {
+      const int n_mem = pl.gstart[gi + 1] - pl.gstart[gi];
+      W += (int64_t)lc * ((n_mem + mem_cap - 1) / mem_cap) * g.Hkv * (pl.gshared[gi] / g.subt);
+    }
+    constexpr int64_t kMinFragment = 8;  // sub-blocks
+    const int64_t grid_sh =
+        std::max<int64_t>(1, std::min<int64_t>(p->num_sms, (W + kMinFragment - 1) / kMinFragment));
+    const int64_t per = (W + grid_sh - 1) / grid_sh;
+    sh_grid = (int)((W + per - 1) / per);
+    pl.sh_cta.assign((size_t)sh_grid + 1, 0);
+    int64_t pos = 0;
+    for (int gi = 0; gi < n_groups; ++gi) {
+      const int32_t* mem = pl.gmembers.data() + pl.gstart[gi];
+      const int n_mem = pl.gstart[gi + 1] - pl.gstart[gi];
+      const int64_t n_sb = pl.gshared[gi] / g.subt;
+      for (int li = 0; li < lc; ++li)
+        for (int mb = 0; mb < n_mem; mb += mem_cap) {
+          const int nm = std::min(mem_cap, n_mem - mb);
+          const int32_t mem_off = (int32_t)pl.sh_members.size();
+          for (int k = 0; k < nm; ++k) pl.sh_members.push_back((int32_t)((int64_t)li * n_seqs + mem[mb + k]));
+          for (int h = 0; h < g.Hkv; ++h) {
+            const int64_t a = pos, b = pos + n_sb;
+            const int64_t first = a / per, last = (b - 1) / per;
+            for (int64_t c = first; c <= last; ++c) {
+              ShItem it{};
+              it.layer = lb + li;
+              it.leader = mem[0];
+              it.sb_begin = (int32_t)(std::max(a, c * per) - a);
+              it.sb_end = (int32_t)(std::min(b, (c + 1) * per) - a);
+              it.mem_off = mem_off;
+              it.n_rows = (int16_t)(nm * g.g);
+              it.h = (int16_t)h;
+              it.slot = (int16_t)(c - first);
+              it.n_frag = (int16_t)(last - first + 1);
+              pl.sh_items.push_back(it);
+              pl.sh_cta[(size_t)c + 1] += 1;
+            }
+            n_pslots = std::max<int>(n_pslots, (int)(last - first + 1));
+            pos = b;
+          }
+        }
+    }
+    for (int c = 0; c < sh_grid; ++c) pl.sh_cta[(size_t)c + 1] += pl.sh_cta[(size_t)c];
+  }
   // ---- items ----
   pl.items.clear();
   int64_t split_count = 0;
@@ -475,17 +599,21 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     const int64_t n_sb = pl.nsb[ui];
     const int64_t n_it = (n_sb + C - 1) / C;
     const int64_t base = n_sb / n_it, extra = n_sb % n_it;
-    u.n_split = (int32_t)n_it;
+    const int sh_sb = pl.seq_sh[u.si];
+    // cascaded units: records [0, n_pslots) come from the cascade items
+    const int64_t off = sh_sb > 0 ? n_pslots : 0;
+    u.n_split = (int32_t)(off + n_it);
     u.first_split = (int32_t)split_count;
-    if (n_it > 1) {
-      split_count += n_it;
+    if (u.n_split > 1 || sh_sb > 0) {
+      split_count += u.n_split;
       pl.split_units.push_back((int32_t)ui);
     }
-    int64_t b = u.t_lo / g.subt;
+    int64_t b = std::max<int64_t>(u.t_lo / g.subt, sh_sb);
     for (int64_t i = 0; i < n_it; ++i) {
       const int64_t sz = base + (i < extra ? 1 : 0);
       for (int h0 = 0; h0 < g.Hkv; h0 += HG)
-        pl.items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int16_t)i, (int16_t)h0});
+        pl.items.push_back(
+            AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int16_t)(off + i), (int16_t)h0});
       b += sz;
     }
   }
@@ -531,7 +659,11 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   const size_t off_bytes = align16((size_t)(grid + 1) * sizeof(int32_t));
   const size_t bt_bytes = align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
   const size_t su_bytes = align16((pl.split_units.size() + 1) * sizeof(int32_t));
-  const size_t total = units_bytes + items_bytes + off_bytes + bt_bytes + su_bytes;
+  const size_t shi_bytes = align16(pl.sh_items.size() * sizeof(ShItem));
+  const size_t shc_bytes = align16(pl.sh_cta.size() * sizeof(int32_t));
+  const size_t shm_bytes = align16(pl.sh_members.size() * sizeof(int32_t));
+  const size_t sh_off = units_bytes + items_bytes + off_bytes + bt_bytes + su_bytes;
+  const size_t total = sh_off + shi_bytes + shc_bytes + shm_bytes;
   StageSlot* slot = nullptr;
   uint8_t* h;
   if (p->host_only) {
@@ -558,6 +690,16 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   int32_t* su = reinterpret_cast<int32_t*>(h + units_bytes + items_bytes + off_bytes + bt_bytes);
   if (!pl.split_units.empty())
     std::memcpy(su, pl.split_units.data(), pl.split_units.size() * sizeof(int32_t));
+  if (sh_grid > 0) {
+    std::memcpy(h + sh_off, pl.sh_items.data(), pl.sh_items.size() * sizeof(ShItem));
+    std::memcpy(h + sh_off + shi_bytes, pl.sh_cta.data(), pl.sh_cta.size() * sizeof(int32_t));
+    std::memcpy(h + sh_off + shi_bytes + shc_bytes, pl.sh_members.data(),
+                pl.sh_members.size() * sizeof(int32_t));
+  }
+  pl.last_groups = n_groups;
+  pl.last_pslots = n_pslots;
+  pl.last_sh_grid = sh_grid;
+  pl.last_sh_items = (int64_t)pl.sh_items.size();
   pl.last_C = C;
   pl.last_HG = HG;
   pl.last_items = n_items;
@@ -588,6 +730,13 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.partials = p->d_partials;
   ap.err = p->d_err;
+  if (sh_grid > 0) {
+    ap.sh_items = reinterpret_cast<const ShItem*>(slot->d + sh_off);
+    ap.sh_cta_off = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes);
+    ap.sh_members = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes + shc_bytes);
+    ap.sh_grid = sh_grid;
+    ap.n_pslots = n_pslots;
+  }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
   TRY(stage_release(slot, stream));
   return KRILL_OK;
@@ -818,6 +967,17 @@ krill_status_t krill_pool_last_plan(krill_pool_t p, int32_t* piece_subblocks, in
   if (heads_per_item) *heads_per_item = p->plan.last_HG;
   if (items) *items = p->plan.last_items;
   if (ctas) *ctas = p->plan.last_grid;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_last_cascade(krill_pool_t p, int32_t* groups, int64_t* shared_items,
+                                       int32_t* prefix_slots, int32_t* ctas) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (groups) *groups = p->plan.last_groups;
+  if (shared_items) *shared_items = p->plan.last_sh_items;
+  if (prefix_slots) *prefix_slots = p->plan.last_pslots;
+  if (ctas) *ctas = p->plan.last_sh_grid;
   return KRILL_OK;
 }
 

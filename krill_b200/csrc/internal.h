@@ -60,6 +60,30 @@ struct AttnItem {
   int16_t h0;        // first kv head of the item's head group
 };
 
+// Cascade (shared-prefix) attention. Sequences of one call whose block tables
+// begin with the same physical blocks attend that common prefix together: a
+// work item is a fragment [sb_begin, sb_end) of the prefix's sub-blocks for
+// one (layer, kv head) and up to sh_rows(D) query rows (member sequences x
+// GQA group), read and dequantized once for all of them. Its result is the
+// partial record `slot` of every member unit; the members' own suffixes go
+// through the decode kernel as later pieces and the combine kernel merges.
+struct ShItem {
+  int32_t layer;     // absolute layer in the pool
+  int32_t leader;    // block-table row holding the shared blocks
+  int32_t sb_begin;  // sub-block range of the shared prefix
+  int32_t sb_end;
+  int32_t mem_off;   // first member unit id in the members array
+  int16_t n_rows;    // members * g, at most sh_rows(D)
+  int16_t h;         // kv head
+  int16_t slot;      // partial-record slot of this fragment
+  int16_t n_frag;    // fragments of this (members, layer, head)
+  int32_t pad;
+};
+
+// Query rows of one cascade item: 8 consumer warps x 32 rows (16 at D = 256,
+// whose fp32 output rows need twice the registers).
+__host__ __device__ constexpr int sh_rows(int D) { return D >= 256 ? 128 : 256; }
+
 struct AttnParams {
   const uint8_t* pool;
   int64_t page_bytes, sb_bytes;
@@ -79,6 +103,12 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   float* partials;   // [splits * Hkv][16 + 8*D]
   int* err;
+  // cascade items (sh_grid = 0: none)
+  const ShItem* sh_items;
+  const int32_t* sh_cta_off;  // [sh_grid + 1]
+  const int32_t* sh_members;  // unit ids
+  int sh_grid;
+  int n_pslots;               // prefix record slots per cascaded unit
 };
 
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
@@ -89,9 +119,11 @@ cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const i
 cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
                            int64_t S, const ScatterIn& in, cudaStream_t stream);
 // grid = number of persistent CTAs (cta_off has grid + 1 entries). Launches
-// the attention kernel and, when some unit is split, the combine kernel.
+// the cascade kernel when p.sh_grid > 0, then the decode kernel and, when
+// some unit is split, the combine kernel.
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
+cudaError_t launch_shared(const Geom& g, const AttnParams& p, cudaStream_t stream);
 // Launch description produced for the allocation-free decode attention:
 // byte offsets of the metadata and partial records inside the caller's
 // scratch, plus the launch parameters (pointers into the scratch unset).

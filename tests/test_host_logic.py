@@ -302,3 +302,86 @@ def test_planner_fixed_split_is_batch_invariant():
     append(p, [a], 3000)
     append(p, [b], 100)
     assert attend(p, [a])[:2] == attend(p, [a, b])[:2] == (8, 8)
+
+
+def _forked_batch(p, prefix, n_req, suffix):
+    """n_req forks of one stored prefix, each with its own suffix appended
+    (the engine's partial-hit path: restore, then prefill the suffix)."""
+    pc = kb.PrefixCache(p)
+    base = p.create_sequence()
+    append(p, [base], prefix)
+    toks = list(range(prefix))
+    pc.store_quantized(toks, "m", base)
+    hit = pc.lookup_quantized(toks, "m")
+    forks = [hit.fork(prefix) for _ in range(n_req)]
+    hit.release()
+    for f in forks:
+        append(p, [f], suffix)
+    return pc, base, forks
+
+
+def test_cascade_groups_forks_of_one_prefix():
+    p = pool(layers=2, blocks=200)
+    pc, base, forks = _forked_batch(p, 1024, 6, 40)
+    attend(p, forks)
+    groups, items, slots, ctas = p.last_cascade()
+    assert groups == 1 and slots >= 1 and items >= 2 * 8 and ctas >= 1
+    # an independent sequence in the batch joins no group
+    lone = p.create_sequence()
+    append(p, [lone], 1064)
+    attend(p, forks + [lone])
+    assert p.last_cascade()[0] == 1
+    attend(p, [forks[0], lone])
+    assert p.last_cascade() == (0, 0, 0, 0)
+    pc.close()
+
+
+def test_cascade_respects_switches_and_short_prefixes():
+    # off, fixed split (batch-invariant results promised), windowed pools,
+    # CUDA-core implementation, and a shared part below the threshold
+    for kw in [dict(cascade_min_tokens=-1), dict(split_tokens=512), dict(window=2048, max_append=1024),
+               dict(attn_impl=L.ATTN_CUDA_CORE)]:
+        p = pool(layers=2, blocks=200, **kw)
+        pc, _, forks = _forked_batch(p, 1024, 4, 10)
+        attend(p, forks)
+        assert p.last_cascade()[0] == 0, kw
+        pc.close()
+    # forks share only the prefix's full blocks: the first append into the
+    # partial last block copies it (copy-on-write)
+    p = pool(layers=2, blocks=200)
+    pc, _, forks = _forked_batch(p, 200, 4, 10)
+    attend(p, forks)
+    assert p.last_cascade()[0] == 0
+    pc.close()
+    p = pool(layers=2, blocks=200, cascade_min_tokens=512)
+    pc, _, forks = _forked_batch(p, 300, 4, 10)  # 256 shared tokens < 512
+    attend(p, forks)
+    assert p.last_cascade()[0] == 0
+    pc.close()
+    p = pool(layers=2, blocks=200)
+    pc, _, forks = _forked_batch(p, 300, 4, 10)
+    attend(p, forks)
+    assert p.last_cascade()[0] == 1
+    pc.close()
+
+
+def test_cascade_shared_part_stays_below_every_length():
+    """A full hit is forked at count - 1 (InferenceEngine.swift:1401-1417):
+    the shared blocks then hold tokens one member never saw; the shared part
+    must end before the shortest member's last token."""
+    p = pool(layers=2, blocks=200, cascade_min_tokens=64)
+    pc = kb.PrefixCache(p)
+    base = p.create_sequence()
+    append(p, [base], 300)
+    toks = list(range(300))
+    pc.store_quantized(toks, "m", base)
+    hit = pc.lookup_quantized(toks, "m")
+    a, b = hit.fork(300), hit.fork(299)
+    hit.release()
+    attend(p, [a, b])
+    assert p.last_cascade()[0] == 1
+    # the two forks share 2 blocks (512 tokens) but b holds only 299 tokens:
+    # shared part = 256 (largest multiple of 64 below 298)
+    attend(p, [a, b, base])
+    assert p.last_cascade()[0] == 1
+    pc.close()
