@@ -68,10 +68,14 @@ enum {
  * quotient in float32. F16 keeps them in the input dtype. */
 enum { KRILL_QUANT_F32 = 0, KRILL_QUANT_INPUT_DTYPE = 1 };
 
-/* Decode-attention implementation: tensor-core (mma.sync m16n8k16 on the
- * dequantized tiles) or CUDA-core FMA. Both give the same results within the
- * attention tolerance; the choice is a performance knob. */
-enum { KRILL_ATTN_TENSOR_CORE = 0, KRILL_ATTN_CUDA_CORE = 1 };
+/* Decode-attention implementation, a performance knob (all give the same
+ * results within the attention tolerance):
+ *   TENSOR_CORE       per-sequence decode on mma.sync m16n8k16 over the
+ *                     dequantized tiles; the shared-prefix (cascade) part on
+ *                     tcgen05 with tensor-memory accumulators (head_dim <= 128)
+ *   CUDA_CORE         per-sequence decode on FMA, no cascade
+ *   TENSOR_CORE_SYNC  as TENSOR_CORE with the cascade part on mma.sync */
+enum { KRILL_ATTN_TENSOR_CORE = 0, KRILL_ATTN_CUDA_CORE = 1, KRILL_ATTN_TENSOR_CORE_SYNC = 2 };
 
 typedef struct krill_pool_s* krill_pool_t;
 typedef uint64_t krill_seq_t;               /* generation << 32 | slot */
@@ -101,7 +105,7 @@ typedef struct {
                              blocks (forks of one prefix entry) attend at least
                              this many common tokens together, read and
                              dequantized once. 0 -> 256; < 0 -> off. Applies
-                             to full-history pools with the tensor-core
+                             to full-history pools with a tensor-core
                              implementation and split_tokens = 0.           */
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
 } krill_pool_cfg;

@@ -435,14 +435,14 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   // one prefix-cache entry) attend that common prefix through cascade items
   // that read and dequantize it once for all of them; each member's decode
   // items then start where the shared part ends. Only on full-history pools
-  // with the tensor-core implementation and adaptive splitting: a fixed
+  // with a tensor-core implementation and adaptive splitting: a fixed
   // split_tokens promises results that do not depend on the rest of the batch.
   pl.gstart.clear();
   pl.gmembers.clear();
   pl.gshared.clear();
   pl.seq_sh.assign((size_t)n_seqs, 0);
   const int64_t min_tok = p->cfg.cascade_min_tokens == 0 ? 256 : p->cfg.cascade_min_tokens;
-  if (!p->windowed() && p->cfg.attn_impl == KRILL_ATTN_TENSOR_CORE && p->cfg.split_tokens == 0 &&
+  if (!p->windowed() && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE && p->cfg.split_tokens == 0 &&
       p->cfg.cascade_min_tokens >= 0 && n_seqs >= 2) {
     const size_t min_blocks = (size_t)std::max<int64_t>(1, (min_tok + kBlockTokens - 1) / kBlockTokens);
     pl.gorder.clear();
@@ -544,7 +544,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.sh_cta.clear();
   int n_pslots = 0, sh_grid = 0;
   if (n_groups > 0) {
-    const int mem_cap = std::max(1, sh_rows(g.D) / g.g);
+    const int mem_cap = std::max(1, shared_rows(g, p->cfg.attn_impl) / g.g);
     int64_t W = 0;
     for (int gi = 0; gi < n_groups; ++gi) {
       const int n_mem = pl.gstart[gi + 1] - pl.gstart[gi];
@@ -830,7 +830,8 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   if (cfg.max_append <= 0) cfg.max_append = 256;
   if (cfg.quant_variant != KRILL_QUANT_F32 && cfg.quant_variant != KRILL_QUANT_INPUT_DTYPE)
     return fail(KRILL_ERR_INVALID, "bad quant_variant");
-  if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE)
+  if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE &&
+      cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_SYNC)
     return fail(KRILL_ERR_INVALID, "bad attn_impl");
   if (cfg.split_tokens < 0 || cfg.split_tokens % 64 != 0)
     return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");

@@ -796,7 +796,8 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
                              cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
   if (p.sh_grid > 0) {  // shared-prefix fragments first: they fill partial records
-    const cudaError_t e = launch_shared(g, p, stream);
+    const cudaError_t e = shared_uses_umma(g, impl) ? launch_shared_umma(g, p, stream)
+                                                    : launch_shared(g, p, stream);
     if (e != cudaSuccess) return e;
   }
   if (impl == 1) {  // KRILL_ATTN_CUDA_CORE

@@ -1,0 +1,529 @@
+// kv_shared_umma.cu — cascade attention over a shared prefix on the
+// 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// Same work items and results as kv_shared.cu (forks of one prefix-cache
+// entry attend the common blocks once per (layer, kv head); see there for the
+// reference mapping), for head_dim 64 and 128. One CTA per SM, 12 warps:
+//   - warp 5 streams raw sub-blocks HBM -> shared memory (cp.async.bulk);
+//   - warps 6-11 dequantize each raw sub-block once (the reference's two fp16
+//     roundings) into f16 K [64 tok][D] and V [D][64 tok] tiles laid out as
+//     the tensor core's canonical K-major 128-byte-swizzled operands;
+//   - warp 4 owns the tensor memory and one of its lanes issues the MMAs:
+//       S_j  = Q · K_jᵀ      (M = 128 query rows, N = 64 tokens, K = D)
+//       O   += P_j · V_j     (M = 128, N = D, K = 64 tokens)
+//     with S double-buffered in tensor memory so the softmax of tile j
+//     overlaps S_{j+1}; each group of MMAs is committed to an mbarrier;
+//   - warps 0-3 (thread t = query row t = tensor-memory lane t) read S_j with
+//     tcgen05.ld, run the online softmax in the exp2 domain and write P_j as
+//     f16 into a swizzled shared tile. The running max is only raised when a
+//     row's max grows by more than 8 (log2 units); the rare O rescale is a
+//     tcgen05.ld / st round trip after the previous P·V has completed. At the
+//     end of an item they read O and write the fp32 partial records.
+// Every wait is bounded (10 s, then 20 us after the first timeout) and sets
+// the pool's error flag; the tensor memory is released on every path.
+#include <atomic>
+
+#include "kv_device.cuh"
+
+namespace krill {
+namespace {
+
+constexpr int kUmNF = 3;         // f16 K/V tile stages
+constexpr int kUmNR = 3;         // raw sub-block stages
+constexpr int kUmDeqWarps = 6;   // warps 6-11
+constexpr int kUmThreads = 384;  // 12 warps: 168 registers a thread at one CTA per SM
+constexpr uint32_t kUmCols = 256;  // tensor-memory columns: O [0, D), S buffers at 128 and 192
+constexpr uint32_t kUmS0 = 128;
+
+// ---- tensor-core primitives (PTX ISA 8.6+, sm_100a) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// generic-proxy shared-memory writes -> visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrives on the mbarrier once every MMA this thread issued so far completed
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's tensor-memory lane; the wait
+// sits in the same statement so no use of the registers can precede it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand in the canonical
+// 128-byte-swizzle layout: rows of 64 f16 (128 B), 8-row groups of 1024 B
+// stacked contiguously, 16-byte chunk c of row r stored at chunk c ^ (r & 7).
+// Advancing along K by 16 elements inside a swizzle atom adds 32 B to the
+// start address; the next 64-element atom starts rows * 128 B further.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
+  d |= (uint64_t)1 << 16;                            // leading byte offset (unused when swizzled)
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;                            // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                            // 128-byte swizzle
+  return d;
+}
+// Instruction descriptor: f16 A and B, f32 accumulator, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// Byte offset of 16-byte chunk c (along K) of row r in a K-major SW128 tile of
+// `rows` rows.
+__device__ __forceinline__ uint32_t sw128_off(int rows, int r, int c) {
+  return (uint32_t)((c >> 3) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+template <int D, int NG>
+struct UmSmem {
+  using SG = SubGeom<D, NG>;
+  static_assert(SG::T == 64, "one 64-token sub-block per tile");
+  static constexpr int Q_BYTES = 128 * D * 2;
+  static constexpr int P_BYTES = 128 * 64 * 2;
+  static constexpr int K_BYTES = 64 * D * 2;
+  static constexpr int V_BYTES = D * 64 * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int P_OFF = Q_OFF + Q_BYTES;  // 2 buffers
+  static constexpr int KV_OFF = P_OFF + 2 * P_BYTES;
+  static constexpr int KV_STAGE = K_BYTES + V_BYTES;
+  static constexpr int RAW_OFF = KV_OFF + kUmNF * KV_STAGE;
+  static constexpr int BAR_OFF = RAW_OFF + kUmNR * SG::SB;
+  // raw full/empty [NR], kv full/empty [NF], s full [2], p full [2], pv done [2], q full, fin
+  static constexpr int B_RF = 0, B_RE = kUmNR, B_KF = 2 * kUmNR, B_KE = 2 * kUmNR + kUmNF,
+                       B_SF = 2 * kUmNR + 2 * kUmNF, B_PF = B_SF + 2, B_PD = B_PF + 2,
+                       B_QF = B_PD + 2, B_FIN = B_QF + 1, NBAR = B_FIN + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem address, abort flag
+  static constexpr int TOTAL = MISC_OFF + 16 + 1024;   // + alignment slack
+  static_assert(SG::SB % 16 == 0 && KV_STAGE % 1024 == 0 && Q_BYTES % 1024 == 0, "alignment");
+};
+
+// One raw sub-block -> f16 K tile [64 tok][D] and V tile [D][64 tok] in the
+// SW128 K-major layout; values f16_rn(f16_rn(code * scale) + zero)
+// (QuantizedKVCache.swift:200-204). t0 = dequantizer thread index.
+template <int D, int NG>
+__device__ __forceinline__ void um_dequant(const uint8_t* __restrict__ raw, uint8_t* __restrict__ kt,
+                                           uint8_t* __restrict__ vt, int t0) {
+  using SG = SubGeom<D, NG>;
+  constexpr int G = SG::G;
+  constexpr int NDT = kUmDeqWarps * 32;
+  for (int i = t0; i < 64 * (D / 16); i += NDT) {
+    const int t = i / (D / 16), c = i % (D / 16);
+    const int pc = D >= 128 ? (c ^ ((t & 1) << 2)) : c;
+    const uint4 w = *reinterpret_cast<const uint4*>(raw + t * D + pc * 16);
+    const int gi = (16 * c) / G;
+    const uint32_t s = *reinterpret_cast<const uint16_t*>(raw + SG::meta(0, gi, t));
+    const uint32_t z = *reinterpret_cast<const uint16_t*>(raw + SG::meta(1, gi, t));
+    const uint32_t s2 = s | (s << 16), z2 = z | (z << 16);
+    uint4 lo, hi;
+    lo.x = deq2(w.x, 0x4140u, s2, z2);
+    lo.y = deq2(w.x, 0x4342u, s2, z2);
+    lo.z = deq2(w.y, 0x4140u, s2, z2);
+    lo.w = deq2(w.y, 0x4342u, s2, z2);
+    hi.x = deq2(w.z, 0x4140u, s2, z2);
+    hi.y = deq2(w.z, 0x4342u, s2, z2);
+    hi.z = deq2(w.w, 0x4140u, s2, z2);
+    hi.w = deq2(w.w, 0x4342u, s2, z2);
+    *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c)) = lo;
+    *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c + 1)) = hi;
+  }
+  for (int i = t0; i < D * 4; i += NDT) {
+    const int d = i >> 2, c = i & 3;
+    const uint4 w = *reinterpret_cast<const uint4*>(raw + SG::VOFF + d * 64 + c * 16);
+    const int gi = d / G;
+    const uint4 sa = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c));
+    const uint4 sb = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c + 8));
+    const uint4 za = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c));
+    const uint4 zb = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c + 8));
+    uint4 lo, hi;
+    lo.x = deq2(w.x, 0x4140u, sa.x, za.x);
+    lo.y = deq2(w.x, 0x4342u, sa.y, za.y);
+    lo.z = deq2(w.y, 0x4140u, sa.z, za.z);
+    lo.w = deq2(w.y, 0x4342u, sa.w, za.w);
+    hi.x = deq2(w.z, 0x4140u, sb.x, zb.x);
+    hi.y = deq2(w.z, 0x4342u, sb.y, zb.y);
+    hi.z = deq2(w.w, 0x4140u, sb.z, zb.z);
+    hi.w = deq2(w.w, 0x4342u, sb.w, zb.w);
+    *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c)) = lo;
+    *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c + 1)) = hi;
+  }
+}
+
+template <int D, int NG>
+__global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnParams p) {
+  using SM = UmSmem<D, NG>;
+  using SG = SubGeom<D, NG>;
+  constexpr int SB = SG::SB;
+  extern __shared__ uint8_t smem_raw[];
+  // the swizzled operand tiles need 1024-byte alignment
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - raw_base);
+  auto bar = [&](int i) { return sbase + SM::BAR_OFF + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::MISC_OFF);
+  volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < kUmNR; ++s) {
+      mbar_init(bar(SM::B_RF + s), 1);            // copy issuer arrive + tx bytes
+      mbar_init(bar(SM::B_RE + s), kUmDeqWarps);  // dequantizer warps
+    }
+    for (int s = 0; s < kUmNF; ++s) {
+      mbar_init(bar(SM::B_KF + s), kUmDeqWarps);
+      mbar_init(bar(SM::B_KE + s), 1);            // MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(SM::B_SF + b), 1);            // MMA commit
+      mbar_init(bar(SM::B_PF + b), 4);            // softmax warps
+      mbar_init(bar(SM::B_PD + b), 1);            // MMA commit
+    }
+    mbar_init(bar(SM::B_QF), 4);
+    mbar_init(bar(SM::B_FIN), 1);
+    *cta_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), kUmCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int it0 = p.sh_cta_off[blockIdx.x], it1 = p.sh_cta_off[blockIdx.x + 1];
+  const int Hkv = p.Hkv;
+
+  if (warp == 5) {
+    // ---------------- copy issuer ----------------
+    if (lane == 0) {
+      const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
+      uint32_t J = 0;
+      for (int it = it0; it < it1; ++it) {
+        const ShItem item = p.sh_items[it];
+        const int32_t* bt = p.bt + (int64_t)item.leader * p.bt_stride;
+        const uint8_t* page = p.pool + ((int64_t)item.layer * Hkv + item.h) * p.page_bytes;
+        for (int j = item.sb_begin; j < item.sb_end; ++j, ++J) {
+          const int b = __ldg(bt + j / SG::SPB);
+          const uint32_t s = J % kUmNR;
+          if (J >= (uint32_t)kUmNR)
+            mbar_wait(bar(SM::B_RE + s), ((J / kUmNR) - 1) & 1, cta_abort, p.err);
+          mbar_expect_tx(bar(SM::B_RF + s), SB);
+          bulk_g2s(sbase + SM::RAW_OFF + s * SB,
+                   page + (int64_t)b * blk_stride + (int64_t)(j % SG::SPB) * SB, SB,
+                   bar(SM::B_RF + s));
+        }
+      }
+      // every issued copy has landed before the CTA may exit
+      for (uint32_t k = J > (uint32_t)kUmNR ? J - kUmNR : 0; k < J; ++k)
+        mbar_wait(bar(SM::B_RF + k % kUmNR), (k / kUmNR) & 1, cta_abort, p.err);
+    }
+  } else if (warp >= 6) {
+    // ---------------- dequantizers ----------------
+    const int t0 = tid - 6 * 32;
+    uint32_t J = 0;
+    for (int it = it0; it < it1; ++it) {
+      const ShItem item = p.sh_items[it];
+      for (int j = item.sb_begin; j < item.sb_end; ++j, ++J) {
+        const uint32_t rs = J % kUmNR, fs = J % kUmNF;
+        mbar_wait(bar(SM::B_RF + rs), (J / kUmNR) & 1, cta_abort, p.err);
+        if (J >= (uint32_t)kUmNF)
+          mbar_wait(bar(SM::B_KE + fs), ((J / kUmNF) - 1) & 1, cta_abort, p.err);
+        uint8_t* kt = smem + SM::KV_OFF + fs * SM::KV_STAGE;
+        um_dequant<D, NG>(smem + SM::RAW_OFF + rs * SB, kt, kt + SM::K_BYTES, t0);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(SM::B_RE + rs));
+          mbar_arrive(bar(SM::B_KF + fs));
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc(128, 64), idO = umma_idesc(128, D);
+      const uint32_t qb = sbase + SM::Q_OFF;
+      auto issue_pv = [&](uint32_t Jp, bool first) {
+        mbar_wait(bar(SM::B_PF + (Jp & 1)), (Jp >> 1) & 1, cta_abort, p.err);
+        tc_fence_after();
+        const uint32_t stp = Jp % kUmNF;
+        const uint32_t vb = sbase + SM::KV_OFF + stp * SM::KV_STAGE + SM::K_BYTES;
+        const uint32_t pb = sbase + SM::P_OFF + (Jp & 1) * SM::P_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16(tmem, sw128_desc(pb + 32 * ks), sw128_desc(vb + 32 * ks), idO,
+                   (!first || ks > 0) ? 1u : 0u);
+        umma_commit(bar(SM::B_KE + stp));        // K/V stage free
+        umma_commit(bar(SM::B_PD + (Jp & 1)));   // O updated, P buffer free
+      };
+      uint32_t J = 0, itn = 0;
+      for (int it = it0; it < it1; ++it, ++itn) {
+        const ShItem item = p.sh_items[it];
+        const int n = item.sb_end - item.sb_begin;
+        mbar_wait(bar(SM::B_QF), itn & 1, cta_abort, p.err);
+        tc_fence_after();
+        for (int j = 0; j < n; ++j) {
+          const uint32_t Jc = J + j, st = Jc % kUmNF;
+          mbar_wait(bar(SM::B_KF + st), (Jc / kUmNF) & 1, cta_abort, p.err);
+          tc_fence_after();
+          const uint32_t kb = sbase + SM::KV_OFF + st * SM::KV_STAGE;
+          const uint32_t sc = tmem + kUmS0 + 64u * (Jc & 1);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_f16(sc, sw128_desc(qb + (ks >> 2) * (128 * 128) + 32 * (ks & 3)),
+                     sw128_desc(kb + (ks >> 2) * (64 * 128) + 32 * (ks & 3)), idS,
+                     ks > 0 ? 1u : 0u);
+          umma_commit(bar(SM::B_SF + (Jc & 1)));
+          if (j > 0) issue_pv(Jc - 1, j == 1);
+        }
+        if (n > 0) issue_pv(J + n - 1, n == 1);
+        J += (uint32_t)n;
+      }
+      // every MMA has completed before the tensor memory is released
+      umma_commit(bar(SM::B_FIN));
+      mbar_wait(bar(SM::B_FIN), 0, cta_abort, p.err);
+    }
+  } else {
+    // ---------------- softmax / epilogue: thread t = query row t ----------------
+    const int t = tid;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    const int gq = p.g;
+    uint32_t J = 0;
+    for (int it = it0; it < it1; ++it) {
+      const ShItem item = p.sh_items[it];
+      const int n = item.sb_end - item.sb_begin;
+      // ---- this row's query -> Q tile (K-major SW128, 128 rows) ----
+      {
+        uint8_t* qs = smem + SM::Q_OFF;
+        int64_t qoff = -1;
+        if (t < item.n_rows) {
+          const int mem = t / gq, jq = t - mem * gq;
+          const int64_t qrow = p.units[p.sh_members[item.mem_off + mem]].qo_row;
+          qoff = (qrow * p.Hq + (int64_t)item.h * gq + jq) * D;
+        }
+#pragma unroll 4
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (qoff >= 0) {
+            v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qoff) + c);
+            if (p.q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
+              uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wv[k]));
+                wv[k] = f2h2(f.x, f.y);
+              }
+              v = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+          *reinterpret_cast<uint4*>(qs + sw128_off(128, t, c)) = v;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(SM::B_QF));
+      }
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const uint32_t Jc = J + j;
+        mbar_wait(bar(SM::B_SF + (Jc & 1)), (Jc >> 1) & 1, cta_abort, p.err);
+        tc_fence_after();
+        float s[64];
+        {
+          float a[32], b[32];
+          tmem_ld32(lane_addr + kUmS0 + 64u * (Jc & 1), a);
+          tmem_ld32(lane_addr + kUmS0 + 64u * (Jc & 1) + 32u, b);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[i] = a[i] * p.scale_log2;
+            s[32 + i] = b[i] * p.scale_log2;
+          }
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
+        if (j == 0) {
+          m = mx;  // O is overwritten by this item's first P·V
+        } else {
+          const bool grow = mx > m + 8.f;
+          if (__any_sync(0xffffffffu, grow)) {
+            // O holds P·V up to tile Jc-1: wait for it, then rescale in place
+            mbar_wait(bar(SM::B_PD + ((Jc - 1) & 1)), ((Jc - 1) >> 1) & 1, cta_abort, p.err);
+            tc_fence_after();
+            const float mn = grow ? mx : m;
+            const float al = exp2f(m - mn);
+            m = mn;
+            l *= al;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              float o[32];
+              tmem_ld32(lane_addr + 32u * c, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= al;
+              tmem_st32(lane_addr + 32u * c, o);
+            }
+          }
+        }
+        float ps = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          s[i] = exp2f(s[i] - m);
+          ps += s[i];
+        }
+        l += ps;
+        // P buffer (Jc & 1) was last read by P·V of tile Jc-2
+        if (Jc >= 2) mbar_wait(bar(SM::B_PD + (Jc & 1)), ((Jc - 2) >> 1) & 1, cta_abort, p.err);
+        uint8_t* pb = smem + SM::P_OFF + (Jc & 1) * SM::P_BYTES;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 w;
+          w.x = f2h2(s[8 * c + 0], s[8 * c + 1]);
+          w.y = f2h2(s[8 * c + 2], s[8 * c + 3]);
+          w.z = f2h2(s[8 * c + 4], s[8 * c + 5]);
+          w.w = f2h2(s[8 * c + 6], s[8 * c + 7]);
+          *reinterpret_cast<uint4*>(pb + sw128_off(128, t, c)) = w;
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(SM::B_PF + (Jc & 1)));
+      }
+      if (n > 0) {
+        // ---- epilogue: O row -> partial record `slot` of the member's unit ----
+        const uint32_t Jl = J + n - 1;
+        mbar_wait(bar(SM::B_PD + (Jl & 1)), (Jl >> 1) & 1, cta_abort, p.err);
+        tc_fence_after();
+        float* part = nullptr;
+        int jq = 0;
+        const AttnUnit* un = nullptr;
+        if (t < item.n_rows) {
+          const int mem = t / gq;
+          jq = t - mem * gq;
+          un = p.units + p.sh_members[item.mem_off + mem];
+          part = p.partials +
+                 ((int64_t)(un->first_split + item.slot) * Hkv + item.h) * partial_floats(D);
+        }
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(lane_addr + 32u * c, o);
+          if (part) {
+            float4* dst = reinterpret_cast<float4*>(part + 16 + jq * D + 32 * c);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
+        }
+        if (part) {
+          part[jq] = m;
+          part[8 + jq] = l;
+          if (item.slot == 0)
+            for (int sl = item.n_frag; sl < p.n_pslots; ++sl) {
+              float* e = p.partials + ((int64_t)(un->first_split + sl) * Hkv + item.h) * partial_floats(D);
+              e[jq] = -INFINITY;
+              e[8 + jq] = 0.f;
+            }
+        }
+        tc_fence_before();
+      }
+      J += (uint32_t)n;
+    }
+  }
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kUmCols);
+  }
+}
+
+template <int D, int NG>
+cudaError_t launch_um(const AttnParams& p, cudaStream_t stream) {
+  using SM = UmSmem<D, NG>;
+  static_assert(SM::TOTAL <= 232448, "shared memory budget");
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(attn_shared_umma_kernel<D, NG>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit);
+  }
+  attn_shared_umma_kernel<D, NG><<<p.sh_grid, kUmThreads, SM::TOTAL, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool shared_uses_umma(const Geom& g, int impl) {
+  return impl == KRILL_ATTN_TENSOR_CORE && g.D <= 128;
+}
+
+cudaError_t launch_shared_umma(const Geom& g, const AttnParams& p, cudaStream_t stream) {
+  if (p.sh_grid <= 0) return cudaSuccess;
+  if (g.D == 64 && g.NG == 1) return launch_um<64, 1>(p, stream);
+  if (g.D == 128 && g.NG == 2) return launch_um<128, 2>(p, stream);
+  if (g.D == 128 && g.NG == 1) return launch_um<128, 1>(p, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace krill

@@ -29,13 +29,14 @@ from tests.test_gpu_attention import ATOL, half_ulp  # noqa: E402
 
 
 def run_cascade(D, G, hq, hkv, dtype, prefixes, scale, layers=2, extra=(), outliers=False,
-                out_dtype=torch.float32, steps=2, seed=0, min_groups=1, min_slots=1):
+                out_dtype=torch.float32, steps=2, seed=0, min_groups=1, min_slots=1,
+                impl=kb.ATTN_TENSOR_CORE):
     """prefixes: list of (prefix length, [suffix length per fork]). extra:
     lengths of independent sequences batched alongside."""
     rng = np.random.default_rng(seed)
     total = sum(p + sum(s) + len(s) * 256 for p, s in prefixes) + sum(extra) + 1024
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=total // 256 + 16 * (len(extra) + 4),
-                     group_size=G)
+                     group_size=G, attn_impl=impl)
     pc = kb.PrefixCache(pool)
     seqs, K, V = [], [], []
     for pi, (P, suffixes) in enumerate(prefixes):
@@ -144,3 +145,13 @@ def test_cascade_outliers():
 def test_cascade_low_precision_out(out_dtype):
     run_cascade(128, 64, 32, 8, F16, [(512, [1, 2, 3])], 1 / math.sqrt(128), out_dtype=out_dtype,
                 layers=1, steps=1)
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,scale", [
+    (128, 64, 32, 8, BF16, 1 / math.sqrt(128)),
+    (64, 64, 32, 8, F16, 1 / 8),
+])
+def test_cascade_mma_sync_variant(D, G, hq, hkv, dtype, scale):
+    # the cascade part on mma.sync (KRILL_ATTN_TENSOR_CORE_SYNC), kept for comparison
+    run_cascade(D, G, hq, hkv, dtype, [(1024, [1, 17, 64, 300])], scale,
+                impl=kb.ATTN_TENSOR_CORE_SYNC)
