@@ -124,12 +124,12 @@ cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
 cudaError_t launch_shared(const Geom& g, const AttnParams& p, cudaStream_t stream);
-// The cascade runs on tcgen05 (accumulators in tensor memory, 128 query rows
-// per item) for head_dim <= 128 under KRILL_ATTN_TENSOR_CORE; otherwise on
-// mma.sync (sh_rows(D) query rows per item).
+// The cascade runs on tcgen05 (accumulators in tensor memory, 256 query rows
+// per item as two 128-row halves) for head_dim <= 128 under
+// KRILL_ATTN_TENSOR_CORE; otherwise on mma.sync (sh_rows(D) rows per item).
 bool shared_uses_umma(const Geom& g, int impl);
 cudaError_t launch_shared_umma(const Geom& g, const AttnParams& p, cudaStream_t stream);
-inline int shared_rows(const Geom& g, int impl) { return shared_uses_umma(g, impl) ? 128 : sh_rows(g.D); }
+inline int shared_rows(const Geom& g, int impl) { return shared_uses_umma(g, impl) ? 256 : sh_rows(g.D); }
 // Launch description produced for the allocation-free decode attention:
 // byte offsets of the metadata and partial records inside the caller's
 // scratch, plus the launch parameters (pointers into the scratch unset).

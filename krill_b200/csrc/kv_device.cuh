@@ -42,7 +42,9 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort,
   const uint64_t limit = *cta_abort ? 20000ull : 10000000000ull;
   const uint64_t t0 = globaltimer();
   for (;;) {
-    if (mbar_try_wait(bar, phase)) return true;
+    // the clock is read once per 16 polls: it is off the wake-up path
+    for (int k = 0; k < 16; ++k)
+      if (mbar_try_wait(bar, phase)) return true;
     if (globaltimer() - t0 > limit) {
       *cta_abort = 1;
       atomicOr(err, kErrTimeout);

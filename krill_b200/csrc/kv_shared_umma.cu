@@ -3,22 +3,26 @@
 //
 // Same work items and results as kv_shared.cu (forks of one prefix-cache
 // entry attend the common blocks once per (layer, kv head); see there for the
-// reference mapping), for head_dim 64 and 128. One CTA per SM, 12 warps:
-//   - warp 5 streams raw sub-blocks HBM -> shared memory (cp.async.bulk);
-//   - warps 6-11 dequantize each raw sub-block once (the reference's two fp16
-//     roundings) into f16 K [64 tok][D] and V [D][64 tok] tiles laid out as
-//     the tensor core's canonical K-major 128-byte-swizzled operands;
-//   - warp 4 owns the tensor memory and one of its lanes issues the MMAs:
-//       S_j  = Q · K_jᵀ      (M = 128 query rows, N = 64 tokens, K = D)
-//       O   += P_j · V_j     (M = 128, N = D, K = 64 tokens)
+// reference mapping), for head_dim 64 and 128. An item covers up to 256 query
+// rows as two 128-row halves that share every K/V tile. One CTA per SM, 16
+// warps:
+//   - warp 9 streams raw sub-blocks HBM -> shared memory (cp.async.bulk);
+//   - warps 10-15 dequantize each raw sub-block once (the reference's two
+//     fp16 roundings) into f16 K [64 tok][D] and V [D][64 tok] tiles laid out
+//     as the tensor core's canonical K-major 128-byte-swizzled operands;
+//   - warp 8 owns the tensor memory (512 columns) and one of its lanes issues
+//     the MMAs, per half h:
+//       S_h  = Q_h · K_jᵀ     (M = 128 query rows, N = 64 tokens, K = D)
+//       O_h += P_h · V_j      (M = 128, N = D, K = 64 tokens)
 //     with S double-buffered in tensor memory so the softmax of tile j
-//     overlaps S_{j+1}; each group of MMAs is committed to an mbarrier;
-//   - warps 0-3 (thread t = query row t = tensor-memory lane t) read S_j with
-//     tcgen05.ld, run the online softmax in the exp2 domain and write P_j as
-//     f16 into a swizzled shared tile. The running max is only raised when a
-//     row's max grows by more than 8 (log2 units); the rare O rescale is a
-//     tcgen05.ld / st round trip after the previous P·V has completed. At the
-//     end of an item they read O and write the fp32 partial records.
+//     overlaps S of tile j+1; each group of MMAs is committed to an mbarrier;
+//   - warps 4h .. 4h+3 (thread t = query row t of half h = tensor-memory
+//     lane t) read S with tcgen05.ld, run the online softmax in the exp2
+//     domain and write P_h as f16 into a swizzled shared tile. The running max
+//     is only raised when a row's max grows by more than 8 (log2 units); the
+//     rare O rescale is a tcgen05.ld / st round trip after the previous P·V
+//     has completed. At the end of an item they read O and write the fp32
+//     partial records.
 // Every wait is bounded (10 s, then 20 us after the first timeout) and sets
 // the pool's error flag; the tensor memory is released on every path.
 #include <atomic>
@@ -29,10 +33,12 @@ namespace krill {
 namespace {
 
 constexpr int kUmNF = 3;         // f16 K/V tile stages
-constexpr int kUmNR = 3;         // raw sub-block stages
-constexpr int kUmDeqWarps = 6;   // warps 6-11
-constexpr int kUmThreads = 384;  // 12 warps: 168 registers a thread at one CTA per SM
-constexpr uint32_t kUmCols = 256;  // tensor-memory columns: O [0, D), S buffers at 128 and 192
+constexpr int kUmNR = 2;         // raw sub-block stages
+constexpr int kUmDeqWarps = 6;   // warps 10-15
+constexpr int kUmThreads = 512;  // 16 warps
+// tensor memory: half h owns columns [256h, 256h + 256): O_h at +0 (D columns),
+// S_h double buffer at +128 and +192
+constexpr uint32_t kUmCols = 512;
 constexpr uint32_t kUmS0 = 128;
 
 // ---- tensor-core primitives (PTX ISA 8.6+, sm_100a) ----
@@ -134,78 +140,137 @@ __device__ __forceinline__ uint32_t sw128_off(int rows, int r, int c) {
   return (uint32_t)((c >> 3) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
+
 template <int D, int NG>
 struct UmSmem {
   using SG = SubGeom<D, NG>;
   static_assert(SG::T == 64, "one 64-token sub-block per tile");
-  static constexpr int Q_BYTES = 128 * D * 2;
-  static constexpr int P_BYTES = 128 * 64 * 2;
+  static constexpr int QH_BYTES = 128 * D * 2;  // one 128-row half of the Q tile
+  static constexpr int P_BYTES = 128 * 64 * 2;  // one half's P tile
   static constexpr int K_BYTES = 64 * D * 2;
   static constexpr int V_BYTES = D * 64 * 2;
-  static constexpr int Q_OFF = 0;
-  static constexpr int P_OFF = Q_OFF + Q_BYTES;  // 2 buffers
+  static constexpr int Q_OFF = 0;                     // 2 halves
+  static constexpr int P_OFF = Q_OFF + 2 * QH_BYTES;  // 2 halves
   static constexpr int KV_OFF = P_OFF + 2 * P_BYTES;
   static constexpr int KV_STAGE = K_BYTES + V_BYTES;
   static constexpr int RAW_OFF = KV_OFF + kUmNF * KV_STAGE;
   static constexpr int BAR_OFF = RAW_OFF + kUmNR * SG::SB;
-  // raw full/empty [NR], kv full/empty [NF], s full [2], p full [2], pv done [2], q full, fin
+  // raw full/empty [NR], kv full/empty [NF]; per half: s full [2], p full,
+  // pv done, q full; fin
   static constexpr int B_RF = 0, B_RE = kUmNR, B_KF = 2 * kUmNR, B_KE = 2 * kUmNR + kUmNF,
-                       B_SF = 2 * kUmNR + 2 * kUmNF, B_PF = B_SF + 2, B_PD = B_PF + 2,
-                       B_QF = B_PD + 2, B_FIN = B_QF + 1, NBAR = B_FIN + 1;
+                       B_SF = 2 * kUmNR + 2 * kUmNF,  // [half][2]
+                       B_PF = B_SF + 4, B_PD = B_PF + 2, B_QF = B_PD + 2, B_FIN = B_QF + 2,
+                       NBAR = B_FIN + 1;
   static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem address, abort flag
-  static constexpr int TOTAL = MISC_OFF + 16 + 1024;   // + alignment slack
-  static_assert(SG::SB % 16 == 0 && KV_STAGE % 1024 == 0 && Q_BYTES % 1024 == 0, "alignment");
+  static constexpr int TOTAL = MISC_OFF + 16;
+  static_assert(SG::SB % 16 == 0 && KV_STAGE % 1024 == 0 && QH_BYTES % 1024 == 0, "alignment");
 };
 
 // One raw sub-block -> f16 K tile [64 tok][D] and V tile [D][64 tok] in the
 // SW128 K-major layout; values f16_rn(f16_rn(code * scale) + zero)
-// (QuantizedKVCache.swift:200-204). t0 = dequantizer thread index.
+// (QuantizedKVCache.swift:200-204). t0 = dequantizer thread index. Each
+// thread first loads all of its items (codes and their scales / zeros), then
+// converts and stores them, so the shared-memory latencies overlap. When every
+// scale of an item is below 64 in magnitude the product is formed by one fma
+// (exact then, see deq2_fast).
+__device__ __forceinline__ uint32_t small2(uint32_t s2) {  // both halves |s| < 64
+  return __vcmpgeu2(s2 & 0x7fff7fffu, 0x54005400u);
+}
+__device__ __forceinline__ uint4 deq16(uint4 w, const uint32_t (&s)[8], const uint32_t (&z)[8],
+                                       bool fast, bool hi) {
+  const int o = hi ? 4 : 0;
+  const uint32_t a = hi ? w.z : w.x, b = hi ? w.w : w.y;
+  uint4 r;
+  if (fast) {
+    r.x = deq2_fast(a, 0x4140u, s[o], neg1024(s[o]), z[o]);
+    r.y = deq2_fast(a, 0x4342u, s[o + 1], neg1024(s[o + 1]), z[o + 1]);
+    r.z = deq2_fast(b, 0x4140u, s[o + 2], neg1024(s[o + 2]), z[o + 2]);
+    r.w = deq2_fast(b, 0x4342u, s[o + 3], neg1024(s[o + 3]), z[o + 3]);
+  } else {
+    r.x = deq2(a, 0x4140u, s[o], z[o]);
+    r.y = deq2(a, 0x4342u, s[o + 1], z[o + 1]);
+    r.z = deq2(b, 0x4140u, s[o + 2], z[o + 2]);
+    r.w = deq2(b, 0x4342u, s[o + 3], z[o + 3]);
+  }
+  return r;
+}
 template <int D, int NG>
 __device__ __forceinline__ void um_dequant(const uint8_t* __restrict__ raw, uint8_t* __restrict__ kt,
                                            uint8_t* __restrict__ vt, int t0) {
   using SG = SubGeom<D, NG>;
   constexpr int G = SG::G;
   constexpr int NDT = kUmDeqWarps * 32;
-  for (int i = t0; i < 64 * (D / 16); i += NDT) {
-    const int t = i / (D / 16), c = i % (D / 16);
-    const int pc = D >= 128 ? (c ^ ((t & 1) << 2)) : c;
-    const uint4 w = *reinterpret_cast<const uint4*>(raw + t * D + pc * 16);
-    const int gi = (16 * c) / G;
-    const uint32_t s = *reinterpret_cast<const uint16_t*>(raw + SG::meta(0, gi, t));
-    const uint32_t z = *reinterpret_cast<const uint16_t*>(raw + SG::meta(1, gi, t));
-    const uint32_t s2 = s | (s << 16), z2 = z | (z << 16);
-    uint4 lo, hi;
-    lo.x = deq2(w.x, 0x4140u, s2, z2);
-    lo.y = deq2(w.x, 0x4342u, s2, z2);
-    lo.z = deq2(w.y, 0x4140u, s2, z2);
-    lo.w = deq2(w.y, 0x4342u, s2, z2);
-    hi.x = deq2(w.z, 0x4140u, s2, z2);
-    hi.y = deq2(w.z, 0x4342u, s2, z2);
-    hi.z = deq2(w.w, 0x4140u, s2, z2);
-    hi.w = deq2(w.w, 0x4342u, s2, z2);
-    *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c)) = lo;
-    *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c + 1)) = hi;
+  constexpr int NK = 64 * (D / 16), NV = D * 4;  // 16-element items
+  constexpr int KI = (NK + NDT - 1) / NDT, VI = (NV + NDT - 1) / NDT;
+  // ---- K: token-major codes (odd rows' chunks swizzled by 4 when D >= 128),
+  // one scale / zero per (token, group) ----
+  uint4 kw[KI];
+  uint32_t ks[KI], kz[KI];
+#pragma unroll
+  for (int k = 0; k < KI; ++k) {
+    const int i = t0 + k * NDT;
+    if (i < NK) {
+      const int t = i / (D / 16), c = i % (D / 16);
+      const int pc = D >= 128 ? (c ^ ((t & 1) << 2)) : c;
+      kw[k] = *reinterpret_cast<const uint4*>(raw + t * D + pc * 16);
+      ks[k] = *reinterpret_cast<const uint16_t*>(raw + SG::meta(0, (16 * c) / G, t));
+      kz[k] = *reinterpret_cast<const uint16_t*>(raw + SG::meta(1, (16 * c) / G, t));
+    }
   }
-  for (int i = t0; i < D * 4; i += NDT) {
-    const int d = i >> 2, c = i & 3;
-    const uint4 w = *reinterpret_cast<const uint4*>(raw + SG::VOFF + d * 64 + c * 16);
-    const int gi = d / G;
-    const uint4 sa = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c));
-    const uint4 sb = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c + 8));
-    const uint4 za = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c));
-    const uint4 zb = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c + 8));
-    uint4 lo, hi;
-    lo.x = deq2(w.x, 0x4140u, sa.x, za.x);
-    lo.y = deq2(w.x, 0x4342u, sa.y, za.y);
-    lo.z = deq2(w.y, 0x4140u, sa.z, za.z);
-    lo.w = deq2(w.y, 0x4342u, sa.w, za.w);
-    hi.x = deq2(w.z, 0x4140u, sb.x, zb.x);
-    hi.y = deq2(w.z, 0x4342u, sb.y, zb.y);
-    hi.z = deq2(w.w, 0x4140u, sb.z, zb.z);
-    hi.w = deq2(w.w, 0x4342u, sb.w, zb.w);
-    *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c)) = lo;
-    *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c + 1)) = hi;
+  // ---- V: transposed codes [D][64]; scale / zero per (token, group) ----
+  uint4 vw[VI], vs[VI][2], vz[VI][2];
+#pragma unroll
+  for (int k = 0; k < VI; ++k) {
+    const int i = t0 + k * NDT;
+    if (i < NV) {
+      const int d = i >> 2, c = i & 3, gi = d / G;
+      vw[k] = *reinterpret_cast<const uint4*>(raw + SG::VOFF + d * 64 + c * 16);
+      vs[k][0] = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c));
+      vs[k][1] = *reinterpret_cast<const uint4*>(raw + SG::meta(2, gi, 16 * c + 8));
+      vz[k][0] = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c));
+      vz[k][1] = *reinterpret_cast<const uint4*>(raw + SG::meta(3, gi, 16 * c + 8));
+    }
   }
+#pragma unroll
+  for (int k = 0; k < KI; ++k) {
+    const int i = t0 + k * NDT;
+    if (i < NK) {
+      const int t = i / (D / 16), c = i % (D / 16);
+      const uint32_t s2 = ks[k] | (ks[k] << 16), z2 = kz[k] | (kz[k] << 16);
+      const uint32_t s8[8] = {s2, s2, s2, s2, s2, s2, s2, s2};
+      const uint32_t z8[8] = {z2, z2, z2, z2, z2, z2, z2, z2};
+      const bool fast = small2(s2) == 0;
+      *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c)) = deq16(kw[k], s8, z8, fast, false);
+      *reinterpret_cast<uint4*>(kt + sw128_off(64, t, 2 * c + 1)) = deq16(kw[k], s8, z8, fast, true);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VI; ++k) {
+    const int i = t0 + k * NDT;
+    if (i < NV) {
+      const int d = i >> 2, c = i & 3;
+      const uint32_t s8[8] = {vs[k][0].x, vs[k][0].y, vs[k][0].z, vs[k][0].w,
+                              vs[k][1].x, vs[k][1].y, vs[k][1].z, vs[k][1].w};
+      const uint32_t z8[8] = {vz[k][0].x, vz[k][0].y, vz[k][0].z, vz[k][0].w,
+                              vz[k][1].x, vz[k][1].y, vz[k][1].z, vz[k][1].w};
+      const bool fast = (small2(s8[0]) | small2(s8[1]) | small2(s8[2]) | small2(s8[3]) |
+                         small2(s8[4]) | small2(s8[5]) | small2(s8[6]) | small2(s8[7])) == 0;
+      // the codes of tokens 8-15 take the scales of words 4-7
+      *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c)) = deq16(vw[k], s8, z8, fast, false);
+      *reinterpret_cast<uint4*>(vt + sw128_off(D, d, 2 * c + 1)) = deq16(vw[k], s8, z8, fast, true);
+    }
+  }
+}
+
+__device__ __forceinline__ float max64(const float (&a)[32], const float (&b)[32]) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    m[k] = fmaxf(fmaxf(fmaxf(a[4 * k], a[4 * k + 1]), fmaxf(a[4 * k + 2], a[4 * k + 3])),
+                 fmaxf(fmaxf(b[4 * k], b[4 * k + 1]), fmaxf(b[4 * k + 2], b[4 * k + 3])));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) m[k] = fmaxf(m[k], m[k + 4]);
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
 template <int D, int NG>
@@ -213,11 +278,16 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
   using SM = UmSmem<D, NG>;
   using SG = SubGeom<D, NG>;
   constexpr int SB = SG::SB;
-  extern __shared__ uint8_t smem_raw[];
-  // the swizzled operand tiles need 1024-byte alignment
-  const uint32_t raw_base = smem_u32(smem_raw);
-  const uint32_t sbase = (raw_base + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (sbase - raw_base);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // The swizzled operand tiles need 1024-byte alignment. The dynamic shared
+  // memory of a kernel without static shared memory starts 1024-aligned on
+  // sm_100; should that not hold, the launch reports an error instead of
+  // computing with misplaced tiles.
+  const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) atomicOr(p.err, kErrBadArg);
+    return;
+  }
   auto bar = [&](int i) { return sbase + SM::BAR_OFF + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::MISC_OFF);
   volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF + 4);
@@ -231,17 +301,18 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       mbar_init(bar(SM::B_KF + s), kUmDeqWarps);
       mbar_init(bar(SM::B_KE + s), 1);            // MMA commit
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(SM::B_SF + b), 1);            // MMA commit
-      mbar_init(bar(SM::B_PF + b), 4);            // softmax warps
-      mbar_init(bar(SM::B_PD + b), 1);            // MMA commit
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(bar(SM::B_SF + 2 * h), 1);        // MMA commit
+      mbar_init(bar(SM::B_SF + 2 * h + 1), 1);
+      mbar_init(bar(SM::B_PF + h), 4);            // the half's softmax warps
+      mbar_init(bar(SM::B_PD + h), 1);            // MMA commit
+      mbar_init(bar(SM::B_QF + h), 4);
     }
-    mbar_init(bar(SM::B_QF), 4);
     mbar_init(bar(SM::B_FIN), 1);
     *cta_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(smem_u32(tmem_slot), kUmCols);
     tmem_relinquish();
   }
@@ -252,7 +323,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
   const int it0 = p.sh_cta_off[blockIdx.x], it1 = p.sh_cta_off[blockIdx.x + 1];
   const int Hkv = p.Hkv;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ---------------- copy issuer ----------------
     if (lane == 0) {
       const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
@@ -276,9 +347,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       for (uint32_t k = J > (uint32_t)kUmNR ? J - kUmNR : 0; k < J; ++k)
         mbar_wait(bar(SM::B_RF + k % kUmNR), (k / kUmNR) & 1, cta_abort, p.err);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 10) {
     // ---------------- dequantizers ----------------
-    const int t0 = tid - 6 * 32;
+    const int t0 = tid - 10 * 32;
     uint32_t J = 0;
     for (int it = it0; it < it1; ++it) {
       const ShItem item = p.sh_items[it];
@@ -297,45 +368,90 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idS = umma_idesc(128, 64), idO = umma_idesc(128, D);
-      const uint32_t qb = sbase + SM::Q_OFF;
-      auto issue_pv = [&](uint32_t Jp, bool first) {
-        mbar_wait(bar(SM::B_PF + (Jp & 1)), (Jp >> 1) & 1, cta_abort, p.err);
-        tc_fence_after();
-        const uint32_t stp = Jp % kUmNF;
-        const uint32_t vb = sbase + SM::KV_OFF + stp * SM::KV_STAGE + SM::K_BYTES;
-        const uint32_t pb = sbase + SM::P_OFF + (Jp & 1) * SM::P_BYTES;
+      uint32_t cnt0 = 0, cnt1 = 0;  // tiles processed by each half
+      uint32_t qn0 = 0, qn1 = 0;    // items processed by each half
+      uint32_t J = 0;
+      // O_h += P_h · V of K/V stage st (P_h ready: PF observed by the caller)
+      auto issue_pv = [&](int h, uint32_t st, bool first) {
+        const uint32_t vb = sbase + SM::KV_OFF + st * SM::KV_STAGE + SM::K_BYTES;
+        const uint32_t pb = sbase + SM::P_OFF + h * SM::P_BYTES;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_f16(tmem, sw128_desc(pb + 32 * ks), sw128_desc(vb + 32 * ks), idO,
+          umma_f16(tmem + 256u * h, sw128_desc(pb + 32 * ks), sw128_desc(vb + 32 * ks), idO,
                    (!first || ks > 0) ? 1u : 0u);
-        umma_commit(bar(SM::B_KE + stp));        // K/V stage free
-        umma_commit(bar(SM::B_PD + (Jp & 1)));   // O updated, P buffer free
+        umma_commit(bar(SM::B_PD + h));  // O_h updated, P_h free
       };
-      uint32_t J = 0, itn = 0;
-      for (int it = it0; it < it1; ++it, ++itn) {
+      for (int it = it0; it < it1; ++it) {
         const ShItem item = p.sh_items[it];
         const int n = item.sb_end - item.sb_begin;
-        mbar_wait(bar(SM::B_QF), itn & 1, cta_abort, p.err);
-        tc_fence_after();
-        for (int j = 0; j < n; ++j) {
-          const uint32_t Jc = J + j, st = Jc % kUmNF;
-          mbar_wait(bar(SM::B_KF + st), (Jc / kUmNF) & 1, cta_abort, p.err);
-          tc_fence_after();
-          const uint32_t kb = sbase + SM::KV_OFF + st * SM::KV_STAGE;
-          const uint32_t sc = tmem + kUmS0 + 64u * (Jc & 1);
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks)
-            umma_f16(sc, sw128_desc(qb + (ks >> 2) * (128 * 128) + 32 * (ks & 3)),
-                     sw128_desc(kb + (ks >> 2) * (64 * 128) + 32 * (ks & 3)), idS,
-                     ks > 0 ? 1u : 0u);
-          umma_commit(bar(SM::B_SF + (Jc & 1)));
-          if (j > 0) issue_pv(Jc - 1, j == 1);
+        const int nh = (item.n_rows + 127) >> 7;
+        mbar_wait(bar(SM::B_QF), qn0 & 1, cta_abort, p.err);
+        ++qn0;
+        if (nh > 1) {
+          mbar_wait(bar(SM::B_QF + 1), qn1 & 1, cta_abort, p.err);
+          ++qn1;
         }
-        if (n > 0) issue_pv(J + n - 1, n == 1);
+        tc_fence_after();
+        // S of tile js goes out once its K/V tiles are ready and its S buffer
+        // has been read (the softmax of tile js-2 is done, i.e. P·V of js-2 was
+        // issued); P·V of tile jp once both halves' P are ready. Whichever is
+        // ready first is issued, so neither chain waits on the other.
+        int js = 0, jp = 0;
+        uint32_t spins = 0;
+        uint64_t idle_since = 0;
+        while (jp < n) {
+          bool progressed = false;
+          if (js < n && js <= jp + 1) {
+            const uint32_t Jc = J + js, st = Jc % kUmNF;
+            if (mbar_try_wait(bar(SM::B_KF + st), (Jc / kUmNF) & 1)) {
+              tc_fence_after();
+              const uint32_t kb = sbase + SM::KV_OFF + st * SM::KV_STAGE;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (h >= nh) break;
+                const uint32_t c = (h == 0 ? cnt0 : cnt1) + js;
+                const uint32_t qb = sbase + SM::Q_OFF + h * SM::QH_BYTES;
+                const uint32_t sc = tmem + 256u * h + kUmS0 + 64u * (c & 1);
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks)
+                  umma_f16(sc, sw128_desc(qb + (ks >> 2) * (128 * 128) + 32 * (ks & 3)),
+                           sw128_desc(kb + (ks >> 2) * (64 * 128) + 32 * (ks & 3)), idS,
+                           ks > 0 ? 1u : 0u);
+                umma_commit(bar(SM::B_SF + 2 * h + (c & 1)));
+              }
+              ++js;
+              progressed = true;
+            }
+          }
+          if (jp < js && mbar_try_wait(bar(SM::B_PF), (cnt0 + jp) & 1) &&
+              (nh < 2 || mbar_try_wait(bar(SM::B_PF + 1), (cnt1 + jp) & 1))) {
+            tc_fence_after();
+            const uint32_t st = (J + jp) % kUmNF;
+            issue_pv(0, st, jp == 0);
+            if (nh > 1) issue_pv(1, st, jp == 0);
+            umma_commit(bar(SM::B_KE + st));  // K/V stage free
+            ++jp;
+            progressed = true;
+          }
+          if (progressed) {
+            spins = 0;
+            idle_since = 0;
+          } else if ((++spins & 63u) == 0) {  // bounded: no progress for 10 s (20 us after an abort)
+            const uint64_t now = globaltimer();
+            if (idle_since == 0) idle_since = now;
+            if (now - idle_since > (*cta_abort ? 20000ull : 10000000000ull)) {
+              *cta_abort = 1;
+              atomicOr(p.err, kErrTimeout);
+              break;
+            }
+          }
+        }
+        cnt0 += (uint32_t)n;
+        if (nh > 1) cnt1 += (uint32_t)n;
         J += (uint32_t)n;
       }
       // every MMA has completed before the tensor memory is released
@@ -343,20 +459,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       mbar_wait(bar(SM::B_FIN), 0, cta_abort, p.err);
     }
   } else {
-    // ---------------- softmax / epilogue: thread t = query row t ----------------
-    const int t = tid;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    // ---------------- softmax / epilogue: half h, thread t = its query row t ----------------
+    const int h = warp >> 2;
+    const int t = tid & 127;
+    const int row = 128 * h + t;
+    const uint32_t lane_addr = tmem + 256u * h + ((uint32_t)((warp & 3) * 32) << 16);
     const int gq = p.g;
-    uint32_t J = 0;
+    uint32_t cnt = 0;
     for (int it = it0; it < it1; ++it) {
       const ShItem item = p.sh_items[it];
       const int n = item.sb_end - item.sb_begin;
-      // ---- this row's query -> Q tile (K-major SW128, 128 rows) ----
+      if (128 * h >= item.n_rows) continue;  // this half has no rows in the item
+      // ---- this row's query -> the half's Q tile (K-major SW128, 128 rows) ----
       {
-        uint8_t* qs = smem + SM::Q_OFF;
+        uint8_t* qs = smem + SM::Q_OFF + h * SM::QH_BYTES;
         int64_t qoff = -1;
-        if (t < item.n_rows) {
-          const int mem = t / gq, jq = t - mem * gq;
+        if (row < item.n_rows) {
+          const int mem = row / gq, jq = row - mem * gq;
           const int64_t qrow = p.units[p.sh_members[item.mem_off + mem]].qo_row;
           qoff = (qrow * p.Hq + (int64_t)item.h * gq + jq) * D;
         }
@@ -379,96 +498,97 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(SM::B_QF));
+        if (lane == 0) mbar_arrive(bar(SM::B_QF + h));
       }
       float m = -INFINITY, l = 0.f;
+      uint8_t* pb = smem + SM::P_OFF + h * SM::P_BYTES;
       for (int j = 0; j < n; ++j) {
-        const uint32_t Jc = J + j;
-        mbar_wait(bar(SM::B_SF + (Jc & 1)), (Jc >> 1) & 1, cta_abort, p.err);
+        const uint32_t c = cnt + j;
+        mbar_wait(bar(SM::B_SF + 2 * h + (c & 1)), (c >> 1) & 1, cta_abort, p.err);
         tc_fence_after();
-        float s[64];
-        {
-          float a[32], b[32];
-          tmem_ld32(lane_addr + kUmS0 + 64u * (Jc & 1), a);
-          tmem_ld32(lane_addr + kUmS0 + 64u * (Jc & 1) + 32u, b);
+        float s0[32], s1[32];
+        tmem_ld32(lane_addr + kUmS0 + 64u * (c & 1), s0);
+        tmem_ld32(lane_addr + kUmS0 + 64u * (c & 1) + 32u, s1);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[i] = a[i] * p.scale_log2;
-            s[32 + i] = b[i] * p.scale_log2;
-          }
+        for (int i = 0; i < 32; ++i) {
+          s0[i] *= p.scale_log2;
+          s1[i] *= p.scale_log2;
         }
-        float mx = s[0];
-#pragma unroll
-        for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
+        const float mx = max64(s0, s1);
+        // O_h and P_h were last used by the P·V of tile c-1: wait for it only
+        // where they are touched (rare O rescale, then the P write)
+        bool pv_done = j == 0;
         if (j == 0) {
           m = mx;  // O is overwritten by this item's first P·V
         } else {
           const bool grow = mx > m + 8.f;
           if (__any_sync(0xffffffffu, grow)) {
-            // O holds P·V up to tile Jc-1: wait for it, then rescale in place
-            mbar_wait(bar(SM::B_PD + ((Jc - 1) & 1)), ((Jc - 1) >> 1) & 1, cta_abort, p.err);
+            mbar_wait(bar(SM::B_PD + h), (c - 1) & 1, cta_abort, p.err);
             tc_fence_after();
+            pv_done = true;
             const float mn = grow ? mx : m;
             const float al = exp2f(m - mn);
             m = mn;
             l *= al;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int cc = 0; cc < D / 32; ++cc) {
               float o[32];
-              tmem_ld32(lane_addr + 32u * c, o);
+              tmem_ld32(lane_addr + 32u * cc, o);
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] *= al;
-              tmem_st32(lane_addr + 32u * c, o);
+              tmem_st32(lane_addr + 32u * cc, o);
             }
           }
         }
-        float ps = 0.f;
+        float ps[8];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          s[i] = exp2f(s[i] - m);
-          ps += s[i];
+        for (int k = 0; k < 8; ++k) ps[k] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s0[i] = exp2f(s0[i] - m);
+          s1[i] = exp2f(s1[i] - m);
+          ps[i & 7] += s0[i] + s1[i];
         }
-        l += ps;
-        // P buffer (Jc & 1) was last read by P·V of tile Jc-2
-        if (Jc >= 2) mbar_wait(bar(SM::B_PD + (Jc & 1)), ((Jc - 2) >> 1) & 1, cta_abort, p.err);
-        uint8_t* pb = smem + SM::P_OFF + (Jc & 1) * SM::P_BYTES;
+        l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        if (!pv_done) mbar_wait(bar(SM::B_PD + h), (c - 1) & 1, cta_abort, p.err);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int cc = 0; cc < 8; ++cc) {
+          const float* src = cc < 4 ? s0 + 8 * cc : s1 + 8 * (cc - 4);
           uint4 w;
-          w.x = f2h2(s[8 * c + 0], s[8 * c + 1]);
-          w.y = f2h2(s[8 * c + 2], s[8 * c + 3]);
-          w.z = f2h2(s[8 * c + 4], s[8 * c + 5]);
-          w.w = f2h2(s[8 * c + 6], s[8 * c + 7]);
-          *reinterpret_cast<uint4*>(pb + sw128_off(128, t, c)) = w;
+          w.x = f2h2(src[0], src[1]);
+          w.y = f2h2(src[2], src[3]);
+          w.z = f2h2(src[4], src[5]);
+          w.w = f2h2(src[6], src[7]);
+          *reinterpret_cast<uint4*>(pb + sw128_off(128, t, cc)) = w;
         }
         fence_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(SM::B_PF + (Jc & 1)));
+        if (lane == 0) mbar_arrive(bar(SM::B_PF + h));
       }
       if (n > 0) {
         // ---- epilogue: O row -> partial record `slot` of the member's unit ----
-        const uint32_t Jl = J + n - 1;
-        mbar_wait(bar(SM::B_PD + (Jl & 1)), (Jl >> 1) & 1, cta_abort, p.err);
+        mbar_wait(bar(SM::B_PD + h), (cnt + n - 1) & 1, cta_abort, p.err);
         tc_fence_after();
         float* part = nullptr;
         int jq = 0;
         const AttnUnit* un = nullptr;
-        if (t < item.n_rows) {
-          const int mem = t / gq;
-          jq = t - mem * gq;
+        if (row < item.n_rows) {
+          const int mem = row / gq;
+          jq = row - mem * gq;
           un = p.units + p.sh_members[item.mem_off + mem];
           part = p.partials +
                  ((int64_t)(un->first_split + item.slot) * Hkv + item.h) * partial_floats(D);
         }
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int cc = 0; cc < D / 32; ++cc) {
           float o[32];
-          tmem_ld32(lane_addr + 32u * c, o);
+          tmem_ld32(lane_addr + 32u * cc, o);
           if (part) {
-            float4* dst = reinterpret_cast<float4*>(part + 16 + jq * D + 32 * c);
+            float4* dst = reinterpret_cast<float4*>(part + 16 + jq * D + 32 * cc);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
           }
         }
         if (part) {
@@ -476,18 +596,19 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
           part[8 + jq] = l;
           if (item.slot == 0)
             for (int sl = item.n_frag; sl < p.n_pslots; ++sl) {
-              float* e = p.partials + ((int64_t)(un->first_split + sl) * Hkv + item.h) * partial_floats(D);
+              float* e =
+                  p.partials + ((int64_t)(un->first_split + sl) * Hkv + item.h) * partial_floats(D);
               e[jq] = -INFINITY;
               e[8 + jq] = 0.f;
             }
         }
         tc_fence_before();
       }
-      J += (uint32_t)n;
+      cnt += (uint32_t)n;
     }
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, kUmCols);
   }
