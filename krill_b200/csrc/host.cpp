@@ -511,7 +511,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       u.layer = L;
       u.t_lo = (int32_t)t_lo;
       u.t_hi = (int32_t)t_hi;
-      u.pad = 0;
+      u.n_pre = 0;
       pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
       total_sb += pl.nsb[ui];
     }
@@ -600,20 +600,29 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     const int64_t n_it = (n_sb + C - 1) / C;
     const int64_t base = n_sb / n_it, extra = n_sb % n_it;
     const int sh_sb = pl.seq_sh[u.si];
-    // cascaded units: records [0, n_pslots) come from the cascade items
+    // cascaded units: records [0, n_pslots) come from the cascade items. A
+    // single suffix piece merges them itself when it finishes; several go
+    // through the combine kernel with the prefix records as pieces 0..
     const int64_t off = sh_sb > 0 ? n_pslots : 0;
-    u.n_split = (int32_t)(off + n_it);
     u.first_split = (int32_t)split_count;
-    if (u.n_split > 1 || sh_sb > 0) {
-      split_count += u.n_split;
-      pl.split_units.push_back((int32_t)ui);
+    u.n_pre = 0;
+    if (sh_sb > 0 && n_it == 1) {
+      u.n_split = 1;
+      u.n_pre = n_pslots;
+      split_count += n_pslots;
+    } else {
+      u.n_split = (int32_t)(off + n_it);
+      if (u.n_split > 1) {
+        split_count += u.n_split;
+        pl.split_units.push_back((int32_t)ui);
+      }
     }
     int64_t b = std::max<int64_t>(u.t_lo / g.subt, sh_sb);
     for (int64_t i = 0; i < n_it; ++i) {
       const int64_t sz = base + (i < extra ? 1 : 0);
       for (int h0 = 0; h0 < g.Hkv; h0 += HG)
-        pl.items.push_back(
-            AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz), (int16_t)(off + i), (int16_t)h0});
+        pl.items.push_back(AttnItem{(int32_t)ui, (int32_t)b, (int32_t)(b + sz),
+                                    (int16_t)(u.n_split == 1 ? 0 : off + i), (int16_t)h0});
       b += sz;
     }
   }

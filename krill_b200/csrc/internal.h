@@ -49,7 +49,8 @@ struct AttnUnit {
   int32_t t_lo, t_hi;   // attended positions
   int32_t first_split;  // partial record of (piece i, head h): (first_split + i) * Hkv + h
   int32_t n_split;
-  int32_t pad;
+  int32_t n_pre;        // with n_split == 1: prefix records [first_split, + n_pre) written
+                        // by the cascade kernel, merged by the decode item that finishes
 };
 
 struct AttnItem {

@@ -312,7 +312,7 @@ constexpr int stages_for() {
 // normalized output, or a partial record plus the last-arriver merge when the
 // unit is split over several items.
 template <int D>
-__device__ __forceinline__ void finish_head(const AttnParams& p, const TCState<D>& st, float l0,
+__device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st, float l0,
                                             float l1, const AttnUnit& un, const AttnItem& item,
                                             int h, int lane) {
   const int r = lane >> 2, tig = lane & 3;
@@ -321,6 +321,50 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, const TCState<D
   const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
   const int h0 = 2 * tig, h1 = 2 * tig + 1;
   if (un.n_split == 1) {
+    if (un.n_pre > 0) {
+      // merge the shared-prefix records the cascade kernel completed earlier
+      // in the stream (heads beyond the GQA group hold no data and are unused)
+      const float* rec = p.partials + ((int64_t)un.first_split * Hkv + h) * partial_floats(D);
+      const int64_t stride = (int64_t)Hkv * partial_floats(D);
+      float M0 = st.m[0], M1 = st.m[1];
+      for (int i = 0; i < un.n_pre; ++i) {
+        M0 = fmaxf(M0, rec[i * stride + (h0 & 7)]);
+        M1 = fmaxf(M1, rec[i * stride + (h1 & 7)]);
+      }
+      const float a0 = st.m[0] == -INFINITY ? 0.f : exp2f(st.m[0] - M0);
+      const float a1 = st.m[1] == -INFINITY ? 0.f : exp2f(st.m[1] - M1);
+      l0 *= a0;
+      l1 *= a1;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        st.o[mt][0] *= a0;
+        st.o[mt][1] *= a1;
+        st.o[mt][2] *= a0;
+        st.o[mt][3] *= a1;
+      }
+      for (int i = 0; i < un.n_pre; ++i) {
+        const float* ri = rec + i * stride;
+        const float m0 = ri[h0 & 7], m1 = ri[h1 & 7];
+        const float b0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
+        const float b1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
+        if (b0 != 0.f && h0 < g) {
+          l0 += ri[8 + h0] * b0;
+#pragma unroll
+          for (int mt = 0; mt < D / 16; ++mt) {
+            st.o[mt][0] += ri[16 + h0 * D + 16 * mt + r] * b0;
+            st.o[mt][2] += ri[16 + h0 * D + 16 * mt + r + 8] * b0;
+          }
+        }
+        if (b1 != 0.f && h1 < g) {
+          l1 += ri[8 + h1] * b1;
+#pragma unroll
+          for (int mt = 0; mt < D / 16; ++mt) {
+            st.o[mt][1] += ri[16 + h1 * D + 16 * mt + r] * b1;
+            st.o[mt][3] += ri[16 + h1 * D + 16 * mt + r + 8] * b1;
+          }
+        }
+      }
+    }
     const float i0 = 1.f / l0, i1 = 1.f / l1;
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
