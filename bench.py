@@ -62,13 +62,15 @@ def algo_bytes_attn(L, hkv, D, G):
     return L * hkv * (2 * D + 8 * D // G)
 
 
-def step_bytes(lengths_after, cfg):
-    """Algorithmic bytes of one step (SURVEY 8(d) definition) split into the
-    attention kernel's share and the whole step."""
+def step_bytes(lengths_after, cfg, raw=False):
+    """Algorithmic bytes of one step split into the attention kernel's share
+    and the whole step. int8: K/V codes + fp16 scale and zero per group,
+    2D + 8D/G bytes per (token, head); raw bf16 pools: 4D."""
     hkv, hq, D, G, layers = cfg["hkv"], cfg["hq"], cfg["D"], cfg["G"], cfg["layers"]
-    attn = sum(algo_bytes_attn(L, hkv, D, G) for L in lengths_after) * layers
+    per_tok = 4 * D if raw else 2 * D + 8 * D // G
+    attn = sum(L * hkv * per_tok for L in lengths_after) * layers
     qo = len(lengths_after) * layers * 2 * hq * D * 2
-    append = len(lengths_after) * layers * (hkv * D * 4 + hkv * (2 * D + 8 * D // G))
+    append = len(lengths_after) * layers * (hkv * D * 4 + hkv * per_tok)
     return attn + qo, attn + qo + append
 
 
@@ -276,6 +278,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     len0 = seqs[0].length(0)
     pool.set_profiling(True)
     pool.kernel_times()
+    pool.kernel_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
@@ -288,6 +291,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
         dist.barrier()
     total_ms = start.elapsed_time(stop)
     am, an, pm, pn = pool.kernel_times()
+    launches = pool.kernel_count()
     ms = total_ms / args.steps
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -321,7 +325,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                          "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
                          "frac_unique": unique / (attn_ms / 1e3) / 1e9 / peak,
                          "algo_bytes_logical": logical, "algo_bytes_unique": unique},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches,
             "clocks": clocks.summary(),
             "device_error_flag": pool.device_error(),
         }
@@ -414,6 +418,8 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     slid.set_profiling(True)
     glob.kernel_times()
     slid.kernel_times()
+    glob.kernel_count()
+    slid.kernel_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
@@ -425,6 +431,7 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(stop) / args.steps
+    launches = glob.kernel_count() + slid.kernel_count()
     ag, _, pg, _ = glob.kernel_times()
     as_, _, ps, _ = slid.kernel_times()
     if world > 1:
@@ -458,7 +465,7 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                          "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
                          "frac": (glob_b + slid_b + qo) / (attn_ms / 1e3) / 1e9 / peak,
                          "algo_bytes": glob_b + slid_b + qo},
-            "gpu_launches": 4 * args.steps, "fill_s": t_fill, "clocks": clocks.summary(),
+            "gpu_launches": launches, "fill_s": t_fill, "clocks": clocks.summary(),
             "device_error_flag": glob.device_error() | slid.device_error(),
         }
         print(json.dumps(line), flush=True)
@@ -477,6 +484,8 @@ def main():
     ap.add_argument("--impl", default="krill", choices=["krill", "reference"])
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--attn-impl", default="tc", choices=["tc", "cuda"])
+    ap.add_argument("--kv", default="int8", choices=["int8", "bf16"],
+                    help="pool format; bf16 = the unquantized comparison variant (default workload)")
     ap.add_argument("--split-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layer-sample", type=int, default=12)
@@ -528,9 +537,13 @@ def main():
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
     total_steps = args.warmup + args.steps * 2 + 2
     blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4
+    raw = args.kv == "bf16"
+    if raw and cfg["dtype"] != "bf16":
+        raise SystemExit("--kv bf16 needs a workload with bf16 K/V")
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G,
                      attn_impl=kb.ATTN_TENSOR_CORE if args.attn_impl == "tc" else kb.ATTN_CUDA_CORE,
-                     split_tokens=args.split_tokens, device=local_rank)
+                     split_tokens=args.split_tokens, kv_format=kb.KV_BF16 if raw else kb.KV_INT8,
+                     device=local_rank)
     seqs = [pool.create_sequence() for _ in mine]
     dev = torch.device("cuda", local_rank)
     gen = torch.Generator(device=dev)
@@ -588,6 +601,7 @@ def main():
     # the launching stream
     pool.set_profiling(True)
     pool.kernel_times()
+    pool.kernel_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
@@ -598,6 +612,7 @@ def main():
         stop.record(stream)
         torch.cuda.synchronize()
     barrier()
+    launches = pool.kernel_count()
     total_ms = start.elapsed_time(stop)
     attn_total, attn_n, app_total, app_n = pool.kernel_times()
     pool.set_profiling(False)
@@ -611,7 +626,7 @@ def main():
     attn_bytes, step_b = 0, 0
     for i in range(args.steps):
         la = [L + i + 1 for L in len_before]
-        a, s_ = step_bytes(la, cfg)
+        a, s_ = step_bytes(la, cfg, raw)
         attn_bytes += a
         step_b += s_
     attn_bytes /= args.steps
@@ -649,7 +664,7 @@ def main():
 
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not raw:
             threads = os.cpu_count() or 1
             v_cpu, el = cpu_baseline(cfg, lengths_all, 1, threads, min(args.cpu_layer_sample, layers))
             cpu = {"value": v_cpu, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -658,7 +673,8 @@ def main():
                              "of QuantizedKVCache.update dataflow + SDPA"}
         clk = clocks.summary()
         line = {
-            "metric": "int8-KV decode-attn+append tokens/s",
+            "metric": ("bf16-KV decode-attn+append tokens/s (comparison variant)" if raw
+                       else "int8-KV decode-attn+append tokens/s"),
             "value": value,
             "unit": "tokens/s",
             "n_gpus": world,
@@ -668,9 +684,10 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "u8",
+            "dtype": "bf16" if raw else "u8",
             "data": "synthetic",
-            "config": {"workload": args.config, "layers": layers, "q_heads": hq, "kv_heads": hkv,
+            "config": {"workload": args.config, "kv_format": args.kv, "layers": layers, "q_heads": hq,
+                       "kv_heads": hkv,
                        "head_dim": D, "group_size": G, "kv_in_dtype": cfg["dtype"],
                        "seqs_per_gpu": cfg["seqs"], "global_seqs": n_total,
                        "mean_len": float(np.mean(lengths_all)),
@@ -678,14 +695,14 @@ def main():
                        "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": profiled_traffic(args.config, attn_bytes),
+                         "traffic": None if raw else profiled_traffic(args.config, attn_bytes),
                          "kernel": "attn_tc_kernel", "peak_kind": peak_kind,
                          "attn_ms": attn_mean_ms, "append_ms": float(np.mean(app_ms)),
                          "step_gbs": step_gbs, "algo_bytes_attn": attn_bytes,
                          "algo_bytes_step": step_b},
             "e2e": {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches,
             "clocks": clk,
             "prefill_s": t_fill,
             "device_error_flag": err_flag,

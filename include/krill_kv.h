@@ -77,6 +77,12 @@ enum { KRILL_QUANT_F32 = 0, KRILL_QUANT_INPUT_DTYPE = 1 };
  *   TENSOR_CORE_SYNC  as TENSOR_CORE with the cascade part on mma.sync */
 enum { KRILL_ATTN_TENSOR_CORE = 0, KRILL_ATTN_CUDA_CORE = 1, KRILL_ATTN_TENSOR_CORE_SYNC = 2 };
 
+/* Storage format of a pool: int8 codes with fp16 scale/zero per group (the
+ * reference's QuantizedKVCache), or raw bf16 K/V (the unquantized KVCache of
+ * Sources/KrillCache/KVCache.swift:94, kept for comparison; head_dim 64 or 128,
+ * bf16 k/v/q, no quantized snapshots or cascade). */
+enum { KRILL_KV_INT8 = 0, KRILL_KV_BF16 = 1 };
+
 typedef struct krill_pool_s* krill_pool_t;
 typedef uint64_t krill_seq_t;               /* generation << 32 | slot */
 typedef struct krill_prefix_s* krill_prefix_t;
@@ -107,6 +113,7 @@ typedef struct {
                              dequantized once. 0 -> 256; < 0 -> off. Applies
                              to full-history pools with a tensor-core
                              implementation and split_tokens = 0.           */
+  int32_t kv_format;      /* KRILL_KV_INT8 (default) or KRILL_KV_BF16           */
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
 } krill_pool_cfg;
 
@@ -139,6 +146,10 @@ krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
 krill_status_t krill_pool_set_profiling(krill_pool_t pool, int32_t enable);
 krill_status_t krill_pool_kernel_times(krill_pool_t pool, double* attn_ms, int32_t* attn_launches,
                                        double* append_ms, int32_t* append_launches);
+/* Measurement hook (no reference counterpart): device kernels this pool
+ * launched (append, attention with its cascade and combine passes, gathers,
+ * scatters) since the previous call; resets the count. */
+krill_status_t krill_pool_kernel_count(krill_pool_t pool, int64_t* kernels);
 
 /* Introspection (no reference counterpart): the decomposition chosen by the
  * last krill_decode_attention on this pool — sequence piece length in 64-token

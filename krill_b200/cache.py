@@ -64,18 +64,20 @@ class KVPool:
     def __init__(self, num_layers: int, num_kv_heads: int, num_q_heads: int, head_dim: int,
                  num_blocks: int, group_size: int = 64, window: int = 0, max_append: int = 0,
                  quant_variant: int = L.QUANT_F32, attn_impl: int = L.ATTN_TENSOR_CORE,
-                 split_tokens: int = 0, cascade_min_tokens: int = 0, device: int = 0):
+                 split_tokens: int = 0, cascade_min_tokens: int = 0, kv_format: int = L.KV_INT8,
+                 device: int = 0):
         cfg = L.PoolCfg(num_layers, num_kv_heads, num_q_heads, head_dim, group_size, window,
                         max_append, quant_variant, attn_impl, split_tokens, cascade_min_tokens,
-                        num_blocks)
+                        kv_format, num_blocks)
         h = C.c_void_p()
         check(L.lib.krill_pool_create(C.byref(cfg), device, C.byref(h)))
         self.handle = h
         self.cfg = cfg
         self.device = device
         self.num_layers, self.num_kv_heads, self.num_q_heads = num_layers, num_kv_heads, num_q_heads
-        self.head_dim, self.group_size, self.window = head_dim, group_size, window
-        self.num_groups = head_dim // group_size
+        self.head_dim, self.window, self.kv_format = head_dim, window, kv_format
+        self.group_size = head_dim if kv_format == L.KV_BF16 else group_size
+        self.num_groups = head_dim // self.group_size
 
     def close(self):
         if self.handle:
@@ -120,6 +122,12 @@ class KVPool:
         check(L.lib.krill_pool_kernel_times(self.handle, C.byref(am), C.byref(an), C.byref(pm),
                                             C.byref(pn)))
         return am.value, an.value, pm.value, pn.value
+
+    def kernel_count(self) -> int:
+        """Device kernels this pool launched since the previous call."""
+        v = C.c_int64()
+        check(L.lib.krill_pool_kernel_count(self.handle, C.byref(v)))
+        return v.value
 
     def last_plan(self):
         """(piece sub-blocks, kv heads per item, items, CTAs) of the last

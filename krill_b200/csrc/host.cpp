@@ -124,6 +124,7 @@ struct krill_pool_s {
   int num_sms = 148;
   float* d_partials = nullptr;
   int64_t partials_cap = 0;
+  int64_t kernels = 0;  // device kernels launched since the last krill_pool_kernel_count
   int* d_err = nullptr;
   StageSlot stage[kStageSlots];
   int stage_next = 0;
@@ -331,6 +332,8 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
                          cudaStream_t stream) {
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(dtype, "k/v"));
+  if (p->geom.fmt == kFmtBf16 && dtype != KRILL_DTYPE_BF16)
+    return fail(KRILL_ERR_INVALID, "a bf16 pool stores bf16 K/V: k/v dtype must be BF16");
   if (n_seqs < 0 || n_new < 0) return fail(KRILL_ERR_INVALID, "negative count");
   if (n_seqs == 0 || lc == 0 || n_new == 0) return KRILL_OK;
   if (!seqs || (!p->host_only && (!k || !v))) return fail(KRILL_ERR_INVALID, "null k/v/seqs");
@@ -379,6 +382,7 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
       return launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
                            n_seqs, n_new, k, v, dtype, stream);
     }));
+    p->kernels += 1;
     TRY(stage_release(slot, stream));
   }
   for (int si = 0; si < n_seqs; ++si) {
@@ -415,6 +419,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
                             int32_t out_dtype, float scale, cudaStream_t stream) {
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(q_dtype, "q"));
+  if (p->geom.fmt == kFmtBf16 && q_dtype != KRILL_DTYPE_BF16)
+    return fail(KRILL_ERR_INVALID, "attention over a bf16 pool takes a BF16 q");
   if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
     return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
   if (n_seqs < 0) return fail(KRILL_ERR_INVALID, "negative n_seqs");
@@ -442,7 +448,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.gshared.clear();
   pl.seq_sh.assign((size_t)n_seqs, 0);
   const int64_t min_tok = p->cfg.cascade_min_tokens == 0 ? 256 : p->cfg.cascade_min_tokens;
-  if (!p->windowed() && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE && p->cfg.split_tokens == 0 &&
+  if (!p->windowed() && g.fmt == kFmtInt8 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE &&
+      p->cfg.split_tokens == 0 &&
       p->cfg.cascade_min_tokens >= 0 && n_seqs >= 2) {
     const size_t min_blocks = (size_t)std::max<int64_t>(1, (min_tok + kBlockTokens - 1) / kBlockTokens);
     pl.gorder.clear();
@@ -747,6 +754,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.n_pslots = n_pslots;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
+  p->kernels += 1 + (pl.split_units.empty() ? 0 : 1) + (sh_grid > 0 ? 1 : 0);
   TRY(stage_release(slot, stream));
   return KRILL_OK;
 }
@@ -796,6 +804,7 @@ krill_status_t do_restore(krill_pool_t p, Seq& s, int32_t layer, int64_t rows, i
       TRY(upload_bt(p, s, stream, &slot));
       CUDA_TRY(launch_scatter(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d),
                               p0, rows, in, stream));
+      p->kernels += 1;
       TRY(stage_release(slot, stream));
     }
   }
@@ -846,6 +855,14 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");
   if (cfg.num_blocks <= 0 || cfg.num_blocks > INT32_MAX)
     return fail(KRILL_ERR_INVALID, "num_blocks out of range");
+  if (cfg.kv_format != KRILL_KV_INT8 && cfg.kv_format != KRILL_KV_BF16)
+    return fail(KRILL_ERR_INVALID, "kv_format must be KRILL_KV_INT8 or KRILL_KV_BF16");
+  if (cfg.kv_format == KRILL_KV_BF16) {
+    if (cfg.head_dim > 128) return fail(KRILL_ERR_INVALID, "bf16 pools support head_dim 64 and 128");
+    if (cfg.attn_impl == KRILL_ATTN_CUDA_CORE)
+      return fail(KRILL_ERR_INVALID, "bf16 pools use the tensor-core attention");
+    cfg.group_size = cfg.head_dim;  // no quantization groups
+  }
   int ring = 0;
   if (cfg.window > 0) {
     int64_t need = (int64_t)cfg.window - 1 + cfg.max_append;
@@ -854,7 +871,8 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   auto* p = new krill_pool_s();
   p->cfg = cfg;
   p->geom = make_geom(cfg.num_layers, cfg.num_kv_heads, cfg.num_q_heads, cfg.head_dim,
-                      cfg.group_size, ring, cfg.window, cfg.quant_variant);
+                      cfg.group_size, ring, cfg.window, cfg.quant_variant,
+                      cfg.kv_format == KRILL_KV_BF16 ? kFmtBf16 : kFmtInt8);
   p->device = device;
   p->host_only = device < 0;
   p->refcnt.assign((size_t)cfg.num_blocks, 0);
@@ -942,6 +960,14 @@ krill_status_t krill_pool_set_profiling(krill_pool_t p, int32_t enable) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
   p->profiling = enable != 0 && !p->host_only;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_kernel_count(krill_pool_t p, int64_t* kernels) {
+  if (!p || !kernels) return fail(KRILL_ERR_INVALID, "null argument");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  *kernels = p->kernels;
+  p->kernels = 0;
   return KRILL_OK;
 }
 
@@ -1144,6 +1170,7 @@ krill_status_t krill_seq_snapshot_quantized(krill_pool_t p, krill_seq_t h, int32
                                             void* value_zeros, void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "quantized snapshots need an int8 pool");
   TRY(require_device(p));
   DeviceGuard dg(p->device);
   Seq* s = nullptr;
@@ -1166,6 +1193,7 @@ krill_status_t krill_seq_snapshot_quantized(krill_pool_t p, krill_seq_t h, int32
   o.mode = 0;
   CUDA_TRY(launch_gather(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S,
                          o, (cudaStream_t)stream));
+  p->kernels += 1;
   return stage_release(slot, (cudaStream_t)stream);
 }
 
@@ -1173,6 +1201,7 @@ krill_status_t krill_seq_snapshot_dequantized(krill_pool_t p, krill_seq_t h, int
                                               void* keys, void* values, void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "quantized snapshots need an int8 pool");
   TRY(require_device(p));
   DeviceGuard dg(p->device);
   Seq* s = nullptr;
@@ -1190,6 +1219,7 @@ krill_status_t krill_seq_snapshot_dequantized(krill_pool_t p, krill_seq_t h, int
   o.mode = 1;
   CUDA_TRY(launch_gather(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S,
                          o, (cudaStream_t)stream));
+  p->kernels += 1;
   return stage_release(slot, (cudaStream_t)stream);
 }
 
@@ -1200,6 +1230,7 @@ krill_status_t krill_seq_restore_quantized(krill_pool_t p, krill_seq_t h, int32_
                                            const void* value_zeros, void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "quantized snapshots need an int8 pool");
   DeviceGuard dg(p->device);
   Seq* s = nullptr;
   TRY(seq_get(p, h, &s));
@@ -1222,6 +1253,7 @@ krill_status_t krill_stack_left_padded(krill_pool_t p, int32_t n_seqs, const kri
                                        void* value_zeros, void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "quantized snapshots need an int8 pool");
   TRY(require_device(p));
   DeviceGuard dg(p->device);
   if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
@@ -1259,6 +1291,7 @@ krill_status_t krill_stack_left_padded(krill_pool_t p, int32_t n_seqs, const kri
     o.rows_total = s_max;
     o.mode = 0;
     CUDA_TRY(launch_gather(g, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d), p0, S, o, st));
+    p->kernels += 1;
     TRY(stage_release(slot, st));
   }
   return KRILL_OK;
@@ -1272,6 +1305,7 @@ krill_status_t krill_scatter_back(krill_pool_t p, int32_t n_seqs, const krill_se
                                   void* stream) {
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "quantized snapshots need an int8 pool");
   TRY(require_device(p));
   DeviceGuard dg(p->device);
   if (layer < 0 || layer >= p->geom.L) return fail(KRILL_ERR_INVALID, "bad layer");
@@ -1675,6 +1709,8 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "compute call on a host-only pool");
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(q_dtype, "q"));
+  if (p->geom.fmt == kFmtBf16 && q_dtype != KRILL_DTYPE_BF16)
+    return fail(KRILL_ERR_INVALID, "attention over a bf16 pool takes a BF16 q");
   if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
     return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
   if (n_seqs <= 0 || lc <= 0) return fail(KRILL_ERR_INVALID, "nothing to attend");
@@ -1808,6 +1844,11 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   o.impl = p->cfg.attn_impl;
   o.device = p->device;
   return KRILL_OK;
+}
+
+void count_kernels(krill_pool_t p, int n) {
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  p->kernels += n;
 }
 
 }  // namespace krill

@@ -146,6 +146,8 @@ struct NoAllocPlan {
 krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                             int32_t lc, const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
                             float scale, uint8_t* buf, size_t buf_cap, NoAllocPlan* np);
+// Adds n to the pool's launched-kernel count (krill_pool_kernel_count).
+void count_kernels(krill_pool_t p, int n);
 // Sets the thread-local message returned by krill_last_error_string().
 krill_status_t set_error(krill_status_t code, const char* msg);
 

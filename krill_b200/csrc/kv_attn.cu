@@ -81,7 +81,7 @@ struct TCState {
 
 
 // Load this lane's Qᵀ fragments for one unit: q[head = r][16*(tig+4hh) + 0..15].
-template <int D>
+template <int D, int FMT = kFmtInt8>
 __device__ __forceinline__ void load_q(TCState<D>& st, const void* q, int q_dtype, int64_t row_elem,
                                        int g, int lane) {
   const int r = lane >> 2, tig = lane & 3;
@@ -94,7 +94,7 @@ __device__ __forceinline__ void load_q(TCState<D>& st, const void* q, int q_dtyp
       uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        if (q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
+        if (FMT == kFmtInt8 && q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
           __nv_bfloat162 bv = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
           float2 f = __bfloat1622float2(bv);
           w[i] = f2h2(f.x, f.y);
@@ -287,9 +287,125 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
 }
 
 
-template <int D, int NG, int NCW, int R, int NSTAGE>
+// Process one raw bf16 sub-block (the unquantized comparison format):
+// Sᵀ = K·Qᵀ on bf16 tensor cores (K and q are bf16, exact products), then the
+// same online softmax and Oᵀ += Vᵀ·Pᵀ in f16 with V converted exactly (V
+// magnitudes beyond the f16 range are not supported). Same fragment
+// permutation as tc_subblock, so q fragments and the state are shared.
+template <int D>
+__device__ __forceinline__ void tc_subblock_raw(const uint8_t* __restrict__ sb, TCState<D>& st,
+                                                int lane, float scale_log2, bool boundary, int pos0,
+                                                int t_lo, int t_hi) {
+  using SG = SubGeom<D, 1, kFmtBf16>;
+  constexpr int NU = SG::NU, TPT = SG::TPT;
+  const int r = lane >> 2, tig = lane & 3;
+  float s[NU][4];
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const int ta = TPT * (r >> 1) + 4 * u + (r & 1);
+    const int tb = ta + 2;  // same parity as ta
+    const int sw = ta & 1;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      // logical 16-byte chunks c, c+1 (d = 16 (tig + 4 hh) .. + 15) sit at
+      // physical chunks c ^ sw, (c + 1) ^ sw of their row
+      const int c = 2 * (tig + 4 * hh);
+      const uint8_t* ra = sb + (size_t)ta * D * 2;
+      const uint8_t* rb = sb + (size_t)tb * D * 2;
+      const uint4 a0 = *reinterpret_cast<const uint4*>(ra + ((c ^ sw) << 4));
+      const uint4 a1 = *reinterpret_cast<const uint4*>(ra + (((c + 1) ^ sw) << 4));
+      const uint4 b0 = *reinterpret_cast<const uint4*>(rb + ((c ^ sw) << 4));
+      const uint4 b1 = *reinterpret_cast<const uint4*>(rb + (((c + 1) ^ sw) << 4));
+      const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma16816_bf16(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], st.qf[hh][2 * k],
+                      st.qf[hh][2 * k + 1]);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[u][c] = acc[c] * scale_log2;
+    if (boundary) {
+      const int pa = pos0 + ta, pb = pos0 + tb;
+      if (pa < t_lo || pa >= t_hi) s[u][0] = s[u][1] = -INFINITY;
+      if (pb < t_lo || pb >= t_hi) s[u][2] = s[u][3] = -INFINITY;
+    }
+  }
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
+    mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(st.m[0], mx0), mn1 = fmaxf(st.m[1], mx1);
+  const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
+  const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+  const float al0 = exp2f(st.m[0] - b0), al1 = exp2f(st.m[1] - b1);
+  st.m[0] = mn0;
+  st.m[1] = mn1;
+  float ps0 = 0.f, ps1 = 0.f;
+  uint32_t pb[NU][2];
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const float p0 = exp2f(s[u][0] - b0), p1 = exp2f(s[u][1] - b1);
+    const float p2 = exp2f(s[u][2] - b0), p3 = exp2f(s[u][3] - b1);
+    ps0 += p0 + p2;
+    ps1 += p1 + p3;
+    pb[u][0] = movm_trans(f2h2(p0, p1));
+    pb[u][1] = movm_trans(f2h2(p2, p3));
+  }
+  st.l[0] = st.l[0] * al0 + ps0;
+  st.l[1] = st.l[1] * al1 + ps1;
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    st.o[mt][0] *= al0;
+    st.o[mt][1] *= al1;
+    st.o[mt][2] *= al0;
+    st.o[mt][3] *= al1;
+  }
+  // ---- V: rows d and d + 8, this lane's tokens TPT*tig .. +TPT-1 ----
+  const uint8_t* vt = sb + SG::VOFF;
+  constexpr int NW = TPT / 2;  // bf16 pairs per row
+  uint32_t vmask[NW];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    // invalid tokens read as zero so stale contents cannot inject non-finite values
+    const int pp = pos0 + TPT * tig + 2 * i;
+    vmask[i] = !boundary ? 0xffffffffu
+                         : (((pp >= t_lo && pp < t_hi) ? 0x0000ffffu : 0u) |
+                            ((pp + 1 >= t_lo && pp + 1 < t_hi) ? 0xffff0000u : 0u));
+  }
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d = 16 * mt + r;
+    uint32_t xv[NW], yv[NW];
+#pragma unroll
+    for (int q4 = 0; q4 < NW / 4; ++q4) {
+      const uint4 x = *reinterpret_cast<const uint4*>(vt + ((size_t)d * SG::T + TPT * tig) * 2 + 16 * q4);
+      const uint4 y = *reinterpret_cast<const uint4*>(vt + ((size_t)(d + 8) * SG::T + TPT * tig) * 2 + 16 * q4);
+      xv[4 * q4] = x.x; xv[4 * q4 + 1] = x.y; xv[4 * q4 + 2] = x.z; xv[4 * q4 + 3] = x.w;
+      yv[4 * q4] = y.x; yv[4 * q4 + 1] = y.y; yv[4 * q4 + 2] = y.z; yv[4 * q4 + 3] = y.w;
+    }
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      const uint32_t a0 = bf2h2(xv[2 * u] & vmask[2 * u]);
+      const uint32_t a1 = bf2h2(yv[2 * u] & vmask[2 * u]);
+      const uint32_t a2 = bf2h2(xv[2 * u + 1] & vmask[2 * u + 1]);
+      const uint32_t a3 = bf2h2(yv[2 * u + 1] & vmask[2 * u + 1]);
+      mma16816(st.o[mt], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+    }
+  }
+}
+
+template <int D, int NG, int NCW, int R, int NSTAGE, int FMT = kFmtInt8>
 struct AttnSmem {
-  static constexpr int SB = SubGeom<D, NG>::SB;
+  static constexpr int SB = SubGeom<D, NG, FMT>::SB;
   static constexpr int STAGE_BYTES = NSTAGE * SB;
   static constexpr int BAR_OFF = STAGE_BYTES;                 // 2*NSTAGE u64
   static constexpr int NV = D / 16 * 4 + 4;                   // per-lane state floats
@@ -301,10 +417,10 @@ struct AttnSmem {
 };
 
 // Number of 64-token stages that fit next to the rest of the shared memory.
-template <int D, int NG, int NCW, int R>
+template <int D, int NG, int NCW, int R, int FMT = kFmtInt8>
 constexpr int stages_for() {
-  constexpr int fixed = AttnSmem<D, NG, NCW, R, 0>::TOTAL;
-  constexpr int n = (232448 - fixed - 2 * 16 * 8) / SubGeom<D, NG>::SB;
+  constexpr int fixed = AttnSmem<D, NG, NCW, R, 0, FMT>::TOTAL;
+  constexpr int n = (232448 - fixed - 2 * 16 * 8) / SubGeom<D, NG, FMT>::SB;
   return n > 16 ? 16 : n;
 }
 
@@ -446,10 +562,10 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 constexpr int kProducerRegs = 40;
 constexpr int kConsumerRegs = 232;
 
-template <int D, int NG, int NCW, int R, int NSTAGE>
+template <int D, int NG, int NCW, int R, int NSTAGE, int FMT>
 __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
   static_assert(NCW == 8, "two consumer warpgroups");
-  using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
+  using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
   constexpr int SB = SM::SB;
   constexpr int HPR = NCW / R;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -489,7 +605,7 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
       const AttnUnit un = p.units[item.unit];
       const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
       const int n_sb = item.sb_end - item.sb_begin;
-      constexpr int SPB = SubGeom<D, NG>::SPB;
+      constexpr int SPB = SubGeom<D, NG, FMT>::SPB;
       const int b0 = item.sb_begin / SPB;
       const int nblk = (item.sb_end - 1) / SPB - b0 + 1;
       for (int rd = 0; rd < rounds; ++rd) {
@@ -546,18 +662,21 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
       const int h = item.h0 + rd * HPR + hr;
       reset_state(st);
       if (rr < n_sb)
-        load_q<D>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g, lane);
+        load_q<D, FMT>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g,
+                       lane);
       for (int k = rr; k < n_sb; k += R) {
         const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
         wait_tag(tags + stage, jj, cta_abort, p.err);
         mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
         const int j = item.sb_begin + k;
-        constexpr int T = SubGeom<D, NG>::T;
+        constexpr int T = SubGeom<D, NG, FMT>::T;
         const int pos0 = j * T;
         const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
         const uint8_t* sbp = stages + (size_t)stage * SB;
-        if (scales_small<D, NG>(sbp, lane))
+        if constexpr (FMT == kFmtBf16)
+          tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+        else if (scales_small<D, NG>(sbp, lane))
           tc_subblock<D, NG, true>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
         else
           tc_subblock<D, NG, false>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
@@ -619,10 +738,10 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
   }
 }
 
-template <int D, int NG, int NCW, int R>
+template <int D, int NG, int NCW, int R, int FMT>
 cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
-  constexpr int NSTAGE = stages_for<D, NG, NCW, R>();
-  using SM = AttnSmem<D, NG, NCW, R, NSTAGE>;
+  constexpr int NSTAGE = stages_for<D, NG, NCW, R, FMT>();
+  using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
   static_assert(NSTAGE >= 4, "too few stages");
   static_assert(SM::TOTAL <= 232448, "shared memory budget");
   // the shared-memory opt-in is a per-device attribute: set it once per device
@@ -635,30 +754,30 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
     // setmaxnreg.inc waits until the producer's released registers cover it:
     // refuse to launch a build whose register count would not balance
     cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE>);
+    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>);
     if (e != cudaSuccess) return e;
     if (fa.numRegs * (NCW + 4) * 32 < 128 * kProducerRegs + NCW * 32 * kConsumerRegs)
       return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE>,
+    e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
-  attn_tc_kernel<D, NG, NCW, R, NSTAGE><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
+  attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
   return cudaGetLastError();
 }
 
-template <int D, int NG, int NCW>
+template <int D, int NG, int NCW, int FMT = kFmtInt8>
 cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
   const int hpr = p.hg < NCW ? p.hg : NCW;
   if (NCW % hpr != 0 || p.hg % hpr != 0) return cudaErrorInvalidValue;
   cudaError_t e = cudaErrorInvalidValue;
   switch (NCW / hpr) {
-    case 1: e = launch_tc<D, NG, NCW, 1>(p, grid, stream); break;
-    case 2: e = launch_tc<D, NG, NCW, 2>(p, grid, stream); break;
-    case 4: e = launch_tc<D, NG, NCW, 4>(p, grid, stream); break;
+    case 1: e = launch_tc<D, NG, NCW, 1, FMT>(p, grid, stream); break;
+    case 2: e = launch_tc<D, NG, NCW, 2, FMT>(p, grid, stream); break;
+    case 4: e = launch_tc<D, NG, NCW, 4, FMT>(p, grid, stream); break;
     case 8:
-      if constexpr (NCW == 8) e = launch_tc<D, NG, NCW, 8>(p, grid, stream);
+      if constexpr (NCW == 8) e = launch_tc<D, NG, NCW, 8, FMT>(p, grid, stream);
       break;
     default: break;
   }
@@ -850,6 +969,11 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
     if (g.D == 128 && g.NG == 1) return launch_cc<128, 1>(p, grid, stream);
     if (g.D == 256 && g.NG == 4) return launch_cc<256, 4>(p, grid, stream);
     if (g.D == 256 && g.NG == 1) return launch_cc<256, 1>(p, grid, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (g.fmt == kFmtBf16) {  // raw bf16 pools: G = D
+    if (g.D == 64) return launch_tc_r<64, 1, 8, kFmtBf16>(p, grid, stream);
+    if (g.D == 128) return launch_tc_r<128, 1, 8, kFmtBf16>(p, grid, stream);
     return cudaErrorInvalidValue;
   }
   if (g.D == 64 && g.NG == 1) return launch_tc_r<64, 1, 8>(p, grid, stream);

@@ -14,6 +14,13 @@
 //                          contiguous bytes
 //     [2*T*D, ...)         K scales, K zeros, V scales, V zeros: [NG][T] f16 each
 // A sub-block is the unit one bulk (TMA) copy moves into shared memory.
+//
+// Raw bf16 pools (the unquantized comparison format) use the same blocks and
+// pages with sub-blocks of T = 32 tokens (64 at D = 64) of T * 4 * D bytes:
+//     [0, 2*T*D)           K rows, token-major bf16; the 16-byte chunks of odd
+//                          rows swapped pairwise (chunk ^ 1) so the decode
+//                          kernel's shared-memory reads are conflict free
+//     [2*T*D, 4*T*D)       V transposed: D rows of T bf16
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -24,6 +31,11 @@ namespace krill {
 constexpr int kBlockTokens = 256;
 // Tokens per sub-block for head dim D.
 __host__ __device__ constexpr int sub_tokens(int D) { return D >= 256 ? 32 : 64; }
+// Tokens per sub-block of a raw bf16 pool.
+__host__ __device__ constexpr int sub_tokens_raw(int D) { return D >= 128 ? 32 : 64; }
+// Pool formats.
+constexpr int kFmtInt8 = 0;
+constexpr int kFmtBf16 = 1;
 
 struct Geom {
   int L;        // layers in the pool
@@ -36,6 +48,7 @@ struct Geom {
   int ring;     // blocks in a windowed sequence's ring; 0 = full history
   int window;   // sliding window (tokens); 0 = full history
   int quant_variant;
+  int fmt;      // kFmtInt8 or kFmtBf16
   int subt;     // tokens per sub-block
   int spb;      // sub-blocks per 256-token block
   int64_t sb_bytes;
@@ -43,13 +56,14 @@ struct Geom {
   int64_t block_bytes;
 };
 
-inline Geom make_geom(int L, int Hkv, int Hq, int D, int G, int ring, int window, int qv) {
+inline Geom make_geom(int L, int Hkv, int Hq, int D, int G, int ring, int window, int qv,
+                      int fmt = kFmtInt8) {
   Geom g;
   g.L = L; g.Hkv = Hkv; g.Hq = Hq; g.g = Hq / Hkv; g.D = D; g.G = G; g.NG = D / G;
-  g.ring = ring; g.window = window; g.quant_variant = qv;
-  g.subt = sub_tokens(D);
+  g.ring = ring; g.window = window; g.quant_variant = qv; g.fmt = fmt;
+  g.subt = fmt == kFmtBf16 ? sub_tokens_raw(D) : sub_tokens(D);
   g.spb = kBlockTokens / g.subt;
-  g.sb_bytes = (int64_t)g.subt * (2 * D + 8 * g.NG);
+  g.sb_bytes = fmt == kFmtBf16 ? (int64_t)g.subt * 4 * D : (int64_t)g.subt * (2 * D + 8 * g.NG);
   g.page_bytes = g.sb_bytes * g.spb;
   g.block_bytes = g.page_bytes * L * Hkv;
   return g;
@@ -70,6 +84,15 @@ __host__ __device__ inline int64_t sb_kcode(int D, int t, int d) {
 }
 __host__ __device__ inline int64_t sb_vcode(int D, int t, int d) {
   return sb_voff(D) + (int64_t)d * sub_tokens(D) + t;
+}
+
+// Raw bf16 sub-block of T tokens: byte offsets of K (token t, element d) and
+// V (element d, token t).
+__host__ __device__ inline int64_t raw_koff(int D, int t, int d) {
+  return ((int64_t)t * D + (((d >> 3) ^ (t & 1)) << 3) + (d & 7)) * 2;
+}
+__host__ __device__ inline int64_t raw_voff(int D, int T, int t, int d) {
+  return ((int64_t)T * D + (int64_t)d * T + t) * 2;
 }
 
 // Error flag bits written by kernels (pool-owned int, read + cleared by host).

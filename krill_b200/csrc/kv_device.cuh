@@ -70,6 +70,13 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma16816_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
@@ -98,17 +105,17 @@ __device__ __forceinline__ uint32_t neg1024(uint32_t s2) {
   return h2u(__hmul2_rn(u2h(s2), u2h(0xE400E400u)));  // -1024 in f16
 }
 
-template <int D, int NG>
+template <int D, int NG, int FMT = kFmtInt8>
 struct SubGeom {
   static constexpr int G = D / NG;
-  static constexpr int T = sub_tokens(D);   // tokens per sub-block
+  static constexpr int T = FMT == kFmtBf16 ? sub_tokens_raw(D) : sub_tokens(D);
   static constexpr int SPB = kBlockTokens / T;
   static constexpr int NU = T / 16;          // 16-token m-tiles per sub-block
   static constexpr int TPT = T / 4;          // tokens per lane chunk (V rows)
-  static constexpr int SB = T * (2 * D + 8 * NG);
-  static constexpr int VOFF = T * D;
-  static constexpr int META = 2 * T * D;
-  // meta array a, group gi, token t -> byte offset
+  static constexpr int SB = FMT == kFmtBf16 ? T * 4 * D : T * (2 * D + 8 * NG);
+  static constexpr int VOFF = FMT == kFmtBf16 ? T * D * 2 : T * D;
+  static constexpr int META = 2 * T * D;     // int8 only
+  // meta array a, group gi, token t -> byte offset (int8 only)
   static __device__ __forceinline__ int meta(int a, int gi, int t) {
     return META + ((a * NG + gi) * T + t) * 2;
   }
@@ -116,6 +123,10 @@ struct SubGeom {
 
 __device__ __forceinline__ uint32_t f2h2(float lo, float hi) {
   return h2u(__floats2half2_rn(lo, hi));
+}
+// bf16 pair -> f16 pair; exact for magnitudes in the f16 normal range
+__device__ __forceinline__ uint32_t bf2h2(uint32_t w) {
+  return f2h2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
 __device__ __forceinline__ void store_out(void* out, int dtype, int64_t i, float v) {

@@ -80,6 +80,7 @@ extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int3
     ap.split_units = reinterpret_cast<const int32_t*>(base + np.su_off);
     ap.partials = reinterpret_cast<float*>(base + np.partials_off);
     e = launch_attention(np.geom, ap, np.grid, np.impl, s);
+    if (e == cudaSuccess) count_kernels(pool, 1 + (ap.n_split_units > 0 ? 1 : 0));
     if (e != cudaSuccess) rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
   } while (false);
   if (prev >= 0 && prev != np.device) cudaSetDevice(prev);

@@ -130,6 +130,35 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
   }
 }
 
+// Raw bf16 pools (the unquantized comparison format): copy one token's K row
+// and V column; one warp per (layer, seq, head, token), bf16 inputs.
+__global__ void append_raw_kernel(uint8_t* __restrict__ pool, Geom geom,
+                                  const AppendDst* __restrict__ dst, int layer_begin,
+                                  int layer_count, int n_seqs, int n_new,
+                                  const uint16_t* __restrict__ k, const uint16_t* __restrict__ v) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
+  if (w >= total) return;
+  const int D = geom.D;
+  const int tok = (int)(w % n_new);
+  const int64_t rest = w / n_new;
+  const int h = (int)(rest % geom.Hkv);
+  const int64_t ls = rest / geom.Hkv;  // li * n_seqs + si
+  const int li = (int)(ls / n_seqs);
+  const AppendDst d = dst[ls * n_new + tok];
+  const int slot = d.pos & (kBlockTokens - 1);
+  const int t = slot % geom.subt;
+  uint8_t* sb = pool + (((int64_t)d.block * geom.L + (layer_begin + li)) * geom.Hkv + h) * geom.page_bytes +
+                (int64_t)(slot / geom.subt) * geom.sb_bytes;
+  const int64_t elem_off = w * D;
+  for (int c = lane; c < D / 8; c += 32)
+    *reinterpret_cast<uint4*>(sb + raw_koff(D, t, 8 * c)) =
+        *reinterpret_cast<const uint4*>(k + elem_off + 8 * c);
+  for (int e = lane; e < D; e += 32)
+    *reinterpret_cast<uint16_t*>(sb + raw_voff(D, geom.subt, t, e)) = v[elem_off + e];
+}
+
 // Gather rows [p0, p0+S) of one (seq, layer) into the reference snapshot
 // layout; one thread per (head, row, element-of-8). mode 0: raw codes + meta;
 // mode 1: dequantized f16 (keys/values are f16 outputs).
@@ -242,6 +271,13 @@ cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, 
   if (warps == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  if (g.fmt == kFmtBf16) {
+    if (dtype != 1) return cudaErrorInvalidValue;
+    append_raw_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new,
+        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v));
+    return cudaGetLastError();
+  }
   const int epl = g.D / 32;
   const int lpg = g.G / epl;
 #define KRILL_APPEND(E, P)                                                                    \

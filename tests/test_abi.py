@@ -129,3 +129,23 @@ def test_prefix_key_matches_oracle():
         toks = [int(t) for t in rng.integers(-2**40, 2**40, size=n)]
         for media in [None, "", "abc"]:
             assert kb.prefix_key(toks, "model-x", media) == oracle.prefix_key(toks, "model-x", media)
+
+
+def test_bf16_pool_geometry_and_limits():
+    # raw bf16 pools: 256 tokens x (2 x D x 2 bytes) per (layer, head), no groups
+    p = kb.KVPool(32, 8, 32, 128, num_blocks=4, device=-1, kv_format=kb.KV_BF16)
+    assert p.block_bytes == 32 * 8 * 256 * 4 * 128
+    assert p.group_size == 128
+    s = p.create_sequence()
+    arr = (C.c_uint64 * 1)(s.handle)
+    st = L.lib.krill_append_quantize(p.handle, 1, arr, 0, 1, 1, None, None, L.DTYPE_F16, None)
+    assert st == L.KRILL_ERR_INVALID and "BF16" in L.last_error()
+    L.check(L.lib.krill_append_quantize(p.handle, 1, arr, 0, 32, 3, None, None, L.DTYPE_BF16, None))
+    st = L.lib.krill_decode_attention(p.handle, 1, arr, 0, 1, None, L.DTYPE_F16, None, 2, 1.0, None)
+    assert st == L.KRILL_ERR_INVALID and "BF16 q" in L.last_error()
+    for kw in [dict(head_dim=256), dict(attn_impl=L.ATTN_CUDA_CORE), dict(kv_format=7)]:
+        args = dict(num_layers=2, num_kv_heads=8, num_q_heads=32, head_dim=128, num_blocks=4,
+                    kv_format=kb.KV_BF16)
+        args.update(kw)
+        with pytest.raises(kb.KrillError):
+            kb.KVPool(device=-1, **args)
