@@ -88,6 +88,8 @@ struct StageSlot {
 constexpr int kStageSlots = 8;
 
 // Decode-attention planner buffers, reused across calls.
+__global__ void or_flag_kernel(int* dst, const int* src) { *dst |= *src; }
+
 struct Plan {
   std::vector<Seq*> sv;
   std::vector<AttnUnit> units;
@@ -380,7 +382,7 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
     TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
     CUDA_TRY(timed_launch(p, 1, stream, [&] {
       return launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
-                           n_seqs, n_new, k, v, dtype, stream);
+                           n_seqs, n_new, k, v, dtype, p->d_err + 1, stream);
     }));
     p->kernels += 1;
     TRY(stage_release(slot, stream));
@@ -746,6 +748,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.partials = p->d_partials;
   ap.err = p->d_err;
+  ap.large_scale = p->d_err + 1;
   if (sh_grid > 0) {
     ap.sh_items = reinterpret_cast<const ShItem*>(slot->d + sh_off);
     ap.sh_cta_off = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes);
@@ -803,7 +806,7 @@ krill_status_t do_restore(krill_pool_t p, Seq& s, int32_t layer, int64_t rows, i
       StageSlot* slot;
       TRY(upload_bt(p, s, stream, &slot));
       CUDA_TRY(launch_scatter(p->geom, p->d_pool, layer, reinterpret_cast<const int32_t*>(slot->d),
-                              p0, rows, in, stream));
+                              p0, rows, in, p->d_err + 1, stream));
       p->kernels += 1;
       TRY(stage_release(slot, stream));
     }
@@ -884,8 +887,9 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     size_t bytes = (size_t)cfg.num_blocks * (size_t)p->geom.block_bytes;
     if (e == cudaSuccess) e = cudaMalloc(&p->d_pool, bytes);
     if (e == cudaSuccess) e = cudaMemset(p->d_pool, 0, bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, sizeof(int));
+    // [0] error flag, [1] large-scale flag (a stored scale with |s| >= 64)
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, 4 * sizeof(int));
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) {
       krill_status_t code = (e == cudaErrorMemoryAllocation) ? KRILL_ERR_OOM : KRILL_ERR_CUDA;
@@ -1667,6 +1671,20 @@ krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
         return fail(KRILL_ERR_PEER, "cudaMemcpyPeerAsync: %s", cudaGetErrorString(ce));
       }
     }
+    // the copied blocks may hold large scales: fold the source pool's flag
+    // into this pool's, in stream order (peer copy into a scratch word, then OR)
+    cudaError_t ce = cudaMemcpyPeerAsync(dp->d_err + 2, dp->device, sp->d_err + 1, sp->device,
+                                         sizeof(int), (cudaStream_t)stream);
+    if (ce == cudaSuccess) {
+      or_flag_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(dp->d_err + 1, dp->d_err + 2);
+      ce = cudaGetLastError();
+    }
+    if (ce != cudaSuccess) {
+      for (int32_t bb : e->blocks) block_unref(dp, bb);
+      delete e;
+      return fail(KRILL_ERR_PEER, "flag copy: %s", cudaGetErrorString(ce));
+    }
+    dp->kernels += 1;
   }
   e->key = se->key;
   e->tokens = se->tokens;
@@ -1839,6 +1857,7 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.out_dtype = out_dtype;
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.err = p->d_err;
+  ap.large_scale = p->d_err + 1;
   o.geom = g;
   o.grid = grid;
   o.impl = p->cfg.attn_impl;

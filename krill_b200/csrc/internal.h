@@ -104,6 +104,7 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   float* partials;   // [splits * Hkv][16 + 8*D]
   int* err;
+  const int* large_scale;  // non-zero once the pool holds a scale with |s| >= 64
   // cascade items (sh_grid = 0: none)
   const ShItem* sh_items;
   const int32_t* sh_cta_off;  // [sh_grid + 1]
@@ -112,13 +113,15 @@ struct AttnParams {
   int n_pslots;               // prefix record slots per cascaded unit
 };
 
+// Kernels that store scales raise *large_scale when one has |s| >= 64 (the
+// one-fma dequantization is exact only below that).
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
                           int layer_count, int n_seqs, int n_new, const void* k, const void* v,
-                          int dtype, cudaStream_t stream);
+                          int dtype, int* large_scale, cudaStream_t stream);
 cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const int32_t* d_bt,
                           int64_t p0, int64_t S, const GatherOut& out, cudaStream_t stream);
 cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
-                           int64_t S, const ScatterIn& in, cudaStream_t stream);
+                           int64_t S, const ScatterIn& in, int* large_scale, cudaStream_t stream);
 // grid = number of persistent CTAs (cta_off has grid + 1 entries). Launches
 // the cascade kernel when p.sh_grid > 0, then the decode kernel and, when
 // some unit is split, the combine kernel.

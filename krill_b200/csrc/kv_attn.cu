@@ -562,6 +562,110 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 constexpr int kProducerRegs = 40;
 constexpr int kConsumerRegs = 232;
 
+// Consumer warps of attn_tc_kernel. FAST selects the one-fma dequantization,
+// exact only while every scale in the pool is below 64 in magnitude; the
+// kernel picks one specialization per launch from the pool's large-scale flag
+// (set by the kernels that store scales), so the hot loop carries one path.
+template <int D, int NG, int NCW, int R, int NSTAGE, int FMT, bool FAST>
+__device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem, uint8_t* stages,
+                                             uint32_t bar_base, volatile int* cta_abort,
+                                             volatile uint32_t* tags, int warp, int lane, int it0,
+                                             int it1, int rounds) {
+  using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
+  constexpr int SB = SM::SB;
+  constexpr int HPR = NCW / R;
+  const int hr = warp / R, rr = warp % R;
+  TCState<D> st;
+  uint32_t J = 0;
+  AttnItem item_next{};
+  AttnUnit un_next{};
+  if (it0 < it1) {
+    item_next = p.items[it0];
+    un_next = p.units[item_next.unit];
+  }
+  for (int it = it0; it < it1; ++it) {
+    const AttnItem item = item_next;
+    const AttnUnit un = un_next;
+    if (it + 1 < it1) item_next = p.items[it + 1];
+    const int n_sb = item.sb_end - item.sb_begin;
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int h = item.h0 + rd * HPR + hr;
+      reset_state(st);
+      if (rr < n_sb)
+        load_q<D, FMT>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g,
+                       lane);
+      for (int k = rr; k < n_sb; k += R) {
+        const uint32_t jj = J + (uint32_t)k * HPR + hr;
+        const uint32_t stage = jj % NSTAGE;
+        wait_tag(tags + stage, jj, cta_abort, p.err);
+        mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
+        const int j = item.sb_begin + k;
+        constexpr int T = SubGeom<D, NG, FMT>::T;
+        const int pos0 = j * T;
+        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
+        const uint8_t* sbp = stages + (size_t)stage * SB;
+        if constexpr (FMT == kFmtBf16)
+          tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+        else
+          tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
+      }
+      J += (uint32_t)n_sb * HPR;
+      if (rd == rounds - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
+
+      float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+      }
+      if constexpr (R > 1) {
+        // merge the R warps of this head through a lane-major buffer
+        float* cb = reinterpret_cast<float*>(smem + SM::CB_OFF);
+        const int nbar = 1 + hr;
+        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");  // buffer free
+        if (rr != 0) {
+          float* mine = cb + (size_t)(hr * (R - 1) + rr - 1) * SM::NV * 32;
+#pragma unroll
+          for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) mine[(mt * 4 + c) * 32 + lane] = st.o[mt][c];
+          mine[(D / 4 + 0) * 32 + lane] = st.m[0];
+          mine[(D / 4 + 1) * 32 + lane] = st.m[1];
+          mine[(D / 4 + 2) * 32 + lane] = l0;
+          mine[(D / 4 + 3) * 32 + lane] = l1;
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");
+        if (rr == 0) {
+#pragma unroll
+          for (int w = 1; w < R; ++w) {
+            const float* o = cb + (size_t)(hr * (R - 1) + w - 1) * SM::NV * 32;
+            const float m0 = o[(D / 4 + 0) * 32 + lane], m1 = o[(D / 4 + 1) * 32 + lane];
+            const float M0 = fmaxf(st.m[0], m0), M1 = fmaxf(st.m[1], m1);
+            const float a0 = (st.m[0] == -INFINITY) ? 0.f : exp2f(st.m[0] - M0);
+            const float a1 = (st.m[1] == -INFINITY) ? 0.f : exp2f(st.m[1] - M1);
+            const float b0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+            const float b1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+            l0 = l0 * a0 + o[(D / 4 + 2) * 32 + lane] * b0;
+            l1 = l1 * a1 + o[(D / 4 + 3) * 32 + lane] * b1;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+              st.o[mt][0] = st.o[mt][0] * a0 + o[(mt * 4 + 0) * 32 + lane] * b0;
+              st.o[mt][1] = st.o[mt][1] * a1 + o[(mt * 4 + 1) * 32 + lane] * b1;
+              st.o[mt][2] = st.o[mt][2] * a0 + o[(mt * 4 + 2) * 32 + lane] * b0;
+              st.o[mt][3] = st.o[mt][3] * a1 + o[(mt * 4 + 3) * 32 + lane] * b1;
+            }
+            st.m[0] = M0;
+            st.m[1] = M1;
+          }
+        }
+      }
+      if (rr == 0) finish_head<D>(p, st, l0, l1, un, item, h, lane);
+    }
+  }
+}
+
 template <int D, int NG, int NCW, int R, int NSTAGE, int FMT>
 __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
   static_assert(NCW == 8, "two consumer warpgroups");
@@ -644,98 +748,12 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
 
   // ---------------- consumers ----------------
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
-  const int hr = warp / R, rr = warp % R;
-  TCState<D> st;
-  uint32_t J = 0;
-  AttnItem item_next{};
-  AttnUnit un_next{};
-  if (it0 < it1) {
-    item_next = p.items[it0];
-    un_next = p.units[item_next.unit];
-  }
-  for (int it = it0; it < it1; ++it) {
-    const AttnItem item = item_next;
-    const AttnUnit un = un_next;
-    if (it + 1 < it1) item_next = p.items[it + 1];
-    const int n_sb = item.sb_end - item.sb_begin;
-    for (int rd = 0; rd < rounds; ++rd) {
-      const int h = item.h0 + rd * HPR + hr;
-      reset_state(st);
-      if (rr < n_sb)
-        load_q<D, FMT>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g,
-                       lane);
-      for (int k = rr; k < n_sb; k += R) {
-        const uint32_t jj = J + (uint32_t)k * HPR + hr;
-        const uint32_t stage = jj % NSTAGE;
-        wait_tag(tags + stage, jj, cta_abort, p.err);
-        mbar_wait(bar_base + 8 * stage, (jj / NSTAGE) & 1, cta_abort, p.err);
-        const int j = item.sb_begin + k;
-        constexpr int T = SubGeom<D, NG, FMT>::T;
-        const int pos0 = j * T;
-        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
-        const uint8_t* sbp = stages + (size_t)stage * SB;
-        if constexpr (FMT == kFmtBf16)
-          tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-        else if (scales_small<D, NG>(sbp, lane))
-          tc_subblock<D, NG, true>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-        else
-          tc_subblock<D, NG, false>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
-      }
-      J += (uint32_t)n_sb * HPR;
-      if (rd == rounds - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
-
-      float l0 = st.l[0], l1 = st.l[1];
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-      }
-      if constexpr (R > 1) {
-        // merge the R warps of this head through a lane-major buffer
-        float* cb = reinterpret_cast<float*>(smem + SM::CB_OFF);
-        const int nbar = 1 + hr;
-        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");  // buffer free
-        if (rr != 0) {
-          float* mine = cb + (size_t)(hr * (R - 1) + rr - 1) * SM::NV * 32;
-#pragma unroll
-          for (int mt = 0; mt < D / 16; ++mt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) mine[(mt * 4 + c) * 32 + lane] = st.o[mt][c];
-          mine[(D / 4 + 0) * 32 + lane] = st.m[0];
-          mine[(D / 4 + 1) * 32 + lane] = st.m[1];
-          mine[(D / 4 + 2) * 32 + lane] = l0;
-          mine[(D / 4 + 3) * 32 + lane] = l1;
-        }
-        asm volatile("bar.sync %0, %1;" ::"r"(nbar), "r"(R * 32) : "memory");
-        if (rr == 0) {
-#pragma unroll
-          for (int w = 1; w < R; ++w) {
-            const float* o = cb + (size_t)(hr * (R - 1) + w - 1) * SM::NV * 32;
-            const float m0 = o[(D / 4 + 0) * 32 + lane], m1 = o[(D / 4 + 1) * 32 + lane];
-            const float M0 = fmaxf(st.m[0], m0), M1 = fmaxf(st.m[1], m1);
-            const float a0 = (st.m[0] == -INFINITY) ? 0.f : exp2f(st.m[0] - M0);
-            const float a1 = (st.m[1] == -INFINITY) ? 0.f : exp2f(st.m[1] - M1);
-            const float b0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
-            const float b1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
-            l0 = l0 * a0 + o[(D / 4 + 2) * 32 + lane] * b0;
-            l1 = l1 * a1 + o[(D / 4 + 3) * 32 + lane] * b1;
-#pragma unroll
-            for (int mt = 0; mt < D / 16; ++mt) {
-              st.o[mt][0] = st.o[mt][0] * a0 + o[(mt * 4 + 0) * 32 + lane] * b0;
-              st.o[mt][1] = st.o[mt][1] * a1 + o[(mt * 4 + 1) * 32 + lane] * b1;
-              st.o[mt][2] = st.o[mt][2] * a0 + o[(mt * 4 + 2) * 32 + lane] * b0;
-              st.o[mt][3] = st.o[mt][3] * a1 + o[(mt * 4 + 3) * 32 + lane] * b1;
-            }
-            st.m[0] = M0;
-            st.m[1] = M1;
-          }
-        }
-      }
-      if (rr == 0) finish_head<D>(p, st, l0, l1, un, item, h, lane);
-    }
-  }
+  if (FMT == kFmtInt8 && *reinterpret_cast<volatile const int*>(p.large_scale) != 0)
+    attn_consume<D, NG, NCW, R, NSTAGE, FMT, false>(p, smem, stages, bar_base, cta_abort, tags, warp,
+                                                    lane, it0, it1, rounds);
+  else
+    attn_consume<D, NG, NCW, R, NSTAGE, FMT, true>(p, smem, stages, bar_base, cta_abort, tags, warp,
+                                                   lane, it0, it1, rounds);
 }
 
 template <int D, int NG, int NCW, int R, int FMT>

@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
                                                               int layer_begin, int layer_count,
                                                               int n_seqs, int n_new,
                                                               const void* __restrict__ k,
-                                                              const void* __restrict__ v, int dtype) {
+                                                              const void* __restrict__ v, int dtype,
+                                                              int* __restrict__ large_scale) {
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 1, gi, t)) = zk;
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = sv;
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = zv;
+    if ((sk & 0x7fffu) >= 0x5400u || (sv & 0x7fffu) >= 0x5400u) atomicOr(large_scale, 1);
   }
 }
 
@@ -226,7 +228,8 @@ __global__ void gather_kernel(const uint8_t* __restrict__ pool, Geom geom, int l
 // Scatter rows from the snapshot layout into a sequence's pages (restore,
 // scatter-back). Row i of the input (at in.row_off + i) lands at position p0+i.
 __global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
-                               const int32_t* __restrict__ bt, int64_t p0, int64_t S, ScatterIn in) {
+                               const int32_t* __restrict__ bt, int64_t p0, int64_t S, ScatterIn in,
+                               int* __restrict__ large_scale) {
   const int D = geom.D, NG = geom.NG, G = geom.G;
   const int per_row = D / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -259,6 +262,8 @@ __global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 1, gi, t)) = in.key_zeros[m];
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = in.value_scales[m];
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = in.value_zeros[m];
+    if ((in.key_scales[m] & 0x7fffu) >= 0x5400u || (in.value_scales[m] & 0x7fffu) >= 0x5400u)
+      atomicOr(large_scale, 1);
   }
 }
 
@@ -266,7 +271,7 @@ __global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
 
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
                           int layer_count, int n_seqs, int n_new, const void* k, const void* v,
-                          int dtype, cudaStream_t stream) {
+                          int dtype, int* large_scale, cudaStream_t stream) {
   const int64_t warps = (int64_t)layer_count * n_seqs * g.Hkv * n_new;
   if (warps == 0) return cudaSuccess;
   const int threads = 256;
@@ -283,7 +288,7 @@ cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, 
 #define KRILL_APPEND(E, P)                                                                    \
   if (epl == E && lpg == P) {                                                                  \
     append_quantize_kernel<E, P><<<(unsigned)blocks, threads, 0, stream>>>(                    \
-        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype);                 \
+        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype, large_scale);    \
     return cudaGetLastError();                                                                 \
   }
   KRILL_APPEND(2, 32)   // D=64,  G=64
@@ -307,12 +312,12 @@ cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const i
 }
 
 cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,
-                           int64_t S, const ScatterIn& in, cudaStream_t stream) {
+                           int64_t S, const ScatterIn& in, int* large_scale, cudaStream_t stream) {
   const int64_t total = (int64_t)g.Hkv * S * (g.D / 8);
   if (total == 0) return cudaSuccess;
   const int threads = 256;
-  scatter_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, stream>>>(pool, g, layer,
-                                                                                      d_bt, p0, S, in);
+  scatter_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, stream>>>(
+      pool, g, layer, d_bt, p0, S, in, large_scale);
   return cudaGetLastError();
 }
 

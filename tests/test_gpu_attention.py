@@ -185,3 +185,46 @@ def test_attention_cuda_core_variant(D, G, hq, hkv, dtype, scale):
 
 def test_attention_cuda_core_windowed():
     run_case(256, 64, 8, 4, F16, [10, 300, 700], 1.0, window=128, impl=kb.ATTN_CUDA_CORE, steps=2)
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+def test_attention_large_scales(dtype):
+    """Groups whose range exceeds 64 * 255 store scales >= 64, where the
+    one-fma dequantization would overflow: the pool's large-scale flag must
+    route the launch to the exact two-rounding path. K stays N(0, 1); a tenth
+    of the tokens carry V of magnitude up to 12000. Tolerance relative to the
+    output magnitude (f16 P weights on values of that size)."""
+    rng = np.random.default_rng(7)
+    D, G, hq, hkv, layers = 128, 64, 32, 8, 1
+    scale = 1 / math.sqrt(D)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=16, group_size=G)
+    lengths = [300, 77]
+    seqs, K, V = [], [], []
+    for L in lengths:
+        s = pool.create_sequence()
+        k = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        vf = rng.standard_normal((layers, hkv, L, D))
+        big = rng.random(L) < 0.1
+        vf[:, :, big, :] = rng.uniform(-12000, 12000, size=vf[:, :, big, :].shape)
+        v = to_bits(vf, dtype)
+        prefill(pool, s, k, v, dtype)
+        seqs.append(s)
+        K.append(k)
+        V.append(v)
+    _, sv, _ = oracle.quantize(V[0][0], dtype, G)
+    assert (oracle.bits_to_f64(sv, F16) >= 64).any()  # the case under test
+    n = len(seqs)
+    qb = to_bits(kv_values(rng, (layers, n, hq, D)), dtype)
+    out = torch.empty((layers, n, hq, D), dtype=torch.float32, device="cuda")
+    kb.decode_attention(pool, seqs, 0, dev_bits(qb, dtype), out, scale)
+    torch.cuda.synchronize()
+    assert pool.device_error() == 0
+    got = out.cpu().numpy().astype(np.float64)
+    for i in range(n):
+        ck, sk, zk = oracle.quantize(K[i][0], dtype, G)
+        cv, sv, zv = oracle.quantize(V[i][0], dtype, G)
+        ref = oracle.reference_attention(ck, sk, zk, cv, sv, zv, qb[0, i], dtype, G, scale)
+        err = np.abs(got[0, i] - ref).max()
+        assert np.isfinite(got[0, i]).all()
+        assert err <= ATOL * max(1.0, np.abs(ref).max()), f"seq {i}: max err {err:.3e}"
+    pool.close()
