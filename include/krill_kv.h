@@ -328,7 +328,24 @@ krill_status_t krill_prefix_entry_release(krill_prefix_t pc, krill_prefix_entry_
 krill_status_t krill_seq_fork_prefix(krill_prefix_t pc, krill_prefix_entry_t entry, int64_t keep,
                                      krill_seq_t* out);
 /* clear() (PrefixCache.swift:403-414) and memoryCount (:417-420). */
+/* clear(): drops the memory entries and, with the disk tier on, its files
+ * (PrefixCache.swift:403-415). */
 krill_status_t krill_prefix_clear(krill_prefix_t pc);
+/* Disk tier (PrefixCache.swift:496-501, 553-695), off by default. budget_bytes
+ * 0 disables it, < 0 is unbounded, > 0 evicts least-recently-used files (by
+ * modification time) down to 90 % of the budget after a write. Each stored
+ * entry is written behind the caller, by a worker thread, as
+ * `<cache_dir>/<key %016llx>.q8.safetensors` with the reference's tensors
+ * layer_{i}_qk / _qv (U8 [1, Hkv, S, D]) and _ks / _kz / _vs / _vz
+ * (F16 [1, Hkv, S, D/G]). krill_prefix_lookup probes memory, then disk, at
+ * every scan length; a disk hit is read into new pool blocks and joins the
+ * memory tier without tokens (longest-prefix matching skips it). Device int8
+ * pools with full history only. */
+krill_status_t krill_prefix_set_disk(krill_prefix_t pc, const char* cache_dir, int64_t budget_bytes);
+/* waitForDiskWrites(): blocks until every queued write finished. */
+krill_status_t krill_prefix_wait_disk(krill_prefix_t pc);
+/* diskCount: number of entry files in the cache directory. */
+krill_status_t krill_prefix_disk_count(krill_prefix_t pc, int32_t* count);
 krill_status_t krill_prefix_memory_count(krill_prefix_t pc, int32_t* count);
 /* FNV-1a cache key (PrefixCache.swift:513-532) for tools and tests. */
 uint64_t krill_prefix_key(const int64_t* tokens, int64_t n_tokens, const char* model_id,

@@ -111,6 +111,9 @@ _SIGS = {
     "krill_prefix_entry_release": (i32, [vp, vp]),
     "krill_seq_fork_prefix": (i32, [vp, vp, i64, P_u64]),
     "krill_prefix_clear": (i32, [vp]),
+    "krill_prefix_set_disk": (i32, [vp, cstr, i64]),
+    "krill_prefix_wait_disk": (i32, [vp]),
+    "krill_prefix_disk_count": (i32, [vp, P_i32]),
     "krill_prefix_memory_count": (i32, [vp, P_i32]),
     "krill_prefix_key": (u64, [P_i64, i64, cstr, cstr, i32]),
     "krill_prefix_peer_fetch": (i32, [vp, vp, vp, vp, C.POINTER(vp)]),

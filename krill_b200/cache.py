@@ -409,13 +409,33 @@ class QuantizedPrefixCacheHit:
 
 
 class PrefixCache:
-    """PrefixCache (PrefixCache.swift:15) over one pool; int8 entries only."""
+    """PrefixCache (PrefixCache.swift:15) over one pool; int8 entries only.
 
-    def __init__(self, pool: KVPool, max_memory_entries: int = 8, min_prefix_length: int = 8):
+    ``cache_dir`` + ``disk_budget_bytes`` enable the persistent tier
+    (PrefixCache.swift:496-695): 0 disables it (the default here; the
+    reference defaults to 2 GB under ~/.krill/cache), a negative budget is
+    unbounded."""
+
+    def __init__(self, pool: KVPool, max_memory_entries: int = 8, min_prefix_length: int = 8,
+                 cache_dir: Optional[str] = None, disk_budget_bytes: int = 0):
         h = C.c_void_p()
         check(L.lib.krill_prefix_create(pool.handle, max_memory_entries, min_prefix_length, C.byref(h)))
         self.handle = h
         self.pool = pool
+        if cache_dir is not None and disk_budget_bytes != 0:
+            self.set_disk(cache_dir, disk_budget_bytes)
+
+    def set_disk(self, cache_dir: str, budget_bytes: int):
+        check(L.lib.krill_prefix_set_disk(self.handle, _enc(cache_dir), budget_bytes))
+
+    def wait_for_disk_writes(self):
+        check(L.lib.krill_prefix_wait_disk(self.handle))
+
+    @property
+    def disk_count(self) -> int:
+        v = C.c_int32()
+        check(L.lib.krill_prefix_disk_count(self.handle, C.byref(v)))
+        return v.value
 
     def close(self):
         if self.handle:

@@ -10,13 +10,18 @@
 // forked sequences share them without copies.
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
+#include <filesystem>
 #include <list>
+#include <map>
 #include <mutex>
 #include <queue>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -1366,6 +1371,8 @@ struct krill_prefix_entry_s {
   int64_t n_tokens = 0;
 };
 
+struct DiskTier;
+
 struct krill_prefix_s {
   krill_pool_t pool = nullptr;
   int max_entries = 8;
@@ -1373,6 +1380,7 @@ struct krill_prefix_s {
   std::unordered_map<uint64_t, krill_prefix_entry_t> map;
   std::list<uint64_t> lru;  // front = least recently used
   std::mutex mu;
+  DiskTier* disk = nullptr;  // persistent tier, null when disabled
 };
 
 namespace {
@@ -1427,6 +1435,476 @@ void evict_locked(krill_prefix_t pc, uint64_t key) {
   entry_unref(pc, e);
 }
 
+// ---------------------------------------------------------------------
+// Disk tier (PrefixCache.swift:496-501 file naming, :553-581 load, :583-648
+// write + byte budget, :650-695 LRU eviction to a 90 % low-water mark). An
+// int8 entry is one safetensors file `<key %016llx>.q8.safetensors` holding,
+// per layer i, `layer_{i}_qk` / `_qv` (U8 [1, Hkv, S, D]) and `_ks` / `_kz` /
+// `_vs` / `_vz` (F16 [1, Hkv, S, D/G]): the reference's names, dtypes and
+// shapes (G = D is the reference's one-scale-per-head layout). Writes run on a
+// per-cache worker thread (the reference's serial disk queue); a disk hit is
+// read back into pool blocks through the restore kernel. Disk-loaded entries
+// carry no tokens, so longest-prefix matching skips them, as in the reference.
+struct StTensor {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  int64_t begin = 0, end = 0;
+};
+
+// Minimal JSON reader for a safetensors header: an object of tensor records
+// ({"dtype", "shape", "data_offsets"}) plus an optional "__metadata__".
+struct JsonCursor {
+  const std::string& s;
+  size_t i = 0;
+  void ws() {
+    while (i < s.size() && (s[i] == ' ' || s[i] == '\n' || s[i] == '\r' || s[i] == '\t')) ++i;
+  }
+  bool eat(char c) {
+    ws();
+    if (i < s.size() && s[i] == c) {
+      ++i;
+      return true;
+    }
+    return false;
+  }
+  bool str(std::string& out) {
+    ws();
+    if (i >= s.size() || s[i] != '"') return false;
+    ++i;
+    out.clear();
+    while (i < s.size() && s[i] != '"') {
+      if (s[i] == '\\') {
+        if (i + 1 >= s.size()) return false;
+        const char c = s[i + 1];
+        if (c == 'u') {  // tensor names are ASCII; keep a placeholder
+          if (i + 5 >= s.size()) return false;
+          out += '?';
+          i += 6;
+          continue;
+        }
+        out += c == 'n' ? '\n' : c == 't' ? '\t' : c;
+        i += 2;
+        continue;
+      }
+      out += s[i++];
+    }
+    if (i >= s.size()) return false;
+    ++i;
+    return true;
+  }
+  bool num(int64_t& v) {
+    ws();
+    size_t j = i;
+    if (j < s.size() && s[j] == '-') ++j;
+    if (j >= s.size() || s[j] < '0' || s[j] > '9') return false;
+    while (j < s.size() && s[j] >= '0' && s[j] <= '9') ++j;
+    v = std::strtoll(s.c_str() + i, nullptr, 10);
+    i = j;
+    return true;
+  }
+  bool skip() {
+    ws();
+    if (i >= s.size()) return false;
+    const char c = s[i];
+    if (c == '"') {
+      std::string t;
+      return str(t);
+    }
+    if (c == '{') {
+      ++i;
+      if (eat('}')) return true;
+      do {
+        std::string k;
+        if (!str(k) || !eat(':') || !skip()) return false;
+      } while (eat(','));
+      return eat('}');
+    }
+    if (c == '[') {
+      ++i;
+      if (eat(']')) return true;
+      do {
+        if (!skip()) return false;
+      } while (eat(','));
+      return eat(']');
+    }
+    const size_t j = i;
+    while (i < s.size() && (isalnum((unsigned char)s[i]) || s[i] == '-' || s[i] == '+' || s[i] == '.')) ++i;
+    return i > j;
+  }
+};
+
+bool parse_st_header(const std::string& js, std::map<std::string, StTensor>* out) {
+  JsonCursor p{js};
+  if (!p.eat('{')) return false;
+  if (p.eat('}')) return true;
+  do {
+    std::string name;
+    if (!p.str(name) || !p.eat(':')) return false;
+    if (name == "__metadata__") {
+      if (!p.skip()) return false;
+      continue;
+    }
+    StTensor t;
+    if (!p.eat('{')) return false;
+    if (!p.eat('}')) {
+      do {
+        std::string f;
+        if (!p.str(f) || !p.eat(':')) return false;
+        if (f == "dtype") {
+          if (!p.str(t.dtype)) return false;
+        } else if (f == "shape") {
+          if (!p.eat('[')) return false;
+          if (!p.eat(']')) {
+            do {
+              int64_t v;
+              if (!p.num(v)) return false;
+              t.shape.push_back(v);
+            } while (p.eat(','));
+            if (!p.eat(']')) return false;
+          }
+        } else if (f == "data_offsets") {
+          int64_t a, b;
+          if (!p.eat('[') || !p.num(a) || !p.eat(',') || !p.num(b) || !p.eat(']')) return false;
+          t.begin = a;
+          t.end = b;
+        } else if (!p.skip()) {
+          return false;
+        }
+      } while (p.eat(','));
+      if (!p.eat('}')) return false;
+    }
+    (*out)[name] = t;
+  } while (p.eat(','));
+  return p.eat('}');
+}
+
+}  // namespace
+
+struct DiskTier {
+  krill_prefix_t pc = nullptr;
+  std::string dir;
+  int64_t budget = 0;  // bytes; < 0 unbounded
+  std::thread worker;
+  std::mutex mu;  // queue, counters
+  std::condition_variable cv, idle;
+  std::deque<krill_prefix_entry_t> queue;
+  int busy = 0;
+  bool stop = false;
+  int64_t counter = 0;
+  bool seeded = false;
+  cudaStream_t wstream = nullptr, lstream = nullptr;
+  uint8_t* d_w = nullptr;  // writer device scratch: block table + one layer
+  size_t d_w_cap = 0;
+  uint8_t* h_w = nullptr;  // writer pinned host buffer: one layer
+  size_t h_w_cap = 0;
+  std::mutex lmu;  // loader scratch
+  uint8_t* d_l = nullptr;
+  size_t d_l_cap = 0;
+};
+
+namespace {
+
+namespace fs = std::filesystem;
+
+std::string disk_path(const DiskTier* dt, uint64_t key) {
+  char name[40];
+  std::snprintf(name, sizeof(name), "%016llx.q8.safetensors", (unsigned long long)key);
+  return dt->dir + "/" + name;
+}
+
+// Bytes of one layer of an S-token entry: codes K, V, then K/V scale and zero.
+int64_t disk_layer_bytes(const Geom& g, int64_t S) {
+  return 2 * (int64_t)g.Hkv * S * g.D + 8 * (int64_t)g.Hkv * S * g.NG;
+}
+
+std::string st_header(const Geom& g, int64_t S) {
+  std::string h = "{";
+  int64_t off = 0;
+  const int64_t codes = (int64_t)g.Hkv * S * g.D, meta = (int64_t)g.Hkv * S * g.NG * 2;
+  const char* names[6] = {"qk", "qv", "ks", "kz", "vs", "vz"};
+  char buf[256];
+  for (int L = 0; L < g.L; ++L)
+    for (int a = 0; a < 6; ++a) {
+      const bool c = a < 2;
+      const int64_t n = c ? codes : meta;
+      std::snprintf(buf, sizeof(buf),
+                    "%s\"layer_%d_%s\":{\"dtype\":\"%s\",\"shape\":[1,%d,%lld,%d],\"data_offsets\":[%lld,%lld]}",
+                    h.size() > 1 ? "," : "", L, names[a], c ? "U8" : "F16", g.Hkv, (long long)S,
+                    c ? g.D : g.NG, (long long)off, (long long)(off + n));
+      h += buf;
+      off += n;
+    }
+  h += "}";
+  while (h.size() % 8) h += ' ';
+  return h;
+}
+
+void disk_evict_to_low_water(DiskTier* dt) {
+  if (dt->budget <= 0) return;
+  const int64_t low = dt->budget - dt->budget / 10;
+  std::vector<std::pair<fs::file_time_type, std::pair<fs::path, int64_t>>> files;
+  int64_t total = 0;
+  std::error_code ec;
+  for (const auto& de : fs::directory_iterator(dt->dir, ec)) {
+    if (de.path().extension() != ".safetensors") continue;
+    const int64_t sz = (int64_t)de.file_size(ec);
+    files.push_back({de.last_write_time(ec), {de.path(), sz}});
+    total += sz;
+  }
+  if (total > dt->budget) {
+    std::sort(files.begin(), files.end(),
+              [](const auto& a, const auto& b) { return a.first < b.first; });
+    for (const auto& f : files) {
+      if (total <= low) break;
+      if (fs::remove(f.second.first, ec)) total -= f.second.second;
+    }
+  }
+  dt->counter = total;
+  dt->seeded = true;
+}
+
+int64_t disk_scan_bytes(const DiskTier* dt) {
+  int64_t total = 0;
+  std::error_code ec;
+  for (const auto& de : fs::directory_iterator(dt->dir, ec))
+    if (de.path().extension() == ".safetensors") total += (int64_t)de.file_size(ec);
+  return total;
+}
+
+// Worker: gather every layer of the entry (gather kernel, mode 0) and write
+// the file under a temporary name, then rename it into place.
+bool disk_write_entry(DiskTier* dt, krill_prefix_entry_t e) {
+  krill_pool_t p = dt->pc->pool;
+  const Geom& g = p->geom;
+  const int64_t S = e->n_tokens;
+  if (S <= 0) return false;
+  const int64_t lb = disk_layer_bytes(g, S);
+  const size_t nb = e->blocks.size();
+  const size_t bt_bytes = (nb * sizeof(int32_t) + 255) & ~size_t(255);
+  if (cudaSetDevice(p->device) != cudaSuccess) return false;
+  if (dt->d_w_cap < bt_bytes + (size_t)lb) {
+    if (dt->d_w) cudaFree(dt->d_w);
+    dt->d_w = nullptr;
+    dt->d_w_cap = 0;
+    if (cudaMalloc(&dt->d_w, bt_bytes + (size_t)lb) != cudaSuccess) return false;
+    dt->d_w_cap = bt_bytes + (size_t)lb;
+  }
+  if (dt->h_w_cap < (size_t)lb) {
+    if (dt->h_w) cudaFreeHost(dt->h_w);
+    dt->h_w = nullptr;
+    dt->h_w_cap = 0;
+    if (cudaMallocHost(&dt->h_w, (size_t)lb) != cudaSuccess) return false;
+    dt->h_w_cap = (size_t)lb;
+  }
+  const std::string path = disk_path(dt, e->key), tmp = path + ".tmp";
+  FILE* f = std::fopen(tmp.c_str(), "wb");
+  if (!f) return false;
+  const std::string hdr = st_header(g, S);
+  const uint64_t hl = hdr.size();
+  bool ok = std::fwrite(&hl, 8, 1, f) == 1 && std::fwrite(hdr.data(), 1, hdr.size(), f) == hdr.size();
+  ok = ok && cudaMemcpyAsync(dt->d_w, e->blocks.data(), nb * sizeof(int32_t), cudaMemcpyHostToDevice,
+                             dt->wstream) == cudaSuccess;
+  const int64_t codes = (int64_t)g.Hkv * S * g.D, meta = (int64_t)g.Hkv * S * g.NG * 2;
+  uint8_t* d = dt->d_w + bt_bytes;
+  for (int L = 0; ok && L < g.L; ++L) {
+    GatherOut o{};
+    o.keys = d;
+    o.values = d + codes;
+    o.key_scales = reinterpret_cast<uint16_t*>(d + 2 * codes);
+    o.key_zeros = reinterpret_cast<uint16_t*>(d + 2 * codes + meta);
+    o.value_scales = reinterpret_cast<uint16_t*>(d + 2 * codes + 2 * meta);
+    o.value_zeros = reinterpret_cast<uint16_t*>(d + 2 * codes + 3 * meta);
+    o.row_off = 0;
+    o.rows_total = S;
+    o.mode = 0;
+    ok = launch_gather(g, p->d_pool, L, reinterpret_cast<const int32_t*>(dt->d_w), 0, S, o,
+                       dt->wstream) == cudaSuccess &&
+         cudaMemcpyAsync(dt->h_w, d, (size_t)lb, cudaMemcpyDeviceToHost, dt->wstream) == cudaSuccess &&
+         cudaStreamSynchronize(dt->wstream) == cudaSuccess &&
+         std::fwrite(dt->h_w, 1, (size_t)lb, f) == (size_t)lb;
+  }
+  ok = (std::fclose(f) == 0) && ok;
+  std::error_code ec;
+  if (!ok) {
+    fs::remove(tmp, ec);
+    return false;
+  }
+  const int64_t prior = fs::exists(path, ec) ? (int64_t)fs::file_size(path, ec) : 0;
+  fs::rename(tmp, path, ec);
+  if (ec) {
+    fs::remove(tmp, ec);
+    return false;
+  }
+  const int64_t now = (int64_t)fs::file_size(path, ec);
+  bool over;
+  {
+    std::lock_guard<std::mutex> lk(dt->mu);
+    if (!dt->seeded) {
+      dt->counter = disk_scan_bytes(dt);
+      dt->seeded = true;
+    } else {
+      dt->counter += now - prior;
+    }
+    over = dt->budget > 0 && dt->counter > dt->budget;
+    if (over) disk_evict_to_low_water(dt);
+  }
+  return true;
+}
+
+void disk_worker(DiskTier* dt) {
+  for (;;) {
+    krill_prefix_entry_t e;
+    {
+      std::unique_lock<std::mutex> lk(dt->mu);
+      dt->cv.wait(lk, [&] { return dt->stop || !dt->queue.empty(); });
+      if (dt->queue.empty()) return;  // stop requested and drained
+      e = dt->queue.front();
+      dt->queue.pop_front();
+      dt->busy += 1;
+    }
+    disk_write_entry(dt, e);
+    entry_unref(dt->pc, e);
+    {
+      std::lock_guard<std::mutex> lk(dt->mu);
+      dt->busy -= 1;
+      if (dt->queue.empty() && dt->busy == 0) dt->idle.notify_all();
+    }
+  }
+}
+
+void disk_wait(DiskTier* dt) {
+  std::unique_lock<std::mutex> lk(dt->mu);
+  dt->idle.wait(lk, [&] { return dt->queue.empty() && dt->busy == 0; });
+}
+
+void disk_shutdown(DiskTier* dt) {
+  {
+    std::lock_guard<std::mutex> lk(dt->mu);
+    dt->stop = true;
+  }
+  dt->cv.notify_all();
+  if (dt->worker.joinable()) dt->worker.join();
+  cudaSetDevice(dt->pc->pool->device);
+  if (dt->wstream) cudaStreamDestroy(dt->wstream);
+  if (dt->lstream) cudaStreamDestroy(dt->lstream);
+  if (dt->d_w) cudaFree(dt->d_w);
+  if (dt->h_w) cudaFreeHost(dt->h_w);
+  if (dt->d_l) cudaFree(dt->d_l);
+  delete dt;
+}
+
+// Disk probe of one key: a missing or unreadable file, or one whose shapes do
+// not fit this pool, is a miss (KRILL_ERR_NOT_FOUND); a hit is read into new
+// pool blocks (restore kernel) and returned as an entry holding one map
+// reference. The file's modification time is refreshed (the LRU recency).
+krill_status_t disk_load(DiskTier* dt, uint64_t key, int64_t S, const char* model, const char* media,
+                         krill_prefix_entry_t* out) {
+  krill_pool_t p = dt->pc->pool;
+  const Geom& g = p->geom;
+  const std::string path = disk_path(dt, key);
+  std::error_code ec;
+  if (!fs::exists(path, ec)) return KRILL_ERR_NOT_FOUND;
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) return KRILL_ERR_NOT_FOUND;
+  uint64_t hl = 0;
+  std::string hdr;
+  std::vector<uint8_t> data;
+  bool ok = std::fread(&hl, 8, 1, f) == 1 && hl < (uint64_t)1 << 28;
+  if (ok) {
+    hdr.resize(hl);
+    ok = std::fread(&hdr[0], 1, hl, f) == hl;
+  }
+  std::map<std::string, StTensor> ts;
+  ok = ok && parse_st_header(hdr, &ts);
+  const int64_t lb = disk_layer_bytes(g, S);
+  const int64_t codes = (int64_t)g.Hkv * S * g.D, meta = (int64_t)g.Hkv * S * g.NG * 2;
+  // every layer present with this pool's shapes
+  const char* names[6] = {"qk", "qv", "ks", "kz", "vs", "vz"};
+  int64_t max_end = 0;
+  for (int L = 0; ok && L < g.L; ++L)
+    for (int a = 0; ok && a < 6; ++a) {
+      auto it = ts.find("layer_" + std::to_string(L) + "_" + names[a]);
+      if (it == ts.end()) {
+        ok = false;
+        break;
+      }
+      const StTensor& t = it->second;
+      const bool c = a < 2;
+      ok = t.dtype == (c ? "U8" : "F16") && t.shape.size() == 4 && t.shape[0] == 1 &&
+           t.shape[1] == g.Hkv && t.shape[2] == S && t.shape[3] == (c ? g.D : g.NG) &&
+           t.end - t.begin == (c ? codes : meta) && t.begin >= 0;
+      max_end = std::max(max_end, t.end);
+    }
+  ok = ok && ts.count("layer_" + std::to_string(g.L) + "_qk") == 0;  // no extra layers
+  if (ok) {
+    data.resize((size_t)max_end);
+    ok = std::fread(data.data(), 1, data.size(), f) == data.size();
+  }
+  std::fclose(f);
+  if (!ok) return KRILL_ERR_NOT_FOUND;
+
+  std::lock_guard<std::mutex> llk(dt->lmu);
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  if (dt->d_l_cap < (size_t)lb) {
+    if (dt->d_l) cudaFree(dt->d_l);
+    dt->d_l = nullptr;
+    dt->d_l_cap = 0;
+    CUDA_TRY(cudaMalloc(&dt->d_l, (size_t)lb));
+    dt->d_l_cap = (size_t)lb;
+  }
+  krill_seq_t h;
+  Seq* s = nullptr;
+  TRY(seq_new(p, &h, &s));
+  krill_status_t st = KRILL_OK;
+  for (int L = 0; st == KRILL_OK && L < g.L; ++L) {
+    uint8_t* d = dt->d_l;
+    const std::string pre = "layer_" + std::to_string(L) + "_";
+    const int64_t offs[6] = {0, codes, 2 * codes, 2 * codes + meta, 2 * codes + 2 * meta,
+                             2 * codes + 3 * meta};
+    for (int a = 0; a < 6 && st == KRILL_OK; ++a) {
+      const StTensor& t = ts[pre + names[a]];
+      if (cudaMemcpyAsync(d + offs[a], data.data() + t.begin, (size_t)(t.end - t.begin),
+                          cudaMemcpyHostToDevice, dt->lstream) != cudaSuccess)
+        st = fail(KRILL_ERR_CUDA, "disk tier upload failed");
+    }
+    if (st != KRILL_OK) break;
+    ScatterIn in{};
+    in.keys = d;
+    in.values = d + codes;
+    in.key_scales = reinterpret_cast<const uint16_t*>(d + offs[2]);
+    in.key_zeros = reinterpret_cast<const uint16_t*>(d + offs[3]);
+    in.value_scales = reinterpret_cast<const uint16_t*>(d + offs[4]);
+    in.value_zeros = reinterpret_cast<const uint16_t*>(d + offs[5]);
+    in.row_off = 0;
+    in.rows_total = S;
+    st = do_restore(p, *s, L, S, S, in, dt->lstream);
+    // the layer scratch is reused by the next layer
+    if (st == KRILL_OK && cudaStreamSynchronize(dt->lstream) != cudaSuccess)
+      st = fail(KRILL_ERR_CUDA, "disk tier restore failed");
+  }
+  if (st == KRILL_OK) {
+    auto* e = new krill_prefix_entry_s();
+    const size_t nb = (size_t)((S + kBlockTokens - 1) / kBlockTokens);
+    e->blocks.assign(s->blocks.begin(), s->blocks.begin() + nb);
+    for (int32_t b : e->blocks) block_ref(p, b);
+    e->len.assign(g.L, S);
+    e->ret.assign(g.L, S);
+    e->n_tokens = S;
+    e->key = key;
+    e->model = model ? model : "";
+    e->media = media ? media : "";
+    *out = e;
+    fs::last_write_time(path, fs::file_time_type::clock::now(), ec);
+  }
+  seq_drop_blocks(p, *s);
+  s->alive = false;
+  s->len.clear();
+  s->ret.clear();
+  p->free_slots.push_back((uint32_t)(h & 0xffffffffu));
+  return st;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1452,16 +1930,87 @@ krill_status_t krill_prefix_create(krill_pool_t pool, int32_t max_entries, int32
 
 krill_status_t krill_prefix_clear(krill_prefix_t pc) {
   if (!pc) return fail(KRILL_ERR_INVALID, "null prefix cache");
-  std::lock_guard<std::mutex> lk(pc->mu);
-  std::vector<uint64_t> keys;
-  for (auto& kv : pc->map) keys.push_back(kv.first);
-  for (uint64_t k : keys) evict_locked(pc, k);
+  {
+    std::lock_guard<std::mutex> lk(pc->mu);
+    std::vector<uint64_t> keys;
+    for (auto& kv : pc->map) keys.push_back(kv.first);
+    for (uint64_t k : keys) evict_locked(pc, k);
+  }
+  if (pc->disk) {  // and the disk tier's files (PrefixCache.swift:403-415)
+    DiskTier* dt = pc->disk;
+    disk_wait(dt);
+    std::error_code ec;
+    for (const auto& de : std::filesystem::directory_iterator(dt->dir, ec)) {
+      const std::string name = de.path().filename().string();
+      if (name.size() > 12 && (name.compare(name.size() - 12, 12, ".safetensors") == 0 ||
+                               name.compare(name.size() - 4, 4, ".tmp") == 0))
+        std::filesystem::remove(de.path(), ec);
+    }
+    std::lock_guard<std::mutex> lk(dt->mu);
+    dt->counter = 0;
+    dt->seeded = true;
+  }
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_set_disk(krill_prefix_t pc, const char* cache_dir, int64_t budget_bytes) {
+  if (!pc) return fail(KRILL_ERR_INVALID, "null prefix cache");
+  if (pc->disk) {
+    disk_shutdown(pc->disk);
+    pc->disk = nullptr;
+  }
+  if (budget_bytes == 0) return KRILL_OK;  // disabled (PrefixCache.swift:585)
+  if (!cache_dir || !*cache_dir) return fail(KRILL_ERR_INVALID, "empty cache_dir");
+  krill_pool_t p = pc->pool;
+  if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "the disk tier needs a device pool");
+  if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "the disk tier stores int8 pools");
+  std::error_code ec;
+  std::filesystem::create_directories(cache_dir, ec);
+  if (ec) return fail(KRILL_ERR_INVALID, "cannot create %s: %s", cache_dir, ec.message().c_str());
+  auto* dt = new DiskTier();
+  dt->pc = pc;
+  dt->dir = cache_dir;
+  dt->budget = budget_bytes;
+  DeviceGuard dg(p->device);
+  if (cudaStreamCreateWithFlags(&dt->wstream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&dt->lstream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (dt->wstream) cudaStreamDestroy(dt->wstream);
+    delete dt;
+    return fail(KRILL_ERR_CUDA, "cannot create disk-tier streams");
+  }
+  dt->worker = std::thread(disk_worker, dt);
+  pc->disk = dt;
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_wait_disk(krill_prefix_t pc) {
+  if (!pc) return fail(KRILL_ERR_INVALID, "null prefix cache");
+  if (pc->disk) disk_wait(pc->disk);
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_disk_count(krill_prefix_t pc, int32_t* count) {
+  if (!pc || !count) return fail(KRILL_ERR_INVALID, "null argument");
+  *count = 0;
+  if (!pc->disk) return KRILL_OK;
+  std::error_code ec;
+  for (const auto& de : std::filesystem::directory_iterator(pc->disk->dir, ec))
+    if (de.path().extension() == ".safetensors") *count += 1;
   return KRILL_OK;
 }
 
 krill_status_t krill_prefix_destroy(krill_prefix_t pc) {
   if (!pc) return KRILL_OK;
-  krill_prefix_clear(pc);
+  if (pc->disk) {  // finish pending writes, keep the files
+    disk_shutdown(pc->disk);
+    pc->disk = nullptr;
+  }
+  {
+    std::lock_guard<std::mutex> lk(pc->mu);
+    std::vector<uint64_t> keys;
+    for (auto& kv : pc->map) keys.push_back(kv.first);
+    for (uint64_t k : keys) evict_locked(pc, k);
+  }
   delete pc;
   return KRILL_OK;
 }
@@ -1523,8 +2072,18 @@ krill_status_t krill_prefix_store(krill_prefix_t pc, krill_seq_t seq, const int6
   e->media = media_hash ? media_hash : "";
   e->n_tokens = n;
   e->key = krill_prefix_key(tokens, n, model_id, media_hash, kDtypeInt8);
-  std::lock_guard<std::mutex> lk(pc->mu);
-  insert_locked(pc, e);
+  {
+    std::lock_guard<std::mutex> lk(pc->mu);
+    insert_locked(pc, e);
+    if (pc->disk && !p->windowed()) e->refs.fetch_add(1);  // held by the disk writer
+  }
+  if (pc->disk && !p->windowed()) {  // write-behind (PrefixCache.swift:396-399)
+    {
+      std::lock_guard<std::mutex> lk(pc->disk->mu);
+      pc->disk->queue.push_back(e);
+    }
+    pc->disk->cv.notify_one();
+  }
   return KRILL_OK;
 }
 
@@ -1541,15 +2100,32 @@ krill_status_t krill_prefix_lookup(krill_prefix_t pc, const int64_t* tokens, int
   keys[0] = key_header(model_id, media_hash, kDtypeInt8);
   for (int64_t i = 0; i < n; ++i) keys[i + 1] = key_extend(keys[i], tokens[i]);
   const int64_t step = std::max(1, pc->min_len / 2);
-  std::lock_guard<std::mutex> lk(pc->mu);
   for (int64_t check = n; check >= pc->min_len; check -= step) {
-    auto it = pc->map.find(keys[check]);
-    if (it == pc->map.end()) continue;
-    lru_touch(pc, it->first);
-    it->second->refs.fetch_add(1);
-    *entry = it->second;
-    *prefix_length = check;
-    return KRILL_OK;
+    {
+      std::lock_guard<std::mutex> lk(pc->mu);
+      auto it = pc->map.find(keys[check]);
+      if (it != pc->map.end()) {
+        lru_touch(pc, it->first);
+        it->second->refs.fetch_add(1);
+        *entry = it->second;
+        *prefix_length = check;
+        return KRILL_OK;
+      }
+    }
+    // then the disk tier, with the map unlocked (PrefixCache.swift:296-301)
+    if (pc->disk && !pc->pool->windowed()) {
+      krill_prefix_entry_t e = nullptr;
+      const krill_status_t st = disk_load(pc->disk, keys[check], check, model_id, media_hash, &e);
+      if (st == KRILL_OK) {
+        std::lock_guard<std::mutex> lk(pc->mu);
+        insert_locked(pc, e);
+        e->refs.fetch_add(1);
+        *entry = e;
+        *prefix_length = check;
+        return KRILL_OK;
+      }
+      if (st != KRILL_ERR_NOT_FOUND) return st;
+    }
   }
   return KRILL_ERR_NOT_FOUND;
 }

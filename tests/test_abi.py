@@ -149,3 +149,15 @@ def test_bf16_pool_geometry_and_limits():
         args.update(kw)
         with pytest.raises(kb.KrillError):
             kb.KVPool(device=-1, **args)
+
+
+def test_disk_tier_needs_a_device_pool(tmp_path):
+    p = kb.KVPool(2, 8, 32, 128, num_blocks=4, device=-1)
+    pc = kb.PrefixCache(p)
+    pc.set_disk(str(tmp_path), 0)  # budget 0 = disabled: always accepted
+    assert pc.disk_count == 0
+    with pytest.raises(kb.KrillError) as e:
+        pc.set_disk(str(tmp_path), -1)
+    assert e.value.status == L.KRILL_ERR_NO_DEVICE
+    pc.wait_for_disk_writes()
+    pc.close()
