@@ -197,6 +197,22 @@ krill_status_t krill_append_quantize(krill_pool_t pool, int32_t n_seqs, const kr
                                      int32_t layer_begin, int32_t layer_count, int32_t n_new,
                                      const void* k_new, const void* v_new, int32_t dtype,
                                      void* stream);
+/* Fused RoPE + quantize + append (no reference counterpart as one call; it
+ * fuses MLXFast.RoPE(dimensions: head_dim, traditional: false) applied to the
+ * new K at each token's position, Gemma4Model.swift:502-509 and the per-row
+ * offsets of Attention.swift:13-20, with the update above). Token t of a
+ * sequence whose layer holds `len` tokens sits at position len + t; element
+ * d < head_dim/2 becomes x[d]*cos[p][d] - x[d+h]*sin[p][d] and element d + h
+ * becomes x[d]*sin[p][d] + x[d+h]*cos[p][d] (h = head_dim/2), each product
+ * and sum rounded to f32 and the result rounded to `dtype` before it is
+ * quantized. rope_cos / rope_sin: device f32 tables [rope_rows][head_dim/2]
+ * owned by the caller (angle(p, d) = p * base^(-2d/head_dim)); positions must
+ * stay below rope_rows. V is appended unrotated. int8 pools only. */
+krill_status_t krill_append_quantize_rope(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                          int32_t layer_begin, int32_t layer_count, int32_t n_new,
+                                          const void* k_new, const void* v_new, int32_t dtype,
+                                          const float* rope_cos, const float* rope_sin,
+                                          int64_t rope_rows, void* stream);
 
 /* Decode attention for one query token per (layer, sequence), reading the
  * int8 cache directly: dequantization (with the reference's fp16 rounding) is

@@ -301,17 +301,26 @@ def make_quantized_kv_caches(pool: KVPool, num_layers: Optional[int] = None):
 
 
 # ---------------------------------------------------------------- hot path
-def append_quantize(pool: KVPool, seqs, layer_begin: int, k_new, v_new, stream=None):
+def append_quantize(pool: KVPool, seqs, layer_begin: int, k_new, v_new, stream=None, rope=None):
     """Quantize and append. k_new/v_new: [layer_count, n_seqs, Hkv, n_new, D]
-    (a 3-D [Hkv, n_new, D] tensor is one layer of one sequence)."""
+    (a 3-D [Hkv, n_new, D] tensor is one layer of one sequence). ``rope`` =
+    (cos, sin) f32 device tables [rows][D/2]: rotate the new K at each token's
+    position first (fused RoPE + quantize + append)."""
     if k_new.dim() == 3:
         k_new = k_new.unsqueeze(0).unsqueeze(0)
         v_new = v_new.unsqueeze(0).unsqueeze(0)
     lc, ns, _, n_new, _ = k_new.shape
     assert ns == len(seqs)
     arr = _seq_array(seqs)
-    check(L.lib.krill_append_quantize(pool.handle, ns, arr, layer_begin, lc, n_new, _ptr(k_new),
-                                      _ptr(v_new), _dt(k_new), _stream(stream)))
+    if rope is None:
+        check(L.lib.krill_append_quantize(pool.handle, ns, arr, layer_begin, lc, n_new, _ptr(k_new),
+                                          _ptr(v_new), _dt(k_new), _stream(stream)))
+        return
+    cos, sin = rope
+    assert cos.shape == sin.shape and cos.dim() == 2 and cos.dtype == torch.float32
+    check(L.lib.krill_append_quantize_rope(pool.handle, ns, arr, layer_begin, lc, n_new, _ptr(k_new),
+                                           _ptr(v_new), _dt(k_new), _ptr(cos), _ptr(sin),
+                                           cos.shape[0], _stream(stream)))
 
 
 def decode_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float, stream=None):

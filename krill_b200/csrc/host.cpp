@@ -336,9 +336,15 @@ krill_status_t check_layers(krill_pool_t p, int32_t lb, int32_t lc) {
 // and length updates run, and the device work is skipped.
 krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                          int32_t lc, int32_t n_new, const void* k, const void* v, int32_t dtype,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, RopeTable rope = RopeTable{nullptr, nullptr, 0}) {
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(dtype, "k/v"));
+  if (rope.cos) {
+    if (p->geom.fmt != kFmtInt8) return fail(KRILL_ERR_INVALID, "the RoPE append needs an int8 pool");
+    if (!rope.sin) return fail(KRILL_ERR_INVALID, "null rope_sin");
+    if ((reinterpret_cast<uintptr_t>(rope.cos) | reinterpret_cast<uintptr_t>(rope.sin)) & 3)
+      return fail(KRILL_ERR_INVALID, "rope tables must be 4-byte aligned");
+  }
   if (p->geom.fmt == kFmtBf16 && dtype != KRILL_DTYPE_BF16)
     return fail(KRILL_ERR_INVALID, "a bf16 pool stores bf16 K/V: k/v dtype must be BF16");
   if (n_seqs < 0 || n_new < 0) return fail(KRILL_ERR_INVALID, "negative count");
@@ -352,6 +358,12 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
   for (int i = 0; i < n_seqs; ++i)
     for (int j = 0; j < i; ++j)
       if (sv[i] == sv[j]) return fail(KRILL_ERR_INVALID, "sequence listed twice in one call");
+  if (rope.cos)
+    for (int i = 0; i < n_seqs; ++i)
+      for (int li = 0; li < lc; ++li)
+        if (sv[i]->len[lb + li] + n_new > rope.rows)
+          return fail(KRILL_ERR_INVALID, "position %lld beyond the %lld-row rope table",
+                      (long long)(sv[i]->len[lb + li] + n_new - 1), (long long)rope.rows);
   const size_t n_dst = (size_t)lc * n_seqs * n_new;
   StageSlot* slot = nullptr;
   std::vector<AppendDst> dry;
@@ -387,7 +399,7 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
     TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
     CUDA_TRY(timed_launch(p, 1, stream, [&] {
       return launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
-                           n_seqs, n_new, k, v, dtype, p->d_err + 1, stream);
+                           n_seqs, n_new, k, v, dtype, p->d_err + 1, rope, stream);
     }));
     p->kernels += 1;
     TRY(stage_release(slot, stream));
@@ -1146,6 +1158,19 @@ krill_status_t krill_append_quantize(krill_pool_t p, int32_t n_seqs, const krill
   DeviceGuard dg(p->device);
   return do_append(p, n_seqs, seqs, layer_begin, layer_count, n_new, k_new, v_new, dtype,
                    (cudaStream_t)stream);
+}
+
+krill_status_t krill_append_quantize_rope(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                          int32_t layer_begin, int32_t layer_count, int32_t n_new,
+                                          const void* k_new, const void* v_new, int32_t dtype,
+                                          const float* rope_cos, const float* rope_sin,
+                                          int64_t rope_rows, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  if (!rope_cos || !rope_sin || rope_rows <= 0) return fail(KRILL_ERR_INVALID, "null rope table");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  return do_append(p, n_seqs, seqs, layer_begin, layer_count, n_new, k_new, v_new, dtype,
+                   (cudaStream_t)stream, RopeTable{rope_cos, rope_sin, rope_rows});
 }
 
 krill_status_t krill_decode_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,

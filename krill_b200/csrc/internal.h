@@ -113,11 +113,19 @@ struct AttnParams {
   int n_pslots;               // prefix record slots per cascaded unit
 };
 
+// Rotary table for the fused RoPE append: cos / sin [rows][D/2] f32 (device),
+// indexed by absolute position; cos == nullptr means no rotation.
+struct RopeTable {
+  const float* cos;
+  const float* sin;
+  int64_t rows;
+};
+
 // Kernels that store scales raise *large_scale when one has |s| >= 64 (the
 // one-fma dequantization is exact only below that).
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
                           int layer_count, int n_seqs, int n_new, const void* k, const void* v,
-                          int dtype, int* large_scale, cudaStream_t stream);
+                          int dtype, int* large_scale, RopeTable rope, cudaStream_t stream);
 cudaError_t launch_gather(const Geom& g, const uint8_t* pool, int layer, const int32_t* d_bt,
                           int64_t p0, int64_t S, const GatherOut& out, cudaStream_t stream);
 cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_t* d_bt, int64_t p0,

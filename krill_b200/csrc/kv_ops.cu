@@ -92,7 +92,8 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
                                                               int n_seqs, int n_new,
                                                               const void* __restrict__ k,
                                                               const void* __restrict__ v, int dtype,
-                                                              int* __restrict__ large_scale) {
+                                                              int* __restrict__ large_scale,
+                                                              RopeTable rope) {
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
@@ -113,6 +114,26 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
   float xk[EPL], xv[EPL];
   load_row<EPL>(k, elem_off, lane, dtype, xk);
   load_row<EPL>(v, elem_off, lane, dtype, xv);
+  if (rope.cos) {
+    // Rotate-half RoPE at the token's absolute position (MLXFast.RoPE with
+    // traditional: false): element d < D/2 pairs with d + D/2, which lives 16
+    // lanes away. Unfused f32 products and sum, then the input-dtype rounding
+    // the reference's rotated K carries before it is quantized.
+    const int half = D / 2;
+    const float* cr = rope.cos + (int64_t)d.pos * half;
+    const float* sr = rope.sin + (int64_t)d.pos * half;
+    float other[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, xk[e], 16);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int i = (lane * EPL + e) % half;
+      const float c = __ldg(cr + i), sn = __ldg(sr + i);
+      const float y = lane < 16 ? __fsub_rn(__fmul_rn(xk[e], c), __fmul_rn(other[e], sn))
+                                : __fadd_rn(__fmul_rn(other[e], sn), __fmul_rn(xk[e], c));
+      xk[e] = round_in(y, dtype);
+    }
+  }
   uint8_t ck[EPL], cv[EPL];
   uint16_t sk, zk, sv, zv;
   quantize_lane<EPL, LPG>(xk, dtype, geom.quant_variant, ck, sk, zk);
@@ -271,13 +292,13 @@ __global__ void scatter_kernel(uint8_t* __restrict__ pool, Geom geom, int layer,
 
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,
                           int layer_count, int n_seqs, int n_new, const void* k, const void* v,
-                          int dtype, int* large_scale, cudaStream_t stream) {
+                          int dtype, int* large_scale, RopeTable rope, cudaStream_t stream) {
   const int64_t warps = (int64_t)layer_count * n_seqs * g.Hkv * n_new;
   if (warps == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
   if (g.fmt == kFmtBf16) {
-    if (dtype != 1) return cudaErrorInvalidValue;
+    if (dtype != 1 || rope.cos) return cudaErrorInvalidValue;
     append_raw_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
         pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new,
         static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v));
@@ -288,7 +309,8 @@ cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, 
 #define KRILL_APPEND(E, P)                                                                    \
   if (epl == E && lpg == P) {                                                                  \
     append_quantize_kernel<E, P><<<(unsigned)blocks, threads, 0, stream>>>(                    \
-        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype, large_scale);    \
+        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype, large_scale,     \
+        rope);                                                                                 \
     return cudaGetLastError();                                                                 \
   }
   KRILL_APPEND(2, 32)   // D=64,  G=64

@@ -93,6 +93,36 @@ def sdpa_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.nd
     return out
 
 
+def rope_table(base: float, head_dim: int, rows: int):
+    """cos / sin [rows][head_dim/2] float32 of angle(p, d) = p * base^(-2d/head_dim),
+    evaluated in float64 (the rotary frequencies of MLXFast.RoPE with
+    traditional: false, as set up at Sources/KrillCore/Attention.swift:55)."""
+    half = head_dim // 2
+    inv = base ** (-2.0 * np.arange(half, dtype=np.float64) / head_dim)
+    ang = np.arange(rows, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def apply_rope(x_bits: np.ndarray, dtype: int, cos: np.ndarray, sin: np.ndarray,
+               positions: np.ndarray) -> np.ndarray:
+    """Rotate-half RoPE of [..., T, D] bits at `positions` [T]: element d <
+    D/2 -> x[d] c - x[d+h] s, element d + h -> x[d] s + x[d+h] c, every
+    product and sum in float32, the result rounded to `dtype` (the rotated K
+    the reference quantizes, Gemma4Model.swift:502-509). Returns bits."""
+    x = bits_to_f64(x_bits, dtype).astype(np.float32)
+    h = x.shape[-1] // 2
+    c = cos[positions]
+    s = sin[positions]
+    x1, x2 = x[..., :h], x[..., h:]
+    y1 = (x1 * c).astype(np.float32) - (x2 * s).astype(np.float32)
+    y2 = (x1 * s).astype(np.float32) + (x2 * c).astype(np.float32)
+    y = np.concatenate([y1, y2], axis=-1).astype(np.float32)
+    if dtype == 0:
+        return y.astype(np.float16).view(np.uint16)
+    u = y.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
 def f16_bits_to_f64(b: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(b, np.uint16).view(np.float16).astype(np.float64)
 

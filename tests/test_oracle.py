@@ -205,3 +205,25 @@ def test_golden_attention_fixtures():
         cv, sv, zv = oracle.quantize(z["v"], dt, G)
         out = oracle.reference_attention(ck, sk, zk, cv, sv, zv, z["q"], dt, G, float(z["scale"]))
         np.testing.assert_allclose(out, z["out"], rtol=0, atol=1e-12, err_msg=f)
+
+
+def test_rope_restatement_against_float64():
+    """The oracle's rotate-half RoPE (the rotation the reference applies to K
+    before caching, traditional: false): identity at position 0, and within
+    one rounding of the input dtype of the float64 rotation elsewhere."""
+    rng = np.random.default_rng(11)
+    D, rows = 128, 64
+    cos, sin = oracle.rope_table(500000.0, D, rows)
+    assert cos.dtype == np.float32 and cos.shape == (rows, D // 2)
+    for dtype in (F16, BF16):
+        x = to_bits(rng.standard_normal((3, 9, D)), dtype)
+        pos = np.array([0, 1, 2, 5, 9, 17, 33, 40, 63])
+        y = oracle.apply_rope(x, dtype, cos, sin, pos)
+        np.testing.assert_array_equal(y[:, 0], x[:, 0])  # cos 1, sin 0
+        xf = oracle.bits_to_f64(x, dtype)
+        h = D // 2
+        ang = pos[:, None] * (500000.0 ** (-2.0 * np.arange(h) / D))[None, :]
+        c, s = np.cos(ang), np.sin(ang)
+        ref = np.concatenate([xf[..., :h] * c - xf[..., h:] * s, xf[..., :h] * s + xf[..., h:] * c], -1)
+        rel = 2.0 ** (-10 if dtype == F16 else -7)
+        assert np.all(np.abs(oracle.bits_to_f64(y, dtype) - ref) <= rel * np.abs(ref) + 1e-6)
