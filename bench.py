@@ -372,9 +372,42 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
         return buf[: lc * hkv * L * D].view(lc, 1, hkv, L, D)
 
     t_fill = time.perf_counter()
-    base = glob.create_sequence()
-    kb.append_quantize(glob, [base], 0, chunk(bufk, Lg, P), chunk(bufv, Lg, P))
-    pc.store_quantized(list(range(P)), "gemma", base)
+    stream = torch.cuda.current_stream()
+    # the shared prefix is owned by GPU 0; other GPUs fetch it once over NVLink
+    # (IPC handle + entry descriptor, then a peer copy into the local pool)
+    if world == 1 or rank == 0:
+        base = glob.create_sequence()
+        kb.append_quantize(glob, [base], 0, chunk(bufk, Lg, P), chunk(bufv, Lg, P))
+        pc.store_quantized(list(range(P)), "gemma", base)
+    peer = None
+    if world > 1:
+        obj = [None]
+        if rank == 0:
+            hit0 = pc.lookup_quantized(list(range(P)), "gemma")
+            torch.cuda.synchronize()
+            obj = [(glob.ipc_handle(), pc.describe(hit0))]
+        dist.broadcast_object_list(obj, src=0)
+        if rank != 0:
+            handle, desc = obj[0]
+            # the first import maps the owner's pool (cudaIpcOpenMemHandle,
+            # host side); the second, timed on the device, is the NVLink copy
+            t0 = time.perf_counter()
+            imp = pc.import_entry(handle, desc, stream=stream)
+            torch.cuda.synchronize()
+            first_ms = (time.perf_counter() - t0) * 1e3
+            imp.release()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            imp = pc.import_entry(handle, desc, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            nbytes = ((P + 255) // 256) * glob.block_bytes
+            peer = {"rank": rank, "bytes": nbytes, "first_import_ms_incl_mapping": first_ms,
+                    "copy_ms": e0.elapsed_time(e1), "GB/s": nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9}
+            imp.release()  # the cache keeps the entry
+        dist.barrier()  # the owner keeps its blocks until every copy is done
+        if rank == 0:
+            hit0.release()
     gseqs, sseqs = [], []
     for i, L in enumerate(mine):
         if i in shared:
@@ -402,7 +435,6 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     qg = torch.randn((Lg, n, hq, D), generator=gen, device=dev).to(torch.float16)
     qs = torch.randn((Ls, n, hq, D), generator=gen, device=dev).to(torch.float16)
     og, os_ = torch.empty_like(qg), torch.empty_like(qs)
-    stream = torch.cuda.current_stream()
 
     def step():
         kb.decode_step(glob, gseqs, 0, kg, kg, qg, og, cfg["scale"], stream=stream)
@@ -446,6 +478,9 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     qo = n * (Lg + Ls) * 2 * hq * D * 2
     attn_ms = (ag + as_) / args.steps
     peak, peak_kind = measured_peak()
+    fetches = [None] * world
+    if world > 1:
+        dist.all_gather_object(fetches, peer)
     if rank == 0:
         line = {
             "metric": "int8-KV decode-attn+append tokens/s (mixed sliding/global)",
@@ -466,6 +501,7 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                          "frac": (glob_b + slid_b + qo) / (attn_ms / 1e3) / 1e9 / peak,
                          "algo_bytes": glob_b + slid_b + qo},
             "gpu_launches": launches, "fill_s": t_fill, "clocks": clocks.summary(),
+            "prefix_peer_fetch": [f for f in fetches if f],
             "device_error_flag": glob.device_error() | slid.device_error(),
         }
         print(json.dumps(line), flush=True)

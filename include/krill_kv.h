@@ -226,6 +226,17 @@ krill_status_t krill_decode_attention(krill_pool_t pool, int32_t n_seqs, const k
                                       int32_t layer_begin, int32_t layer_count, const void* q,
                                       int32_t q_dtype, void* out, int32_t out_dtype, float scale,
                                       void* stream);
+/* Multi-query verify attention for speculative decoding: the batched verify
+ * forward with buildBatchedVerifyMask (BatchedDecode.swift:299-312). The last
+ * n_query tokens of each sequence (appended beforehand, e.g. by
+ * krill_append_quantize with n_new = n_query) are the queries; query j attends
+ * the cache up to and including its own token and none of the later drafts, so
+ * the result equals n_query sequential single-token decode steps.
+ * q / out: [layer_count][n_seqs][n_query][Hq][D]. Full-history pools only. */
+krill_status_t krill_verify_attention(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, int32_t n_query,
+                                      const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                                      float scale, void* stream);
 
 /* Allocation-free decode attention. No counterpart in the reference: it
  * exists for callers that cannot have the library allocate memory while they
@@ -375,6 +386,22 @@ uint64_t krill_prefix_key(const int64_t* tokens, int64_t n_tokens, const char* m
 krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
                                        krill_prefix_entry_t src_entry, void* stream,
                                        krill_prefix_entry_t* dst_entry);
+
+/* Cross-process form of the same fetch, for one process per GPU (no
+ * reference counterpart). The owner publishes its pool's IPC handle
+ * (krill_pool_ipc_handle, 64 bytes) and an entry descriptor
+ * (krill_prefix_entry_describe: geometry, key, length, block ids, per-layer
+ * lengths, model id, media hash, tokens; call with buf = NULL for the size);
+ * the caller moves both to the other process. krill_prefix_import maps the
+ * owner's pool once per process (cudaIpcOpenMemHandle), copies the entry's
+ * blocks over NVLink into new local blocks on `stream` and registers the entry
+ * in dst, returning a held reference. The owner must keep the entry alive
+ * until the copy on `stream` has finished. */
+krill_status_t krill_pool_ipc_handle(krill_pool_t pool, void* handle);
+krill_status_t krill_prefix_entry_describe(krill_prefix_t pc, krill_prefix_entry_t entry, void* buf,
+                                           int64_t cap, int64_t* size);
+krill_status_t krill_prefix_import(krill_prefix_t dst, const void* pool_handle, const void* desc,
+                                   int64_t desc_size, void* stream, krill_prefix_entry_t* dst_entry);
 
 #ifdef __cplusplus
 }

@@ -93,6 +93,7 @@ _SIGS = {
     "krill_seq_can_truncate": (i32, [vp, u64, i64, P_i32]),
     "krill_seq_blocks": (i32, [vp, u64, P_i32, i32, P_i32]),
     "krill_append_quantize": (i32, [vp, i32, P_u64, i32, i32, i32, vp, vp, i32, vp]),
+    "krill_verify_attention": (i32, [vp, i32, P_u64, i32, i32, i32, vp, i32, vp, i32, C.c_float, vp]),
     "krill_append_quantize_rope": (i32, [vp, i32, P_u64, i32, i32, i32, vp, vp, i32, vp, vp, i64, vp]),
     "krill_decode_attention": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),
     "krill_decode_attention_noalloc": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),
@@ -118,6 +119,9 @@ _SIGS = {
     "krill_prefix_memory_count": (i32, [vp, P_i32]),
     "krill_prefix_key": (u64, [P_i64, i64, cstr, cstr, i32]),
     "krill_prefix_peer_fetch": (i32, [vp, vp, vp, vp, C.POINTER(vp)]),
+    "krill_pool_ipc_handle": (i32, [vp, vp]),
+    "krill_prefix_entry_describe": (i32, [vp, vp, vp, i64, P_i64]),
+    "krill_prefix_import": (i32, [vp, vp, vp, i64, vp, C.POINTER(vp)]),
 }
 
 for _name, (_res, _args) in _SIGS.items():

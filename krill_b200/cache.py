@@ -136,6 +136,12 @@ class KVPool:
         check(L.lib.krill_pool_last_plan(self.handle, C.byref(c), C.byref(hg), C.byref(n), C.byref(g)))
         return c.value, hg.value, n.value, g.value
 
+    def ipc_handle(self) -> bytes:
+        """This pool's CUDA IPC handle (64 bytes) for krill_prefix_import."""
+        buf = C.create_string_buffer(64)
+        check(L.lib.krill_pool_ipc_handle(self.handle, buf))
+        return buf.raw
+
     def last_cascade(self):
         """(sequence groups attended together, cascade items, prefix record
         slots per member, cascade CTAs) of the last decode-attention launch."""
@@ -323,6 +329,18 @@ def append_quantize(pool: KVPool, seqs, layer_begin: int, k_new, v_new, stream=N
                                            cos.shape[0], _stream(stream)))
 
 
+def verify_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float, stream=None):
+    """Multi-query verify attention (buildBatchedVerifyMask semantics): q/out
+    [layer_count, n_seqs, n_query, Hq, D]; the last n_query cached tokens of
+    each sequence are the queries, each seeing the cache up to its own token."""
+    lc, ns, nq = q.shape[0], q.shape[1], q.shape[2]
+    assert ns == len(seqs)
+    arr = _seq_array(seqs)
+    check(L.lib.krill_verify_attention(pool.handle, ns, arr, layer_begin, lc, nq, _ptr(q), _dt(q),
+                                       _ptr(out), _dt(out), scale, _stream(stream)))
+    return out
+
+
 def decode_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float, stream=None):
     """q/out: [layer_count, n_seqs, Hq, D]."""
     lc, ns = q.shape[0], q.shape[1]
@@ -485,6 +503,24 @@ class PrefixCache:
         check(L.lib.krill_prefix_peer_fetch(self.handle, src.handle, hit.entry, _stream(stream),
                                             C.byref(e)))
         return QuantizedPrefixCacheHit(self, e, hit.prefix_length)
+
+    def describe(self, hit: QuantizedPrefixCacheHit) -> bytes:
+        """Entry descriptor for krill_prefix_import in another process."""
+        n = C.c_int64()
+        check(L.lib.krill_prefix_entry_describe(self.handle, hit.entry, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        check(L.lib.krill_prefix_entry_describe(self.handle, hit.entry, buf, n.value, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def import_entry(self, pool_handle: bytes, desc: bytes, stream=None) -> QuantizedPrefixCacheHit:
+        """Copy an entry owned by another process's pool (IPC handle +
+        descriptor) into this cache over NVLink; returns a held hit."""
+        e = C.c_void_p()
+        check(L.lib.krill_prefix_import(self.handle, pool_handle, desc, len(desc), _stream(stream),
+                                        C.byref(e)))
+        n = C.c_int64()
+        check(L.lib.krill_prefix_entry_length(e, C.byref(n)))
+        return QuantizedPrefixCacheHit(self, e, n.value)
 
 
 def prefix_key(tokens, model_id: str, media_hash: Optional[str] = None, dtype_tag: int = 2) -> int:

@@ -132,6 +132,7 @@ struct krill_pool_s {
   float* d_partials = nullptr;
   int64_t partials_cap = 0;
   int64_t kernels = 0;  // device kernels launched since the last krill_pool_kernel_count
+  std::map<std::string, uint8_t*> ipc_maps;  // other processes' pools opened here (handle bytes)
   int* d_err = nullptr;
   StageSlot stage[kStageSlots];
   int stage_next = 0;
@@ -435,8 +436,12 @@ krill_status_t ensure_scratch(krill_pool_t p, int64_t records, int64_t /*unused*
 
 krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                             int32_t lc, const void* q, int32_t q_dtype, void* out,
-                            int32_t out_dtype, float scale, cudaStream_t stream) {
+                            int32_t out_dtype, float scale, cudaStream_t stream,
+                            int32_t n_query = 1) {
   TRY(check_layers(p, lb, lc));
+  if (n_query < 1) return fail(KRILL_ERR_INVALID, "n_query must be positive");
+  if (n_query > 1 && p->windowed())
+    return fail(KRILL_ERR_INVALID, "multi-query verify attention needs a full-history pool");
   TRY(check_dtype16(q_dtype, "q"));
   if (p->geom.fmt == kFmtBf16 && q_dtype != KRILL_DTYPE_BF16)
     return fail(KRILL_ERR_INVALID, "attention over a bf16 pool takes a BF16 q");
@@ -468,7 +473,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.seq_sh.assign((size_t)n_seqs, 0);
   const int64_t min_tok = p->cfg.cascade_min_tokens == 0 ? 256 : p->cfg.cascade_min_tokens;
   if (!p->windowed() && g.fmt == kFmtInt8 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE &&
-      p->cfg.split_tokens == 0 &&
+      p->cfg.split_tokens == 0 && n_query == 1 &&
       p->cfg.cascade_min_tokens >= 0 && n_seqs >= 2) {
     const size_t min_blocks = (size_t)std::max<int64_t>(1, (min_tok + kBlockTokens - 1) / kBlockTokens);
     pl.gorder.clear();
@@ -517,8 +522,12 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   }
   const int n_groups = (int)pl.gshared.size();
   pl.gstart.push_back((int32_t)pl.gmembers.size());
-  // ---- units (layer, seq) ----
-  const int64_t n_units = (int64_t)lc * n_seqs;
+  // ---- units (layer, seq[, query]) ----
+  // With n_query > 1 (speculative verify) the last n_query tokens of each
+  // sequence are the queries: query j sees the cache up to and including its
+  // own token and none of the later drafts (buildBatchedVerifyMask,
+  // BatchedDecode.swift:299-312), i.e. one unit per query with its own bound.
+  const int64_t n_units = (int64_t)lc * n_seqs * n_query;
   pl.units.resize((size_t)n_units);
   pl.nsb.resize((size_t)n_units);
   int64_t total_sb = 0;
@@ -528,18 +537,23 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       const Seq& s = *pl.sv[si];
       const int64_t len = s.len[L];
       if (len <= 0) return fail(KRILL_ERR_INVALID, "attention over an empty cache (layer %d)", L);
-      const int64_t t_hi = len;
-      const int64_t t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
-      const int64_t ui = (int64_t)li * n_seqs + si;
-      AttnUnit& u = pl.units[ui];
-      u.qo_row = (int32_t)ui;
-      u.si = si;
-      u.layer = L;
-      u.t_lo = (int32_t)t_lo;
-      u.t_hi = (int32_t)t_hi;
-      u.n_pre = 0;
-      pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
-      total_sb += pl.nsb[ui];
+      if (len < n_query)
+        return fail(KRILL_ERR_INVALID, "%d queries need their tokens in the cache (layer %d holds %lld)",
+                    n_query, L, (long long)len);
+      for (int j = 0; j < n_query; ++j) {
+        const int64_t t_hi = len - n_query + 1 + j;
+        const int64_t t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
+        const int64_t ui = ((int64_t)li * n_seqs + si) * n_query + j;
+        AttnUnit& u = pl.units[ui];
+        u.qo_row = (int32_t)ui;
+        u.si = si;
+        u.layer = L;
+        u.t_lo = (int32_t)t_lo;
+        u.t_hi = (int32_t)t_hi;
+        u.n_pre = 0;
+        pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
+        total_sb += pl.nsb[ui];
+      }
     }
   }
   // ---- decomposition: sequence piece length C (sub-blocks) and kv heads per
@@ -936,6 +950,7 @@ krill_status_t krill_pool_destroy(krill_pool_t p) {
       cudaEventDestroy(e.b);
     }
     for (auto e : p->spare_events) cudaEventDestroy(e);
+    for (auto& m : p->ipc_maps) cudaIpcCloseMemHandle(m.second);
     if (p->d_pool) cudaFree(p->d_pool);
     if (p->d_partials) cudaFree(p->d_partials);
     if (p->d_err) cudaFree(p->d_err);
@@ -1182,6 +1197,17 @@ krill_status_t krill_decode_attention(krill_pool_t p, int32_t n_seqs, const kril
   DeviceGuard dg(p->device);
   return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
                       (cudaStream_t)stream);
+}
+
+krill_status_t krill_verify_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, int32_t n_query,
+                                      const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                                      float scale, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
+                      (cudaStream_t)stream, n_query);
 }
 
 krill_status_t krill_decode_step(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
@@ -2294,6 +2320,189 @@ krill_status_t krill_prefix_peer_fetch(krill_prefix_t dst, krill_prefix_t src,
   e->len = se->len;
   e->ret = se->ret;
   e->n_tokens = se->n_tokens;
+  std::lock_guard<std::mutex> lk(dst->mu);
+  insert_locked(dst, e);
+  e->refs.fetch_add(1);
+  *out = e;
+  return KRILL_OK;
+}
+
+// ---- cross-process fetch (one process per GPU) ----
+// Entry descriptor, little-endian: "KKV1", geometry (L, Hkv, D, G, format,
+// window, ring, block bytes), key, length, large-scale flag, block ids,
+// per-layer length / retained, model id, media hash, tokens.
+}  // extern "C"
+namespace {
+struct DescWriter {
+  std::vector<uint8_t> b;
+  template <class T>
+  void put(T v) {
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(&v);
+    b.insert(b.end(), p, p + sizeof(T));
+  }
+  void bytes(const void* p, size_t n) {
+    b.insert(b.end(), (const uint8_t*)p, (const uint8_t*)p + n);
+  }
+};
+struct DescReader {
+  const uint8_t* p;
+  size_t n, i = 0;
+  bool ok = true;
+  template <class T>
+  T get() {
+    T v{};
+    if (i + sizeof(T) > n) {
+      ok = false;
+      return v;
+    }
+    std::memcpy(&v, p + i, sizeof(T));
+    i += sizeof(T);
+    return v;
+  }
+  bool bytes(void* out, size_t m) {
+    if (i + m > n) return ok = false;
+    std::memcpy(out, p + i, m);
+    i += m;
+    return true;
+  }
+};
+}  // namespace
+extern "C" {
+
+krill_status_t krill_pool_ipc_handle(krill_pool_t p, void* handle) {
+  if (!p || !handle) return fail(KRILL_ERR_INVALID, "null argument");
+  if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "a host-only pool has no device memory");
+  DeviceGuard dg(p->device);
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(cudaIpcGetMemHandle(&h, p->d_pool));
+  std::memcpy(handle, &h, sizeof(h));
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_entry_describe(krill_prefix_t pc, krill_prefix_entry_t e, void* buf,
+                                           int64_t cap, int64_t* size) {
+  if (!pc || !e || !size) return fail(KRILL_ERR_INVALID, "null argument");
+  krill_pool_t p = pc->pool;
+  const Geom& g = p->geom;
+  int32_t large = 0;
+  if (!p->host_only) {
+    DeviceGuard dg(p->device);
+    CUDA_TRY(cudaDeviceSynchronize());  // appends in flight may still raise the flag
+    CUDA_TRY(cudaMemcpy(&large, p->d_err + 1, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  }
+  DescWriter w;
+  w.bytes("KKV1", 4);
+  for (int32_t v : {g.L, g.Hkv, g.D, g.G, g.fmt, g.window, g.ring}) w.put<int32_t>(v);
+  w.put<int64_t>(g.block_bytes);
+  w.put<uint64_t>(e->key);
+  w.put<int64_t>(e->n_tokens);
+  w.put<int32_t>(large != 0);
+  w.put<int32_t>((int32_t)e->blocks.size());
+  for (int32_t b : e->blocks) w.put<int32_t>(b);
+  for (int L = 0; L < g.L; ++L) w.put<int64_t>(e->len[L]);
+  for (int L = 0; L < g.L; ++L) w.put<int64_t>(e->ret[L]);
+  w.put<int32_t>((int32_t)e->model.size());
+  w.bytes(e->model.data(), e->model.size());
+  w.put<int32_t>((int32_t)e->media.size());
+  w.bytes(e->media.data(), e->media.size());
+  w.put<int64_t>((int64_t)e->tokens.size());
+  if (!e->tokens.empty()) w.bytes(e->tokens.data(), e->tokens.size() * sizeof(int64_t));
+  *size = (int64_t)w.b.size();
+  if (!buf) return KRILL_OK;  // size query
+  if (cap < *size) return fail(KRILL_ERR_INVALID, "descriptor needs %lld bytes", (long long)*size);
+  std::memcpy(buf, w.b.data(), w.b.size());
+  return KRILL_OK;
+}
+
+krill_status_t krill_prefix_import(krill_prefix_t dst, const void* pool_handle, const void* desc,
+                                   int64_t desc_size, void* stream, krill_prefix_entry_t* out) {
+  if (!dst || !pool_handle || !desc || !out) return fail(KRILL_ERR_INVALID, "null argument");
+  krill_pool_t dp = dst->pool;
+  if (dp->host_only) return fail(KRILL_ERR_NO_DEVICE, "import needs a device pool");
+  const Geom& g = dp->geom;
+  DescReader r{static_cast<const uint8_t*>(desc), (size_t)std::max<int64_t>(0, desc_size)};
+  char magic[4];
+  if (!r.bytes(magic, 4) || std::memcmp(magic, "KKV1", 4) != 0)
+    return fail(KRILL_ERR_INVALID, "not an entry descriptor");
+  int32_t geo[7];
+  for (auto& v : geo) v = r.get<int32_t>();
+  const int64_t block_bytes = r.get<int64_t>();
+  if (!r.ok || geo[0] != g.L || geo[1] != g.Hkv || geo[2] != g.D || geo[3] != g.G || geo[4] != g.fmt ||
+      geo[5] != g.window || geo[6] != g.ring || block_bytes != g.block_bytes)
+    return fail(KRILL_ERR_INVALID, "import between pools of different geometry");
+  auto* e = new krill_prefix_entry_s();
+  e->key = r.get<uint64_t>();
+  e->n_tokens = r.get<int64_t>();
+  const int32_t large = r.get<int32_t>();
+  const int32_t nb = r.get<int32_t>();
+  std::vector<int32_t> src_blocks(nb > 0 && nb < (1 << 24) ? nb : 0);
+  for (auto& b : src_blocks) b = r.get<int32_t>();
+  e->len.resize(g.L);
+  e->ret.resize(g.L);
+  for (auto& v : e->len) v = r.get<int64_t>();
+  for (auto& v : e->ret) v = r.get<int64_t>();
+  int32_t ml = r.get<int32_t>();
+  if (ml >= 0 && ml < (1 << 20)) {
+    e->model.resize(ml);
+    r.bytes(&e->model[0], ml);
+  } else {
+    r.ok = false;
+  }
+  int32_t dl = r.get<int32_t>();
+  if (dl >= 0 && dl < (1 << 20)) {
+    e->media.resize(dl);
+    r.bytes(&e->media[0], dl);
+  } else {
+    r.ok = false;
+  }
+  const int64_t nt = r.get<int64_t>();
+  if (nt >= 0 && nt < ((int64_t)1 << 30)) {
+    e->tokens.resize((size_t)nt);
+    if (nt) r.bytes(e->tokens.data(), (size_t)nt * sizeof(int64_t));
+  } else {
+    r.ok = false;
+  }
+  if (!r.ok || (int32_t)src_blocks.size() != nb) {
+    delete e;
+    return fail(KRILL_ERR_INVALID, "truncated entry descriptor");
+  }
+  {
+    std::lock_guard<std::recursive_mutex> lk(dp->mu);
+    DeviceGuard dg(dp->device);
+    // map the owner's pool once per (handle) in this process
+    const std::string hk(static_cast<const char*>(pool_handle), sizeof(cudaIpcMemHandle_t));
+    uint8_t* src = nullptr;
+    auto it = dp->ipc_maps.find(hk);
+    if (it != dp->ipc_maps.end()) {
+      src = it->second;
+    } else {
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, pool_handle, sizeof(h));
+      void* ptr = nullptr;
+      const cudaError_t ce = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+      if (ce != cudaSuccess) {
+        delete e;
+        return fail(KRILL_ERR_PEER, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(ce));
+      }
+      src = static_cast<uint8_t*>(ptr);
+      dp->ipc_maps[hk] = src;
+    }
+    e->blocks.assign(src_blocks.size(), -1);
+    for (size_t i = 0; i < src_blocks.size(); ++i) {
+      if (src_blocks[i] < 0) continue;
+      krill_status_t st = block_alloc(dp, &e->blocks[i]);
+      cudaError_t ce = cudaSuccess;
+      if (st == KRILL_OK)
+        ce = cudaMemcpyAsync(dp->block_ptr(e->blocks[i]), src + (int64_t)src_blocks[i] * g.block_bytes,
+                             (size_t)g.block_bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+      if (st != KRILL_OK || ce != cudaSuccess) {
+        for (int32_t bb : e->blocks) block_unref(dp, bb);
+        delete e;
+        return st != KRILL_OK ? st : fail(KRILL_ERR_PEER, "peer copy: %s", cudaGetErrorString(ce));
+      }
+    }
+    if (large) CUDA_TRY(cudaMemsetAsync(dp->d_err + 1, 1, 1, (cudaStream_t)stream));
+  }
   std::lock_guard<std::mutex> lk(dst->mu);
   insert_locked(dst, e);
   e->refs.fetch_add(1);

@@ -161,3 +161,23 @@ def test_disk_tier_needs_a_device_pool(tmp_path):
     assert e.value.status == L.KRILL_ERR_NO_DEVICE
     pc.wait_for_disk_writes()
     pc.close()
+
+
+def test_entry_descriptor_and_ipc_need_devices():
+    p = kb.KVPool(2, 8, 32, 128, num_blocks=8, device=-1)
+    pc = kb.PrefixCache(p)
+    s = p.create_sequence()
+    arr = (C.c_uint64 * 1)(s.handle)
+    L.check(L.lib.krill_append_quantize(p.handle, 1, arr, 0, 2, 300, None, None, L.DTYPE_BF16, None))
+    pc.store_quantized(list(range(300)), "m", s)
+    hit = pc.lookup_quantized(list(range(300)), "m")
+    desc = pc.describe(hit)
+    assert desc[:4] == b"KKV1" and len(desc) > 300 * 8
+    with pytest.raises(kb.KrillError) as e:
+        p.ipc_handle()
+    assert e.value.status == L.KRILL_ERR_NO_DEVICE
+    with pytest.raises(kb.KrillError) as e:
+        pc.import_entry(b"\0" * 64, desc)
+    assert e.value.status == L.KRILL_ERR_NO_DEVICE
+    hit.release()
+    pc.close()

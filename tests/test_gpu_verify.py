@@ -1,0 +1,69 @@
+"""Multi-query verify attention over the int8 cache (speculative decoding;
+the batched verify forward with buildBatchedVerifyMask,
+BatchedDecode.swift:299-312): after n_query draft tokens are appended, query
+j must equal single-token decode attention over the cache up to and
+including draft j (oracle: the reference's dequantize + SDPA). Tolerance as
+for decode attention: max-abs 2e-3 on fp32 outputs."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from tests._data import BF16, F16, kv_values, to_bits
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import krill_b200 as kb  # noqa: E402
+from tests._gpu import dev_bits, prefill  # noqa: E402
+from tests.test_gpu_attention import ATOL  # noqa: E402
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,nq", [
+    (128, 64, 32, 8, BF16, 4),
+    (128, 64, 32, 4, BF16, 2),
+    (64, 64, 32, 8, F16, 5),
+    (256, 64, 8, 4, F16, 3),
+])
+def test_verify_matches_sequential_oracle(D, G, hq, hkv, dtype, nq):
+    rng = np.random.default_rng(9)
+    layers = 2
+    scale = 1 / math.sqrt(D)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=48, group_size=G)
+    lengths = [1, 63, 64, 300, 700]
+    seqs, K, V = [], [], []
+    for L in lengths:
+        s = pool.create_sequence()
+        k = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        v = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        prefill(pool, s, k, v, dtype)
+        seqs.append(s)
+        K.append(k)
+        V.append(v)
+    n = len(seqs)
+    kd = to_bits(kv_values(rng, (layers, n, hkv, nq, D)), dtype)
+    vd = to_bits(kv_values(rng, (layers, n, hkv, nq, D)), dtype)
+    kb.append_quantize(pool, seqs, 0, dev_bits(kd, dtype), dev_bits(vd, dtype))
+    qb = to_bits(kv_values(rng, (layers, n, nq, hq, D)), dtype)
+    out = torch.empty((layers, n, nq, hq, D), dtype=torch.float32, device="cuda")
+    kb.verify_attention(pool, seqs, 0, dev_bits(qb, dtype), out, scale)
+    torch.cuda.synchronize()
+    assert pool.device_error() == 0
+    got = out.cpu().numpy().astype(np.float64)
+    for i in range(n):
+        for layer in range(layers):
+            kk = np.concatenate([K[i][layer], kd[layer, i]], axis=1)
+            vv = np.concatenate([V[i][layer], vd[layer, i]], axis=1)
+            ck, sk, zk = oracle.quantize(kk, dtype, G)
+            cv, sv, zv = oracle.quantize(vv, dtype, G)
+            for j in range(nq):
+                t = lengths[i] + j + 1  # the cache as the sequential step j sees it
+                ref = oracle.reference_attention(ck[:, :t], sk[:, :t], zk[:, :t], cv[:, :t], sv[:, :t],
+                                                 zv[:, :t], qb[layer, i, j], dtype, G, scale)
+                err = np.abs(got[layer, i, j] - ref).max()
+                assert err <= ATOL, f"seq {i} layer {layer} query {j}: {err:.3e}"
+    pool.close()

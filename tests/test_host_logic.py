@@ -385,3 +385,23 @@ def test_cascade_shared_part_stays_below_every_length():
     attend(p, [a, b, base])
     assert p.last_cascade()[0] == 1
     pc.close()
+
+
+def test_verify_attention_planning():
+    """Multi-query verify: one unit per query, each bounded by its own token
+    (buildBatchedVerifyMask, BatchedDecode.swift:299-312); the queries must be
+    in the cache; full-history pools only."""
+    p = pool(layers=2, blocks=64)
+    a, b = p.create_sequence(), p.create_sequence()
+    append(p, [a], 500)
+    append(p, [b], 3)
+    arr = (C.c_uint64 * 2)(a.handle, b.handle)
+    L.check(L.lib.krill_verify_attention(p.handle, 2, arr, 0, 2, 3, None, 1, None, 2, 1.0, None))
+    with pytest.raises(kb.KrillError):
+        L.check(L.lib.krill_verify_attention(p.handle, 2, arr, 0, 2, 4, None, 1, None, 2, 1.0, None))
+    w = pool(layers=2, blocks=64, window=1024, max_append=512)
+    s = w.create_sequence()
+    append(w, [s], 100)
+    arr1 = (C.c_uint64 * 1)(s.handle)
+    st = L.lib.krill_verify_attention(w.handle, 1, arr1, 0, 2, 2, None, 1, None, 2, 1.0, None)
+    assert st == L.KRILL_ERR_INVALID
