@@ -232,11 +232,23 @@ krill_status_t krill_decode_attention(krill_pool_t pool, int32_t n_seqs, const k
  * krill_append_quantize with n_new = n_query) are the queries; query j attends
  * the cache up to and including its own token and none of the later drafts, so
  * the result equals n_query sequential single-token decode steps.
- * q / out: [layer_count][n_seqs][n_query][Hq][D]. Full-history pools only. */
+ * q / out: [layer_count][n_seqs][n_query][Hq][D]. Full-history pools only.
+ * Few queries run as one decode unit per query; many (n_query x GQA group >=
+ * 64, head_dim <= 128, tensor-core implementation) run as causal tcgen05
+ * items that read each sequence's K/V once per block of 256 query rows. */
 krill_status_t krill_verify_attention(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
                                       int32_t layer_begin, int32_t layer_count, int32_t n_query,
                                       const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
                                       float scale, void* stream);
+/* Chunked-prefill attention over the int8 cache (chunkedTextPrefill,
+ * InferenceEngine.swift:3122-3147: each chunk's K/V goes into the cache, then
+ * the chunk's queries attend the whole cache causally). The same operation as
+ * krill_verify_attention with n_query = the chunk length: append the chunk
+ * first, then call this. */
+krill_status_t krill_prefill_attention(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                       int32_t layer_begin, int32_t layer_count, int32_t n_query,
+                                       const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                                       float scale, void* stream);
 
 /* Allocation-free decode attention. No counterpart in the reference: it
  * exists for callers that cannot have the library allocate memory while they

@@ -94,6 +94,7 @@ _SIGS = {
     "krill_seq_blocks": (i32, [vp, u64, P_i32, i32, P_i32]),
     "krill_append_quantize": (i32, [vp, i32, P_u64, i32, i32, i32, vp, vp, i32, vp]),
     "krill_verify_attention": (i32, [vp, i32, P_u64, i32, i32, i32, vp, i32, vp, i32, C.c_float, vp]),
+    "krill_prefill_attention": (i32, [vp, i32, P_u64, i32, i32, i32, vp, i32, vp, i32, C.c_float, vp]),
     "krill_append_quantize_rope": (i32, [vp, i32, P_u64, i32, i32, i32, vp, vp, i32, vp, vp, i64, vp]),
     "krill_decode_attention": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),
     "krill_decode_attention_noalloc": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),

@@ -341,6 +341,17 @@ def verify_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float,
     return out
 
 
+def prefill_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float, stream=None):
+    """Chunked-prefill attention (InferenceEngine.swift:3122-3147): the chunk's
+    K/V are already appended; q/out [layer_count, n_seqs, chunk, Hq, D]."""
+    lc, ns, nq = q.shape[0], q.shape[1], q.shape[2]
+    assert ns == len(seqs)
+    arr = _seq_array(seqs)
+    check(L.lib.krill_prefill_attention(pool.handle, ns, arr, layer_begin, lc, nq, _ptr(q), _dt(q),
+                                        _ptr(out), _dt(out), scale, _stream(stream)))
+    return out
+
+
 def decode_attention(pool: KVPool, seqs, layer_begin: int, q, out, scale: float, stream=None):
     """q/out: [layer_count, n_seqs, Hq, D]."""
     lc, ns = q.shape[0], q.shape[1]

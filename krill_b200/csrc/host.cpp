@@ -105,7 +105,13 @@ struct Plan {
   std::vector<uint8_t> dry;
   std::vector<int64_t> nsb;
   std::vector<int32_t> split_units;
-  // cascade (shared-prefix) planning
+  // cascade (shared-prefix / causal) planning
+  struct Pair {
+    int32_t layer, leader;
+    int64_t n_sb;
+    int32_t mem_off, n_rows, h, causal;
+  };
+  std::vector<Pair> pairs;
   std::vector<int32_t> gorder, gstart, gmembers, seq_sh;
   std::vector<int64_t> gshared;
   std::vector<ShItem> sh_items;
@@ -442,6 +448,11 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   if (n_query < 1) return fail(KRILL_ERR_INVALID, "n_query must be positive");
   if (n_query > 1 && p->windowed())
     return fail(KRILL_ERR_INVALID, "multi-query verify attention needs a full-history pool");
+  // Many queries per sequence (chunked prefill, long verify) run as causal
+  // tcgen05 cascade items: the sequence's K/V is read once per query block.
+  const bool causal_path = n_query > 1 && p->geom.fmt == kFmtInt8 &&
+                           shared_uses_umma(p->geom, p->cfg.attn_impl) &&
+                           (int64_t)n_query * p->geom.g >= 64;
   TRY(check_dtype16(q_dtype, "q"));
   if (p->geom.fmt == kFmtBf16 && q_dtype != KRILL_DTYPE_BF16)
     return fail(KRILL_ERR_INVALID, "attention over a bf16 pool takes a BF16 q");
@@ -551,7 +562,9 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
         u.t_lo = (int32_t)t_lo;
         u.t_hi = (int32_t)t_hi;
         u.n_pre = 0;
-        pl.nsb[ui] = (t_hi + g.subt - 1) / g.subt - std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
+        pl.nsb[ui] = causal_path ? 0
+                                 : (t_hi + g.subt - 1) / g.subt -
+                                       std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
         total_sb += pl.nsb[ui];
       }
     }
@@ -574,22 +587,52 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     C = 8;
     while (C < 128 && (int64_t)(2 * C) * HG <= quarter) C *= 2;
   }
-  // ---- cascade items: (group, layer, row block, kv head) pairs cut into
-  // fragments. The pairs' sub-blocks are laid end to end and split into
-  // equal contiguous ranges, one per CTA; the fragment index within a pair is
-  // its partial-record slot. Pairs that read the same blocks are adjacent, so
-  // the CTAs working on them run side by side and share L2.
+  // ---- cascade items: (layer, row block, kv head) pairs cut into fragments.
+  // A pair is either a shared-prefix group (rows = member sequences x GQA
+  // group, tokens = the common blocks) or, on the causal path, a block of one
+  // sequence's queries (rows = queries x GQA group, tokens = everything up to
+  // the block's last query, masked per row). The pairs' sub-blocks are laid
+  // end to end and split into equal contiguous ranges, one per CTA; the
+  // fragment index within a pair is its partial-record slot. Pairs that read
+  // the same blocks are adjacent, so the CTAs working on them share L2.
   pl.sh_items.clear();
   pl.sh_members.clear();
   pl.sh_cta.clear();
+  pl.pairs.clear();
   int n_pslots = 0, sh_grid = 0;
-  if (n_groups > 0) {
+  {
     const int mem_cap = std::max(1, shared_rows(g, p->cfg.attn_impl) / g.g);
-    int64_t W = 0;
     for (int gi = 0; gi < n_groups; ++gi) {
+      const int32_t* mem = pl.gmembers.data() + pl.gstart[gi];
       const int n_mem = pl.gstart[gi + 1] - pl.gstart[gi];
-      W += (int64_t)lc * ((n_mem + mem_cap - 1) / mem_cap) * g.Hkv * (pl.gshared[gi] / g.subt);
+      for (int li = 0; li < lc; ++li)
+        for (int mb = 0; mb < n_mem; mb += mem_cap) {
+          const int nm = std::min(mem_cap, n_mem - mb);
+          const int32_t mem_off = (int32_t)pl.sh_members.size();
+          for (int k = 0; k < nm; ++k) pl.sh_members.push_back((int32_t)((int64_t)li * n_seqs + mem[mb + k]));
+          for (int h = 0; h < g.Hkv; ++h)
+            pl.pairs.push_back(Plan::Pair{lb + li, mem[0], pl.gshared[gi] / g.subt, mem_off, nm * g.g, h, -1});
+        }
     }
+    if (causal_path)
+      for (int li = 0; li < lc; ++li)
+        for (int si = 0; si < n_seqs; ++si) {
+          const int64_t len = pl.sv[si]->len[lb + li];
+          for (int q0 = 0; q0 < n_query; q0 += mem_cap) {
+            const int nq = std::min(mem_cap, n_query - q0);
+            const int32_t mem_off = (int32_t)pl.sh_members.size();
+            for (int k = 0; k < nq; ++k)
+              pl.sh_members.push_back((int32_t)(((int64_t)li * n_seqs + si) * n_query + q0 + k));
+            const int64_t first_pos = len - n_query + q0;  // position of the block's first query
+            const int64_t n_sb = (first_pos + nq + g.subt - 1) / g.subt;
+            for (int h = 0; h < g.Hkv; ++h)
+              pl.pairs.push_back(Plan::Pair{lb + li, si, n_sb, mem_off, nq * g.g, h, (int32_t)first_pos});
+          }
+        }
+  }
+  if (!pl.pairs.empty()) {
+    int64_t W = 0;
+    for (const Plan::Pair& pr : pl.pairs) W += pr.n_sb;
     constexpr int64_t kMinFragment = 8;  // sub-blocks
     const int64_t grid_sh =
         std::max<int64_t>(1, std::min<int64_t>(p->num_sms, (W + kMinFragment - 1) / kMinFragment));
@@ -597,36 +640,26 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     sh_grid = (int)((W + per - 1) / per);
     pl.sh_cta.assign((size_t)sh_grid + 1, 0);
     int64_t pos = 0;
-    for (int gi = 0; gi < n_groups; ++gi) {
-      const int32_t* mem = pl.gmembers.data() + pl.gstart[gi];
-      const int n_mem = pl.gstart[gi + 1] - pl.gstart[gi];
-      const int64_t n_sb = pl.gshared[gi] / g.subt;
-      for (int li = 0; li < lc; ++li)
-        for (int mb = 0; mb < n_mem; mb += mem_cap) {
-          const int nm = std::min(mem_cap, n_mem - mb);
-          const int32_t mem_off = (int32_t)pl.sh_members.size();
-          for (int k = 0; k < nm; ++k) pl.sh_members.push_back((int32_t)((int64_t)li * n_seqs + mem[mb + k]));
-          for (int h = 0; h < g.Hkv; ++h) {
-            const int64_t a = pos, b = pos + n_sb;
-            const int64_t first = a / per, last = (b - 1) / per;
-            for (int64_t c = first; c <= last; ++c) {
-              ShItem it{};
-              it.layer = lb + li;
-              it.leader = mem[0];
-              it.sb_begin = (int32_t)(std::max(a, c * per) - a);
-              it.sb_end = (int32_t)(std::min(b, (c + 1) * per) - a);
-              it.mem_off = mem_off;
-              it.n_rows = (int16_t)(nm * g.g);
-              it.h = (int16_t)h;
-              it.slot = (int16_t)(c - first);
-              it.n_frag = (int16_t)(last - first + 1);
-              pl.sh_items.push_back(it);
-              pl.sh_cta[(size_t)c + 1] += 1;
-            }
-            n_pslots = std::max<int>(n_pslots, (int)(last - first + 1));
-            pos = b;
-          }
-        }
+    for (const Plan::Pair& pr : pl.pairs) {
+      const int64_t a = pos, b = pos + pr.n_sb;
+      const int64_t first = a / per, last = (b - 1) / per;
+      for (int64_t c = first; c <= last; ++c) {
+        ShItem it{};
+        it.layer = pr.layer;
+        it.leader = pr.leader;
+        it.sb_begin = (int32_t)(std::max(a, c * per) - a);
+        it.sb_end = (int32_t)(std::min(b, (c + 1) * per) - a);
+        it.mem_off = pr.mem_off;
+        it.n_rows = (int16_t)pr.n_rows;
+        it.h = (int16_t)pr.h;
+        it.slot = (int16_t)(c - first);
+        it.n_frag = (int16_t)(last - first + 1);
+        it.causal = pr.causal;
+        pl.sh_items.push_back(it);
+        pl.sh_cta[(size_t)c + 1] += 1;
+      }
+      n_pslots = std::max<int>(n_pslots, (int)(last - first + 1));
+      pos = b;
     }
     for (int c = 0; c < sh_grid; ++c) pl.sh_cta[(size_t)c + 1] += pl.sh_cta[(size_t)c];
   }
@@ -636,6 +669,14 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.split_units.clear();
   for (int64_t ui = 0; ui < n_units; ++ui) {
     AttnUnit& u = pl.units[ui];
+    if (causal_path) {  // every record comes from the causal cascade items
+      u.first_split = (int32_t)split_count;
+      u.n_pre = 0;
+      u.n_split = (int32_t)n_pslots;
+      split_count += n_pslots;
+      pl.split_units.push_back((int32_t)ui);
+      continue;
+    }
     const int64_t n_sb = pl.nsb[ui];
     const int64_t n_it = (n_sb + C - 1) / C;
     const int64_t base = n_sb / n_it, extra = n_sb % n_it;
@@ -788,7 +829,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.n_pslots = n_pslots;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
-  p->kernels += 1 + (pl.split_units.empty() ? 0 : 1) + (sh_grid > 0 ? 1 : 0);
+  p->kernels += (grid > 0 ? 1 : 0) + (pl.split_units.empty() ? 0 : 1) + (sh_grid > 0 ? 1 : 0);
   TRY(stage_release(slot, stream));
   return KRILL_OK;
 }
@@ -1208,6 +1249,14 @@ krill_status_t krill_verify_attention(krill_pool_t p, int32_t n_seqs, const kril
   DeviceGuard dg(p->device);
   return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
                       (cudaStream_t)stream, n_query);
+}
+
+krill_status_t krill_prefill_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                       int32_t layer_begin, int32_t layer_count, int32_t n_query,
+                                       const void* q, int32_t q_dtype, void* out, int32_t out_dtype,
+                                       float scale, void* stream) {
+  return krill_verify_attention(p, n_seqs, seqs, layer_begin, layer_count, n_query, q, q_dtype, out,
+                                out_dtype, scale, stream);
 }
 
 krill_status_t krill_decode_step(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,

@@ -78,7 +78,10 @@ struct ShItem {
   int16_t h;         // kv head
   int16_t slot;      // partial-record slot of this fragment
   int16_t n_frag;    // fragments of this (members, layer, head)
-  int32_t pad;
+  int32_t causal;    // -1: every row sees every token. Else the rows are the
+                     // queries (row / g) of one sequence at positions causal +
+                     // row / g, each seeing tokens up to its own (multi-query
+                     // verify / chunked prefill)
 };
 
 // Query rows of one cascade item: 8 consumer warps x 32 rows (16 at D = 256,
@@ -136,6 +139,8 @@ cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
 cudaError_t launch_shared(const Geom& g, const AttnParams& p, cudaStream_t stream);
+// Merge the partial records of p.split_units (attn_combine_kernel) on its own.
+cudaError_t launch_combine(const Geom& g, const AttnParams& p, cudaStream_t stream);
 // The cascade runs on tcgen05 (accumulators in tensor memory, 256 query rows
 // per item as two 128-row halves) for head_dim <= 128 under
 // KRILL_ATTN_TENSOR_CORE; otherwise on mma.sync (sh_rows(D) rows per item).

@@ -973,14 +973,24 @@ cudaError_t launch_cc(const AttnParams& p, int grid, cudaStream_t stream) {
 }
 }  // namespace
 
+cudaError_t launch_combine(const Geom& g, const AttnParams& p, cudaStream_t stream) {
+  if (p.n_split_units == 0) return cudaSuccess;
+  const unsigned blocks = (unsigned)p.n_split_units * p.Hkv;
+  if (g.D == 64) attn_combine_kernel<64><<<blocks, 128, 0, stream>>>(p);
+  else if (g.D == 128) attn_combine_kernel<128><<<blocks, 128, 0, stream>>>(p);
+  else if (g.D == 256) attn_combine_kernel<256><<<blocks, 128, 0, stream>>>(p);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream) {
-  if (grid <= 0) return cudaSuccess;
   if (p.sh_grid > 0) {  // shared-prefix fragments first: they fill partial records
     const cudaError_t e = shared_uses_umma(g, impl) ? launch_shared_umma(g, p, stream)
                                                     : launch_shared(g, p, stream);
     if (e != cudaSuccess) return e;
   }
+  if (grid <= 0) return launch_combine(g, p, stream);  // everything was in cascade items
   if (impl == 1) {  // KRILL_ATTN_CUDA_CORE
     if (g.D == 64 && g.NG == 1) return launch_cc<64, 1>(p, grid, stream);
     if (g.D == 128 && g.NG == 2) return launch_cc<128, 2>(p, grid, stream);

@@ -514,6 +514,17 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
           s0[i] *= p.scale_log2;
           s1[i] *= p.scale_log2;
         }
+        if (item.causal >= 0) {  // tokens after this row's own position
+          const int pos0 = (item.sb_begin + j) * 64;
+          const int lim = item.causal + row / gq - pos0;  // last visible token in this tile
+          if (lim < 63) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i > lim) s0[i] = -INFINITY;
+              if (32 + i > lim) s1[i] = -INFINITY;
+            }
+          }
+        }
         const float mx = max64(s0, s1);
         // O_h and P_h were last used by the P·V of tile c-1: wait for it only
         // where they are touched (rare O rescale, then the P write)
@@ -521,13 +532,13 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         if (j == 0) {
           m = mx;  // O is overwritten by this item's first P·V
         } else {
-          const bool grow = mx > m + 8.f;
+          const bool grow = mx > m + 8.f || (m == -INFINITY && mx > -INFINITY);
           if (__any_sync(0xffffffffu, grow)) {
             mbar_wait(bar(SM::B_PD + h), (c - 1) & 1, cta_abort, p.err);
             tc_fence_after();
             pv_done = true;
             const float mn = grow ? mx : m;
-            const float al = exp2f(m - mn);
+            const float al = m == -INFINITY ? 0.f : exp2f(m - mn);
             m = mn;
             l *= al;
 #pragma unroll 1
@@ -543,10 +554,12 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         float ps[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) ps[k] = 0.f;
+        // a row that has seen no visible token yet (causal) keeps m = -inf
+        const float base = m == -INFINITY ? 0.f : m;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          s0[i] = exp2f(s0[i] - m);
-          s1[i] = exp2f(s1[i] - m);
+          s0[i] = exp2f(s0[i] - base);
+          s1[i] = exp2f(s1[i] - base);
           ps[i & 7] += s0[i] + s1[i];
         }
         l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));

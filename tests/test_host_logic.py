@@ -405,3 +405,19 @@ def test_verify_attention_planning():
     arr1 = (C.c_uint64 * 1)(s.handle)
     st = L.lib.krill_verify_attention(w.handle, 1, arr1, 0, 2, 2, None, 1, None, 2, 1.0, None)
     assert st == L.KRILL_ERR_INVALID
+
+
+def test_prefill_attention_takes_the_causal_cascade_path():
+    """Many queries per sequence (chunked prefill) become causal tcgen05
+    cascade items; a short verify (n_query x GQA group < 64 rows) stays on the
+    per-query decode units."""
+    p = pool(layers=2, blocks=64)
+    s = p.create_sequence()
+    append(p, [s], 1300)
+    arr = (C.c_uint64 * 1)(s.handle)
+    L.check(L.lib.krill_prefill_attention(p.handle, 1, arr, 0, 2, 300, None, 1, None, 2, 1.0, None))
+    groups, items, slots, ctas = p.last_cascade()
+    assert groups == 0 and items >= 2 * 8 * 5 and slots >= 1 and ctas >= 1  # 1200 rows -> 5 blocks
+    assert p.last_plan()[2] == 0  # no decode items
+    L.check(L.lib.krill_verify_attention(p.handle, 1, arr, 0, 2, 4, None, 1, None, 2, 1.0, None))
+    assert p.last_cascade()[1] == 0 and p.last_plan()[2] > 0
