@@ -56,6 +56,7 @@ CONFIGS = {
                                 prefix=4096, suffix=256),
 }
 DEFAULT_CONFIG = "llama31_8b_batch32"
+L2_FLUSH_BYTES = 256 << 20  # 2 x the B200's 126 MB L2, rounded up
 
 
 def algo_bytes_attn(L, hkv, D, G):
@@ -523,6 +524,8 @@ def main():
     ap.add_argument("--kv", default="int8", choices=["int8", "bf16"],
                     help="pool format; bf16 = the unquantized comparison variant (default workload)")
     ap.add_argument("--split-tokens", type=int, default=0)
+    ap.add_argument("--e2e-chunk", type=int, default=0,
+                    help="layers per chunk of the host-buffer step (0 = one chunk)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layer-sample", type=int, default=12)
     ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (profiling)")
@@ -633,23 +636,36 @@ def main():
     torch.cuda.synchronize()
     barrier()
     len_before = [s.length(0) for s in seqs]
+    # A step whose bytes fit in L2 would be served from it on the next step:
+    # then each step is timed alone, with an L2 flush (a write of 2 x L2)
+    # between steps, outside the timed pairs. Otherwise the inputs are larger
+    # than L2 and the steps run back to back.
+    flush = None
+    if step_bytes([L + 1 for L in len_before], cfg, raw)[1] < L2_FLUSH_BYTES:
+        flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     # per-kernel CUDA events recorded by the library around each launch, on
     # the launching stream
     pool.set_profiling(True)
     pool.kernel_times()
     pool.kernel_count()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_pairs = 1 if flush is None else args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_pairs)]
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
-        start.record(stream)
         for i in range(args.steps):
+            if flush is not None:
+                flush.add_(1)
+            if flush is not None or i == 0:
+                evs[min(i, n_pairs - 1)][0].record(stream)
             kb.append_quantize(pool, seqs, 0, k_new, v_new, stream=stream)
             kb.decode_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
-        stop.record(stream)
+            if flush is not None or i == args.steps - 1:
+                evs[min(i, n_pairs - 1)][1].record(stream)
         torch.cuda.synchronize()
     barrier()
     launches = pool.kernel_count()
-    total_ms = start.elapsed_time(stop)
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
     attn_total, attn_n, app_total, app_n = pool.kernel_times()
     pool.set_profiling(False)
     attn_ms = [attn_total / max(1, attn_n)]
@@ -677,19 +693,27 @@ def main():
     h_v = torch.empty(v_new.shape, dtype=tdt, pin_memory=True).copy_(v_new.cpu())
     h_q = torch.empty(q.shape, dtype=tdt, pin_memory=True).copy_(q.cpu())
     h_out = torch.empty(out.shape, dtype=tdt, pin_memory=True)
-    d_k, d_v, d_q = torch.empty_like(k_new), torch.empty_like(v_new), torch.empty_like(q)
     e2e_steps = max(3, args.steps // 2)
+    # krill_decode_step_host: the public call for a step whose inputs and
+    # output live in host memory; it overlaps the copies of one chunk of
+    # layers with the kernels of its neighbours. One untimed call first (it
+    # sizes the device staging), then wall-clock steps, each ending with the
+    # host waiting for its output.
+    kb.decode_step_host(pool, seqs, 0, h_k, h_v, h_q, h_out, cfg["scale"], layer_chunk=args.e2e_chunk,
+                        stream=stream)
     torch.cuda.synchronize()
     barrier()
-    t0 = time.perf_counter()
+    e2e_ms = []
     for _ in range(e2e_steps):
-        d_k.copy_(h_k, non_blocking=True)
-        d_v.copy_(h_v, non_blocking=True)
-        d_q.copy_(h_q, non_blocking=True)
-        kb.decode_step(pool, seqs, 0, d_k, d_v, d_q, out, cfg["scale"], stream=stream)
-        h_out.copy_(out, non_blocking=True)
+        if flush is not None:
+            flush.add_(1)
+            torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        kb.decode_step_host(pool, seqs, 0, h_k, h_v, h_q, h_out, cfg["scale"],
+                            layer_chunk=args.e2e_chunk, stream=stream)
         stream.synchronize()
-    e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e_s = max_over_ranks(sum(e2e_ms) / 1e3 / e2e_steps)
     barrier()
     if args.diag:
         print(f"[rank {rank}] timed {total_ms / args.steps:.3f} ms/step attn {attn_ms[0]:.3f} ms "
@@ -727,7 +751,9 @@ def main():
                        "head_dim": D, "group_size": G, "kv_in_dtype": cfg["dtype"],
                        "seqs_per_gpu": cfg["seqs"], "global_seqs": n_total,
                        "mean_len": float(np.mean(lengths_all)),
-                       "l2": f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)",
+                       "l2": (f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)" if flush is None
+                              else f"L2 flushed between steps ({step_b / 1e9:.3f} GB/step < "
+                                   f"{L2_FLUSH_BYTES / 1e9:.2f} GB; each step timed alone)"),
                        "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -737,7 +763,8 @@ def main():
                          "step_gbs": step_gbs, "algo_bytes_attn": attn_bytes,
                          "algo_bytes_step": step_b},
             "e2e": {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
+                    "layer_chunk": args.e2e_chunk, "ms_steps": [round(x, 4) for x in e2e_ms]},
             "gpu_launches": launches,
             "clocks": clk,
             "prefill_s": t_fill,

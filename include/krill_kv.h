@@ -286,6 +286,26 @@ krill_status_t krill_decode_step(krill_pool_t pool, int32_t n_seqs, const krill_
                                  int32_t q_dtype, void* out, int32_t out_dtype, float scale,
                                  void* stream);
 
+/* One decode step from HOST buffers (same layouts as krill_decode_step):
+ * k_new/v_new [layer_count][n_seqs][Hkv][1][D], q and out
+ * [layer_count][n_seqs][Hq][D]. The reference's cache calls take arrays in
+ * the unified memory of the Apple device (QuantizedKVCache.update,
+ * QuantizedKVCache.swift:118-142, then SDPA, Gemma4Model.swift:508,516); on a
+ * discrete GPU this call is that step with the transfers included. The layers
+ * are processed in chunks of layer_chunk (0 = all layers in one chunk):
+ * chunk c's inputs are copied in on a second stream while chunk c-1 computes,
+ * and its output is copied back on a third while chunk c+1 computes. The call
+ * returns once the work is enqueued on `stream`; `out` is complete when
+ * `stream` has finished. Page-locked host buffers (cudaHostAlloc or
+ * cudaHostRegister) let the copies overlap; pageable ones work, without the
+ * overlap. On an error after the first chunk, the layers of the chunks
+ * already enqueued have been appended. */
+krill_status_t krill_decode_step_host(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, const void* k_new,
+                                      const void* v_new, int32_t kv_dtype, const void* q,
+                                      int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                      int32_t layer_chunk, void* stream);
+
 /* ---- snapshots / restore -------------------------------------------------- */
 /* quantizedSnapshot() for one layer (QuantizedKVCache.swift:106-115): the raw
  * codes and fp16 scales/zeros of the retained rows, in the QuantizedKVSnapshot

@@ -99,6 +99,8 @@ _SIGS = {
     "krill_decode_attention": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),
     "krill_decode_attention_noalloc": (i32, [vp, i32, P_u64, i32, i32, vp, i32, vp, i32, f32, vp]),
     "krill_decode_step": (i32, [vp, i32, P_u64, i32, i32, vp, vp, i32, vp, i32, vp, i32, f32, vp]),
+    "krill_decode_step_host": (i32, [vp, i32, P_u64, i32, i32, vp, vp, i32, vp, i32, vp, i32, f32, i32,
+                                     vp]),
     "krill_seq_snapshot_quantized": (i32, [vp, u64, i32, vp, vp, vp, vp, vp, vp, vp]),
     "krill_seq_snapshot_dequantized": (i32, [vp, u64, i32, vp, vp, vp]),
     "krill_seq_restore_quantized": (i32, [vp, u64, i32, i64, i64, vp, vp, vp, vp, vp, vp, vp]),

@@ -373,6 +373,22 @@ def decode_step(pool: KVPool, seqs, layer_begin: int, k_new, v_new, q, out, scal
     return out
 
 
+def decode_step_host(pool: KVPool, seqs, layer_begin: int, k_new, v_new, q, out, scale: float,
+                     layer_chunk: int = 0, stream=None):
+    """decode_step with CPU tensors (page-locked for overlapped copies): the
+    transfers in and out run on their own streams, a chunk of layers ahead of
+    and behind the kernels. `out` is complete once `stream` has finished."""
+    for t, name in ((k_new, "k_new"), (v_new, "v_new"), (q, "q"), (out, "out")):
+        if t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous host tensor")
+    lc, ns = q.shape[0], q.shape[1]
+    arr = _seq_array(seqs)
+    check(L.lib.krill_decode_step_host(pool.handle, ns, arr, layer_begin, lc, _ptr(k_new), _ptr(v_new),
+                                       _dt(k_new), _ptr(q), _dt(q), _ptr(out), _dt(out), scale,
+                                       layer_chunk, _stream(stream)))
+    return out
+
+
 # ---------------------------------------------------------------- batch glue
 def stack_caches_left_padded_quantized(pool: KVPool, seqs, layer: int, s_max: Optional[int] = None,
                                        stream=None) -> QuantizedKVSnapshot:

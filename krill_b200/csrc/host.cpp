@@ -89,8 +89,12 @@ struct StageSlot {
   size_t cap = 0;
   cudaEvent_t ev = nullptr;
   bool pending = false;
+  bool owned = false;  // h/d allocated for this slot (else a slice of the pool's arena)
 };
-constexpr int kStageSlots = 8;
+constexpr int kStageSlots = 16;
+// Every slot starts as a slice of one pinned + one device arena made with the
+// pool, so no call allocates staging until a packet outgrows its slice.
+constexpr size_t kStageSliceBytes = 1 << 20;
 
 // Decode-attention planner buffers, reused across calls.
 __global__ void or_flag_kernel(int* dst, const int* src) { *dst |= *src; }
@@ -137,11 +141,15 @@ struct krill_pool_s {
   int num_sms = 148;
   float* d_partials = nullptr;
   int64_t partials_cap = 0;
+  unsigned long long* d_split_ctr = nullptr;  // arrival counters, one per partial record
+  uint32_t attn_epoch = 0;                    // launches of the decode kernel (never 0 in use)
   int64_t kernels = 0;  // device kernels launched since the last krill_pool_kernel_count
   std::map<std::string, uint8_t*> ipc_maps;  // other processes' pools opened here (handle bytes)
   int* d_err = nullptr;
   StageSlot stage[kStageSlots];
   int stage_next = 0;
+  uint8_t* stage_arena_h = nullptr;  // kStageSlots slices of kStageSliceBytes
+  uint8_t* stage_arena_d = nullptr;
   std::recursive_mutex mu;
   // kernel timing (measurement hook): event pairs around each launch
   bool profiling = false;
@@ -152,6 +160,14 @@ struct krill_pool_s {
   std::vector<Timed> timed;
   std::vector<cudaEvent_t> spare_events;
   Plan plan;
+  // krill_decode_step_host: device staging for the step's inputs and output,
+  // the two copy streams and the per-chunk events that order them.
+  struct HostIo {
+    uint8_t* d = nullptr;
+    int64_t cap = 0;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    std::vector<cudaEvent_t> ev;
+  } io;
 
   int64_t ring_tokens() const { return (int64_t)geom.ring * kBlockTokens; }
   bool windowed() const { return cfg.window > 0; }
@@ -266,11 +282,15 @@ krill_status_t stage_acquire(krill_pool_t p, size_t bytes, StageSlot** out) {
   }
   if (!s.ev) CUDA_TRY(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
   if (s.cap < bytes) {
-    if (s.h) cudaFreeHost(s.h);
-    if (s.d) cudaFree(s.d);
+    if (s.owned) {
+      if (s.h) cudaFreeHost(s.h);
+      if (s.d) cudaFree(s.d);
+    }
     s.h = nullptr;
     s.d = nullptr;
-    size_t cap = 1 << 20;
+    s.cap = 0;
+    s.owned = true;
+    size_t cap = kStageSliceBytes;
     while (cap < bytes) cap *= 2;
     CUDA_TRY(cudaMallocHost(&s.h, cap));
     CUDA_TRY(cudaMalloc(&s.d, cap));
@@ -432,9 +452,15 @@ krill_status_t ensure_scratch(krill_pool_t p, int64_t records, int64_t /*unused*
     // grows rarely (first launches); the free must not race kernels in flight
     CUDA_TRY(cudaDeviceSynchronize());
     if (p->d_partials) cudaFree(p->d_partials);
+    if (p->d_split_ctr) cudaFree(p->d_split_ctr);
     p->d_partials = nullptr;
+    p->d_split_ctr = nullptr;
+    p->partials_cap = 0;
     int64_t cap = std::max<int64_t>(records * pf * 3 / 2, 1 << 20);
     CUDA_TRY(cudaMalloc(&p->d_partials, (size_t)cap * sizeof(float)));
+    const int64_t n_ctr = cap / pf + 1;
+    CUDA_TRY(cudaMalloc(&p->d_split_ctr, (size_t)n_ctr * sizeof(unsigned long long)));
+    CUDA_TRY(cudaMemset(p->d_split_ctr, 0, (size_t)n_ctr * sizeof(unsigned long long)));
     p->partials_cap = cap;
   }
   return KRILL_OK;
@@ -576,14 +602,53 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   // CTA's share, halving the head group when even 8-sub-block pieces are too
   // coarse (small batches). Results depend only on shapes, never on contents.
   int C, HG = g.Hkv;
+  bool latency_bound = false;
   if (p->cfg.split_tokens > 0) {
     C = std::max(1, p->cfg.split_tokens / g.subt);
-  } else {
+  } else if ((latency_bound = (int64_t)8 * g.Hkv >
+                               std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4))) {
+    // Small batch (8-sub-block items of all kv heads would exceed a quarter of
+    // a CTA's share): the step is latency-bound, and its time is about the
+    // largest item plus, where a sequence is split over CTAs, the merge of
+    // the pieces through global memory. Splitting heads costs less: the R =
+    // 8 / HG warps of one head share its sub-blocks and merge in shared
+    // memory. So for each head group HG, take the shortest pieces (at least
+    // R sub-blocks, one per warp) that give at most one item per CTA, and
+    // keep the (HG, C) with the least estimated time in sub-blocks per warp:
+    // the item's share, plus for a split plan about 3 for the fence, count
+    // and merge latency and 1/8 per piece the merge reads.
     const int W = attn_warps(g.D);
+    int64_t max_nsb = 1;
+    for (int64_t ui = 0; ui < n_units; ++ui) max_nsb = std::max<int64_t>(max_nsb, pl.nsb[ui]);
+    auto n_items_for = [&](int hg, int64_t c) {
+      int64_t n = 0;
+      for (int64_t ui = 0; ui < n_units; ++ui) n += (pl.nsb[ui] + c - 1) / c;
+      return n * (g.Hkv / hg);
+    };
+    double best = 1e300;
+    C = 1;
+    for (int hg = g.Hkv; hg >= 1; hg /= 2) {
+      if (g.Hkv % hg != 0 || !(hg % W == 0 || W % hg == 0)) break;
+      const int64_t cmin = std::max(1, W / hg);
+      int64_t lo = cmin, hi = std::max<int64_t>(cmin, max_nsb);  // items fall as C grows
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) / 2;
+        if (n_items_for(hg, mid) > p->num_sms) lo = mid + 1;
+        else hi = mid;
+      }
+      const int64_t items = n_items_for(hg, lo);
+      const int64_t waves = (items + p->num_sms - 1) / p->num_sms;
+      const bool split = lo < max_nsb;
+      const double cost = (double)(waves * lo * hg) / W + (split ? 3.0 + (double)((max_nsb + lo - 1) / lo) / 8.0 : 0.0);
+      if (cost < best) {
+        best = cost;
+        HG = hg;
+        C = (int)std::min<int64_t>(lo, INT32_MAX);
+      }
+      if (hg % 2 != 0) break;
+    }
+  } else {
     const int64_t quarter = std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4);
-    while (HG > 1 && (int64_t)8 * HG > quarter && (HG % 2 == 0) &&
-           ((HG / 2) % W == 0 || W % (HG / 2) == 0))
-      HG /= 2;
     C = 8;
     while (C < 128 && (int64_t)(2 * C) * HG <= quarter) C *= 2;
   }
@@ -667,6 +732,12 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.items.clear();
   int64_t split_count = 0;
   pl.split_units.clear();
+  // In a latency-bound plan the decode piece that arrives last merges its
+  // split unit, which saves the combine kernel's launch and its serial
+  // latency. A bandwidth-bound plan keeps the combine kernel: there the
+  // fence and count that every split piece would pay cost more than the
+  // combine's ~1 % of the step. Units without decode pieces always need it.
+  bool merge_in_kernel = latency_bound && !causal_path;
   for (int64_t ui = 0; ui < n_units; ++ui) {
     AttnUnit& u = pl.units[ui];
     if (causal_path) {  // every record comes from the causal cascade items
@@ -693,6 +764,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       split_count += n_pslots;
     } else {
       u.n_split = (int32_t)(off + n_it);
+      u.n_pre = (int32_t)off;
+      if (u.n_split > 1 && n_it < 1) merge_in_kernel = false;
       if (u.n_split > 1) {
         split_count += u.n_split;
         pl.split_units.push_back((int32_t)ui);
@@ -819,6 +892,9 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.out_dtype = out_dtype;
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.partials = p->d_partials;
+  ap.split_ctr = merge_in_kernel ? p->d_split_ctr : nullptr;
+  if (++p->attn_epoch == 0) p->attn_epoch = 1;
+  ap.epoch = p->attn_epoch;
   ap.err = p->d_err;
   ap.large_scale = p->d_err + 1;
   if (sh_grid > 0) {
@@ -829,7 +905,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.n_pslots = n_pslots;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
-  p->kernels += (grid > 0 ? 1 : 0) + (pl.split_units.empty() ? 0 : 1) + (sh_grid > 0 ? 1 : 0);
+  p->kernels += (grid > 0 ? 1 : 0) + (attn_needs_combine(ap, grid, p->cfg.attn_impl) ? 1 : 0) +
+                (sh_grid > 0 ? 1 : 0);
   TRY(stage_release(slot, stream));
   return KRILL_OK;
 }
@@ -963,10 +1040,20 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     if (e == cudaSuccess) e = cudaMalloc(&p->d_err, 4 * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, 4 * sizeof(int));
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaMallocHost(&p->stage_arena_h, kStageSlots * kStageSliceBytes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->stage_arena_d, kStageSlots * kStageSliceBytes);
+    if (e == cudaSuccess)
+      for (int i = 0; i < kStageSlots; ++i) {
+        p->stage[i].h = p->stage_arena_h + (size_t)i * kStageSliceBytes;
+        p->stage[i].d = p->stage_arena_d + (size_t)i * kStageSliceBytes;
+        p->stage[i].cap = kStageSliceBytes;
+      }
     if (e != cudaSuccess) {
       krill_status_t code = (e == cudaErrorMemoryAllocation) ? KRILL_ERR_OOM : KRILL_ERR_CUDA;
       if (p->d_pool) cudaFree(p->d_pool);
       if (p->d_err) cudaFree(p->d_err);
+      if (p->stage_arena_h) cudaFreeHost(p->stage_arena_h);
+      if (p->stage_arena_d) cudaFree(p->stage_arena_d);
       delete p;
       cudaGetLastError();
       return fail(code, "pool allocation on device %d failed: %s", device, cudaGetErrorString(e));
@@ -982,18 +1069,25 @@ krill_status_t krill_pool_destroy(krill_pool_t p) {
     DeviceGuard dg(p->device);
     cudaDeviceSynchronize();
     for (auto& s : p->stage) {
-      if (s.h) cudaFreeHost(s.h);
-      if (s.d) cudaFree(s.d);
+      if (s.owned && s.h) cudaFreeHost(s.h);
+      if (s.owned && s.d) cudaFree(s.d);
       if (s.ev) cudaEventDestroy(s.ev);
     }
+    if (p->stage_arena_h) cudaFreeHost(p->stage_arena_h);
+    if (p->stage_arena_d) cudaFree(p->stage_arena_d);
     for (auto& e : p->timed) {
       cudaEventDestroy(e.a);
       cudaEventDestroy(e.b);
     }
     for (auto e : p->spare_events) cudaEventDestroy(e);
+    for (auto e : p->io.ev) cudaEventDestroy(e);
+    if (p->io.h2d) cudaStreamDestroy(p->io.h2d);
+    if (p->io.d2h) cudaStreamDestroy(p->io.d2h);
+    if (p->io.d) cudaFree(p->io.d);
     for (auto& m : p->ipc_maps) cudaIpcCloseMemHandle(m.second);
     if (p->d_pool) cudaFree(p->d_pool);
     if (p->d_partials) cudaFree(p->d_partials);
+    if (p->d_split_ctr) cudaFree(p->d_split_ctr);
     if (p->d_err) cudaFree(p->d_err);
   }
   delete p;
@@ -1271,6 +1365,104 @@ krill_status_t krill_decode_step(krill_pool_t p, int32_t n_seqs, const krill_seq
                 (cudaStream_t)stream));
   return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
                       (cudaStream_t)stream);
+}
+
+krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
+                                      int32_t layer_begin, int32_t layer_count, const void* k_new,
+                                      const void* v_new, int32_t kv_dtype, const void* q,
+                                      int32_t q_dtype, void* out, int32_t out_dtype, float scale,
+                                      int32_t layer_chunk, void* stream) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  TRY(require_device(p));
+  TRY(check_layers(p, layer_begin, layer_count));
+  TRY(check_dtype16(kv_dtype, "k/v"));
+  TRY(check_dtype16(q_dtype, "q"));
+  if (out_dtype != KRILL_DTYPE_F16 && out_dtype != KRILL_DTYPE_BF16 && out_dtype != KRILL_DTYPE_F32)
+    return fail(KRILL_ERR_INVALID, "out dtype must be F16, BF16 or F32");
+  if (n_seqs < 1 || !seqs) return fail(KRILL_ERR_INVALID, "need at least one sequence");
+  if (!k_new || !v_new || !q || !out) return fail(KRILL_ERR_INVALID, "null host buffer");
+  if (layer_chunk < 0) return fail(KRILL_ERR_INVALID, "layer_chunk must be >= 0");
+  DeviceGuard dg(p->device);
+  const Geom& g = p->geom;
+  // Bytes per layer of each buffer; the buffers are layer-major, so a chunk of
+  // layers is one contiguous range of each.
+  const int64_t kv_l = (int64_t)n_seqs * g.Hkv * g.D * 2;
+  const int64_t q_l = (int64_t)n_seqs * g.Hq * g.D * 2;
+  const int64_t o_l = (int64_t)n_seqs * g.Hq * g.D * (out_dtype == KRILL_DTYPE_F32 ? 4 : 2);
+  const int64_t k_off = 0, v_off = align16(kv_l * layer_count), q_off = 2 * v_off;
+  const int64_t o_off = q_off + (int64_t)align16(q_l * layer_count);
+  const int64_t need = o_off + (int64_t)align16(o_l * layer_count);
+  if (need > p->io.cap) {
+    CUDA_TRY(cudaDeviceSynchronize());  // earlier steps may still read the old staging
+    if (p->io.d) cudaFree(p->io.d);
+    p->io.d = nullptr;
+    p->io.cap = 0;
+    CUDA_TRY(cudaMalloc(&p->io.d, need));
+    p->io.cap = need;
+  }
+  if (!p->io.h2d) CUDA_TRY(cudaStreamCreateWithFlags(&p->io.h2d, cudaStreamNonBlocking));
+  if (!p->io.d2h) CUDA_TRY(cudaStreamCreateWithFlags(&p->io.d2h, cudaStreamNonBlocking));
+  // Chunking (layer_chunk = 0: one chunk). Measured at the Llama-3.1-8B
+  // batch of 32 (12.6 MB in, 8.4 MB out per step): 4 chunks overlap the
+  // copies but their launches lose more to ramp-up and tail (1.96 ms of
+  // kernels against 1.60 ms in one launch) than the 0.33 ms of copies they
+  // hide, so the default keeps the step in one launch.
+  int chunk = layer_chunk == 0 ? (int)layer_count : std::min(layer_chunk, (int)layer_count);
+  const int n_ch = (layer_count + chunk - 1) / chunk;
+  while ((int)p->io.ev.size() < 2 + 2 * n_ch) {
+    cudaEvent_t e = nullptr;
+    CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    p->io.ev.push_back(e);
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaEvent_t ev_start = p->io.ev[0], ev_end = p->io.ev[1];
+  uint8_t* d = p->io.d;
+  // Everything earlier on `stream` (the previous step's reads of the staging
+  // and its output copies, which it joined) precedes this step's uploads.
+  CUDA_TRY(cudaEventRecord(ev_start, s));
+  CUDA_TRY(cudaStreamWaitEvent(p->io.h2d, ev_start, 0));
+  auto copy_in = [&](int c) -> krill_status_t {
+    const int64_t c0 = (int64_t)c * chunk, lc = std::min<int64_t>(chunk, layer_count - c0);
+    CUDA_TRY(cudaMemcpyAsync(d + k_off + c0 * kv_l, (const uint8_t*)k_new + c0 * kv_l, lc * kv_l,
+                             cudaMemcpyHostToDevice, p->io.h2d));
+    CUDA_TRY(cudaMemcpyAsync(d + v_off + c0 * kv_l, (const uint8_t*)v_new + c0 * kv_l, lc * kv_l,
+                             cudaMemcpyHostToDevice, p->io.h2d));
+    CUDA_TRY(cudaMemcpyAsync(d + q_off + c0 * q_l, (const uint8_t*)q + c0 * q_l, lc * q_l,
+                             cudaMemcpyHostToDevice, p->io.h2d));
+    CUDA_TRY(cudaEventRecord(p->io.ev[2 + c], p->io.h2d));
+    return KRILL_OK;
+  };
+  // Chunk c+1's inputs are queued after chunk c's metadata uploads, so that
+  // those small copies never wait behind the next chunk's inputs.
+  krill_status_t rc = copy_in(0);
+  int issued = rc == KRILL_OK ? 1 : 0;
+  for (int c = 0; c < n_ch && rc == KRILL_OK; ++c) {
+    const int64_t c0 = (int64_t)c * chunk;
+    const int32_t lc = (int32_t)std::min<int64_t>(chunk, layer_count - c0);
+    CUDA_TRY(cudaStreamWaitEvent(s, p->io.ev[2 + c], 0));
+    rc = do_append(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc, 1, d + k_off + c0 * kv_l,
+                   d + v_off + c0 * kv_l, kv_dtype, s);
+    if (rc == KRILL_OK)
+      rc = do_attention(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc, d + q_off + c0 * q_l, q_dtype,
+                        d + o_off + c0 * o_l, out_dtype, scale, s);
+    if (rc != KRILL_OK) break;
+    if (c + 1 < n_ch) {
+      rc = copy_in(c + 1);
+      if (rc != KRILL_OK) break;
+      ++issued;
+    }
+    CUDA_TRY(cudaEventRecord(p->io.ev[2 + n_ch + c], s));
+    CUDA_TRY(cudaStreamWaitEvent(p->io.d2h, p->io.ev[2 + n_ch + c], 0));
+    CUDA_TRY(cudaMemcpyAsync((uint8_t*)out + c0 * o_l, d + o_off + c0 * o_l, (int64_t)lc * o_l,
+                             cudaMemcpyDeviceToHost, p->io.d2h));
+  }
+  // Join the copy streams back into `stream` even after an error, so that
+  // nothing of this call is left running unordered.
+  if (issued > 0) CUDA_TRY(cudaStreamWaitEvent(s, p->io.ev[2 + issued - 1], 0));
+  CUDA_TRY(cudaEventRecord(ev_end, p->io.d2h));
+  CUDA_TRY(cudaStreamWaitEvent(s, ev_end, 0));
+  return rc;
 }
 
 krill_status_t krill_seq_snapshot_quantized(krill_pool_t p, krill_seq_t h, int32_t layer,
@@ -2633,6 +2825,7 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   o.su_off = o.bt_off + align16((size_t)n_seqs * bt_stride * sizeof(int32_t));
   o.packet_bytes = o.su_off + align16((size_t)(n_split_units + 1) * sizeof(int32_t));
   o.partials_off = (o.packet_bytes + 255) & ~(size_t)255;
+  o.records = (int64_t)splits * g.Hkv;
   o.total_bytes = o.partials_off + (size_t)splits * g.Hkv * partial_floats(g.D) * sizeof(float);
   if (o.total_bytes > buf_cap)
     return fail(KRILL_ERR_INVALID,

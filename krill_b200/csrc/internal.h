@@ -49,8 +49,10 @@ struct AttnUnit {
   int32_t t_lo, t_hi;   // attended positions
   int32_t first_split;  // partial record of (piece i, head h): (first_split + i) * Hkv + h
   int32_t n_split;
-  int32_t n_pre;        // with n_split == 1: prefix records [first_split, + n_pre) written
-                        // by the cascade kernel, merged by the decode item that finishes
+  int32_t n_pre;        // prefix records [first_split, + n_pre) written by the cascade
+                        // kernel: with n_split == 1 merged by the decode item that
+                        // finishes; with n_split > 1 the first n_pre of the n_split
+                        // records (the decode pieces arrive as the other n_split - n_pre)
 };
 
 struct AttnItem {
@@ -98,8 +100,15 @@ struct AttnParams {
   const int32_t* cta_off;  // [grid + 1] item ranges per CTA
   const int32_t* bt;       // [n_seqs][bt_stride]
   int bt_stride;
-  const int32_t* split_units;  // units with n_split > 1 (merged by the combine kernel)
+  const int32_t* split_units;  // units with n_split > 1
   int n_split_units;
+  // Arrival counters of split units, one per partial record ((first_split +
+  // i) * Hkv + h, only i = 0 used): the decode piece that arrives last merges
+  // the unit's records. Each word is (epoch << 32 | arrivals); a word from
+  // another epoch counts as zero, so the counters never need clearing.
+  // nullptr: the combine kernel merges instead.
+  unsigned long long* split_ctr;
+  uint32_t epoch;
   const void* q;
   int q_dtype;
   void* out;
@@ -141,6 +150,12 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
 cudaError_t launch_shared(const Geom& g, const AttnParams& p, cudaStream_t stream);
 // Merge the partial records of p.split_units (attn_combine_kernel) on its own.
 cudaError_t launch_combine(const Geom& g, const AttnParams& p, cudaStream_t stream);
+// True when launch_attention runs the combine kernel: split units whose records
+// are not merged by the last-arriving decode piece (no counters, no decode
+// kernel, or the CUDA-core variant).
+inline bool attn_needs_combine(const AttnParams& p, int grid, int impl) {
+  return p.n_split_units > 0 && (grid <= 0 || impl == 1 || p.split_ctr == nullptr);
+}
 // The cascade runs on tcgen05 (accumulators in tensor memory, 256 query rows
 // per item as two 128-row halves) for head_dim <= 128 under
 // KRILL_ATTN_TENSOR_CORE; otherwise on mma.sync (sh_rows(D) rows per item).
@@ -153,6 +168,7 @@ inline int shared_rows(const Geom& g, int impl) { return shared_uses_umma(g, imp
 struct NoAllocPlan {
   size_t units_off, items_off, cta_off_off, bt_off, su_off;
   size_t packet_bytes, partials_off, total_bytes;
+  int64_t records;  // partial records (split pieces x kv heads)
   AttnParams ap;
   Geom geom;
   int grid, impl, device;

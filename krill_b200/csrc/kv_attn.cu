@@ -424,9 +424,94 @@ constexpr int stages_for() {
   return n > 16 ? 16 : n;
 }
 
+// Merge a split unit's n_split partial records for kv head h into the output,
+// in one warp: the piece that finished last does this in place of a combine
+// kernel. The arithmetic and its order are those of attn_combine_kernel
+// (max, then the weighted sums in record order), so both give the same bits.
+// Records written by other CTAs are read through L2 (ld.global.cg).
+template <int D>
+__device__ __forceinline__ void merge_split(const AttnParams& p, const AttnUnit& un, int h, int lane) {
+  const int g = p.g, n = un.n_split;
+  const int64_t stride = (int64_t)p.Hkv * partial_floats(D);
+  const float* base = p.partials + ((int64_t)un.first_split * p.Hkv + h) * partial_floats(D);
+  // lane j < g: max and normalizer of query head j
+  float M = -INFINITY, Ls = 0.f;
+  if (lane < g) {
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) M = fmaxf(M, __ldcg(base + i * stride + lane));
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) {
+      const float mi = __ldcg(base + i * stride + lane);
+      Ls += (mi == -INFINITY) ? 0.f : __ldcg(base + i * stride + 8 + lane) * exp2f(mi - M);
+    }
+  }
+  const float inv = 1.f / Ls;
+  constexpr int NC = D / 32;  // output dims per lane and query head
+  float acc[8][NC];
+#pragma unroll
+  for (int hq = 0; hq < 8; ++hq)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc[hq][c] = 0.f;
+#pragma unroll 2
+  for (int i = 0; i < n; ++i) {
+    const float* ri = base + i * stride;
+    const float mj = lane < g ? __ldcg(ri + lane) : -INFINITY;
+    const float wj = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
+#pragma unroll
+    for (int hq = 0; hq < 8; ++hq) {
+      if (hq < g) {
+        const float mh = __shfl_sync(0xffffffffu, mj, hq);
+        const float wh = __shfl_sync(0xffffffffu, wj, hq);
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const float o = __ldcg(ri + 16 + hq * D + lane + 32 * c);
+          acc[hq][c] = (mh == -INFINITY) ? acc[hq][c] : acc[hq][c] + o * wh;
+        }
+      }
+    }
+  }
+  const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
+#pragma unroll
+  for (int hq = 0; hq < 8; ++hq) {
+    if (hq < g) {
+      const float ih = __shfl_sync(0xffffffffu, inv, hq);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) store_out(p.out, p.out_dtype, orow + hq * D + lane + 32 * c, acc[hq][c] * ih);
+    }
+  }
+}
+
+// Count this piece's arrival at (unit, head h); true for the piece that
+// completes the unit (n_split - n_pre decode pieces; the n_pre prefix records
+// were finished by an earlier kernel). Called by the whole warp after its
+// partial record is stored.
+__device__ __forceinline__ bool arrive_split(const AttnParams& p, const AttnUnit& un, int h, int lane) {
+  __threadfence();  // this lane's record stores, device-wide, before the count
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    unsigned long long* c = p.split_ctr + (int64_t)un.first_split * p.Hkv + h;
+    const unsigned long long need = (unsigned long long)(un.n_split - un.n_pre);
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(c);
+    int tries = 0;
+    for (; tries < (1 << 16); ++tries) {
+      const unsigned long long cnt = (old >> 32) == p.epoch ? (old & 0xffffffffull) : 0ull;
+      const unsigned long long got = atomicCAS(c, old, ((unsigned long long)p.epoch << 32) | (cnt + 1));
+      if (got == old) {
+        last = cnt + 1 == need;
+        break;
+      }
+      old = got;
+    }
+    if (tries == (1 << 16)) atomicOr(p.err, kErrTimeout);
+    if (last) __threadfence();  // the other pieces' records, before reading them
+  }
+  return __shfl_sync(0xffffffffu, last, 0) != 0;
+}
+
 // Finish one (item, head) in the warp that holds the merged state: write the
-// normalized output, or a partial record plus the last-arriver merge when the
-// unit is split over several items.
+// normalized output, or a partial record plus, for the piece that arrives
+// last, the merge of the unit's records.
 template <int D>
 __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st, float l0,
                                             float l1, const AttnUnit& un, const AttnItem& item,
@@ -512,6 +597,7 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
     part[8 + h0] = l0;
     part[8 + h1] = l1;
   }
+  if (p.split_ctr != nullptr && arrive_split(p, un, h, lane)) merge_split<D>(p, un, h, lane);
 }
 
 // Merge the partial records of split units: one CTA per (split unit, kv head).
@@ -799,7 +885,7 @@ cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
       break;
     default: break;
   }
-  if (e != cudaSuccess || p.n_split_units == 0) return e;
+  if (e != cudaSuccess || p.n_split_units == 0 || p.split_ctr != nullptr) return e;
   attn_combine_kernel<D><<<p.n_split_units * p.Hkv, 128, 0, stream>>>(p);
   return cudaGetLastError();
 }

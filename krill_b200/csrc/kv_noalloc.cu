@@ -26,10 +26,17 @@ namespace {
 
 // The scratch every call shares: metadata packet, then partial records.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[KRILL_NOALLOC_SCRATCH_BYTES];
+// Arrival counters of split units (one per partial record; zero at load,
+// epoch-tagged after that). The scratch holds at most 16 MiB / (4 * (16 + 8 *
+// 64)) = 7,943 records, so 8,192 counters cover every head_dim.
+constexpr int kNoallocCounters = 8192;
+static __device__ unsigned long long g_noalloc_ctr[kNoallocCounters];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;                        // one call at a time through the shared buffers
 void* g_scratch_addr[kMaxDevices];      // device address of g_noalloc_scratch per device
+void* g_ctr_addr[kMaxDevices];          // device address of g_noalloc_ctr per device
+uint32_t g_epoch[kMaxDevices];          // decode launches per device
 alignas(64) uint8_t g_host_packet[KRILL_NOALLOC_SCRATCH_BYTES];  // host side of the metadata
 
 }  // namespace
@@ -62,6 +69,12 @@ extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int3
         break;
       }
       g_scratch_addr[np.device] = addr;
+      e = cudaGetSymbolAddress(&addr, g_noalloc_ctr);
+      if (e != cudaSuccess || !addr) {
+        rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+        break;
+      }
+      g_ctr_addr[np.device] = addr;
     }
     uint8_t* base = static_cast<uint8_t*>(g_scratch_addr[np.device]);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -79,8 +92,13 @@ extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int3
     ap.bt = reinterpret_cast<const int32_t*>(base + np.bt_off);
     ap.split_units = reinterpret_cast<const int32_t*>(base + np.su_off);
     ap.partials = reinterpret_cast<float*>(base + np.partials_off);
+    if (np.records <= kNoallocCounters) {
+      ap.split_ctr = static_cast<unsigned long long*>(g_ctr_addr[np.device]);
+      if (++g_epoch[np.device] == 0) g_epoch[np.device] = 1;
+      ap.epoch = g_epoch[np.device];
+    }
     e = launch_attention(np.geom, ap, np.grid, np.impl, s);
-    if (e == cudaSuccess) count_kernels(pool, 1 + (ap.n_split_units > 0 ? 1 : 0));
+    if (e == cudaSuccess) count_kernels(pool, 1 + (attn_needs_combine(ap, np.grid, np.impl) ? 1 : 0));
     if (e != cudaSuccess) rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
   } while (false);
   if (prev >= 0 && prev != np.device) cudaSetDevice(prev);

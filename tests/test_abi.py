@@ -91,6 +91,10 @@ def test_device_only_calls_on_host_pool():
     assert st == L.KRILL_ERR_NO_DEVICE
     st = L.lib.krill_decode_attention_noalloc(p.handle, 1, arr, 0, 2, None, 1, None, 1, 1.0, None)
     assert st == L.KRILL_ERR_NO_DEVICE
+    buf = (C.c_uint8 * 64)()
+    st = L.lib.krill_decode_step_host(p.handle, 1, arr, 0, 2, buf, buf, L.DTYPE_BF16, buf, L.DTYPE_BF16,
+                                      buf, L.DTYPE_BF16, 1.0, 0, None)
+    assert st == L.KRILL_ERR_NO_DEVICE
 
 
 def test_argument_errors():

@@ -1,0 +1,94 @@
+"""Decode step from host buffers (krill_decode_step_host): the layers run in
+chunks with their input and output copies overlapped on side streams. With a
+fixed split length a (layer, sequence) result does not depend on the rest of
+the call, so every chunking must give bit-identical outputs and cache
+contents to krill_decode_step on device buffers (itself checked against the
+oracle in test_gpu_attention.py)."""
+import numpy as np
+import pytest
+
+from tests._data import BF16, F16, kv_values, to_bits
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import krill_b200 as kb  # noqa: E402
+from tests._gpu import TORCH16, dev_bits, prefill  # noqa: E402
+
+
+def host_tensor(bits: np.ndarray, dtype: int, pinned: bool) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(TORCH16[dtype])
+    return t.pin_memory() if pinned else t.clone()
+
+
+def twin_pools(layers, hkv, hq, D, lengths, dtype, rng):
+    pools = [kb.KVPool(layers, hkv, hq, D, num_blocks=64, group_size=64, split_tokens=256)
+             for _ in range(2)]
+    seqs = [[], []]
+    for L in lengths:
+        k = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        v = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        for i in range(2):
+            s = pools[i].create_sequence()
+            prefill(pools[i], s, k, v, dtype)
+            seqs[i].append(s)
+    return pools, seqs
+
+
+@pytest.mark.parametrize("chunk,pinned,out_f32", [(0, True, False), (1, True, False), (4, True, True),
+                                                  (6, False, False), (3, False, True)])
+def test_host_step_matches_device_step(chunk, pinned, out_f32):
+    layers, hkv, hq, D, dtype = 6, 4, 16, 128, BF16
+    rng = np.random.default_rng(7 + chunk)
+    lengths = [300, 1, 777, 2049]
+    (pa, pb), (sa, sb) = twin_pools(layers, hkv, hq, D, lengths, dtype, rng)
+    n = len(lengths)
+    odt = torch.float32 if out_f32 else TORCH16[dtype]
+    stream = torch.cuda.current_stream()
+    for step in range(3):
+        k1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        v1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        qb = to_bits(kv_values(rng, (layers, n, hq, D)), dtype)
+        out_dev = torch.empty((layers, n, hq, D), dtype=odt, device="cuda")
+        kb.decode_step(pa, sa, 0, dev_bits(k1, dtype), dev_bits(v1, dtype), dev_bits(qb, dtype), out_dev,
+                       0.088, stream=stream)
+        out_host = torch.empty((layers, n, hq, D), dtype=odt, pin_memory=pinned)
+        out_host.fill_(float("nan"))
+        kb.decode_step_host(pb, sb, 0, host_tensor(k1, dtype, pinned), host_tensor(v1, dtype, pinned),
+                            host_tensor(qb, dtype, pinned), out_host, 0.088, layer_chunk=chunk,
+                            stream=stream)
+        stream.synchronize()
+        a = out_dev.cpu().view(torch.int32 if out_f32 else torch.int16)
+        b = out_host.view(torch.int32 if out_f32 else torch.int16)
+        assert torch.equal(a, b), f"step {step}: host-buffer step differs from the device step"
+    for i in range(n):
+        for layer in range(layers):
+            assert sa[i].length(layer) == sb[i].length(layer) == lengths[i] + 3
+    assert pa.device_error() == 0 and pb.device_error() == 0
+
+
+def test_host_step_layer_subrange_and_errors():
+    layers, hkv, hq, D, dtype = 4, 2, 8, 64, F16
+    rng = np.random.default_rng(3)
+    (pa, pb), (sa, sb) = twin_pools(layers, hkv, hq, D, [129, 640], dtype, rng)
+    n = 2
+    k1 = to_bits(kv_values(rng, (2, n, hkv, 1, D)), dtype)
+    v1 = to_bits(kv_values(rng, (2, n, hkv, 1, D)), dtype)
+    qb = to_bits(kv_values(rng, (2, n, hq, D)), dtype)
+    out_dev = torch.empty((2, n, hq, D), dtype=torch.float16, device="cuda")
+    kb.decode_step(pa, sa, 1, dev_bits(k1, dtype), dev_bits(v1, dtype), dev_bits(qb, dtype), out_dev, 0.125)
+    out_host = torch.empty((2, n, hq, D), dtype=torch.float16, pin_memory=True)
+    kb.decode_step_host(pb, sb, 1, host_tensor(k1, dtype, True), host_tensor(v1, dtype, True),
+                        host_tensor(qb, dtype, True), out_host, 0.125, layer_chunk=1)
+    torch.cuda.synchronize()
+    assert torch.equal(out_dev.cpu().view(torch.int16), out_host.view(torch.int16))
+    assert [s.length(0) for s in sb] == [129, 640] and [s.length(1) for s in sb] == [130, 641]
+    with pytest.raises(ValueError):
+        kb.decode_step_host(pb, sb, 1, dev_bits(k1, dtype), host_tensor(v1, dtype, True),
+                            host_tensor(qb, dtype, True), out_host, 0.125)
+    with pytest.raises(kb.KrillError):
+        kb.decode_step_host(pb, sb, 3, host_tensor(k1, dtype, True), host_tensor(v1, dtype, True),
+                            host_tensor(qb, dtype, True), out_host, 0.125)

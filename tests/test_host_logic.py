@@ -293,7 +293,16 @@ def test_planner_adapts_to_batch_shape():
     one = small.create_sequence()
     append(small, [one], 2048)
     C_, HG, items, ctas = attend(small, [one])
-    assert HG < 8 and ctas == 148  # heads split so one sequence fills the GPU
+    # latency-bound: one kv head per item, the whole sequence in it (16 layers
+    # x 8 heads = 128 items, no piece merged across CTAs)
+    assert HG == 1 and C_ == 32 and items == 128 and ctas == 128
+    # one long sequence on one layer: heads alone give 8 items, so the
+    # sequence is cut into pieces of at least 8 sub-blocks to fill the GPU
+    lone = pool(layers=1, D=64, blocks=200)
+    s1 = lone.create_sequence()
+    append(lone, [s1], 32768)
+    C_, HG, items, ctas = attend(lone, [s1])
+    assert HG == 1 and 8 <= C_ < 512 and 128 <= items <= 148
 
 
 def test_planner_fixed_split_is_batch_invariant():
