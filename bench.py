@@ -631,8 +631,7 @@ def main():
                   file=sys.stderr, flush=True)
         pool.set_profiling(False)
     for _ in range(args.warmup):
-        kb.append_quantize(pool, seqs, 0, k_new, v_new, stream=stream)
-        kb.decode_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+        kb.decode_step(pool, seqs, 0, k_new, v_new, q, out, cfg["scale"], stream=stream)
     torch.cuda.synchronize()
     barrier()
     len_before = [s.length(0) for s in seqs]
@@ -658,8 +657,7 @@ def main():
                 flush.add_(1)
             if flush is not None or i == 0:
                 evs[min(i, n_pairs - 1)][0].record(stream)
-            kb.append_quantize(pool, seqs, 0, k_new, v_new, stream=stream)
-            kb.decode_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+            kb.decode_step(pool, seqs, 0, k_new, v_new, q, out, cfg["scale"], stream=stream)
             if flush is not None or i == args.steps - 1:
                 evs[min(i, n_pairs - 1)][1].record(stream)
         torch.cuda.synchronize()
@@ -703,6 +701,18 @@ def main():
                         stream=stream)
     torch.cuda.synchronize()
     barrier()
+    # the host link as this process sees it (pinned copies of the query)
+    d_probe = torch.empty_like(q)
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    link = {}
+    for name, dst, src in (("h2d_gbs", d_probe, h_q), ("d2h_gbs", h_out, d_probe)):
+        for _ in range(3):
+            pe0.record(stream)
+            dst.copy_(src, non_blocking=True)
+            pe1.record(stream)
+            stream.synchronize()
+        link[name] = round(q.numel() * q.element_size() / (pe0.elapsed_time(pe1) / 1e3) / 1e9, 2)
+    del d_probe
     e2e_ms = []
     for _ in range(e2e_steps):
         if flush is not None:
@@ -764,7 +774,8 @@ def main():
                          "algo_bytes_step": step_b},
             "e2e": {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
-                    "layer_chunk": args.e2e_chunk, "ms_steps": [round(x, 4) for x in e2e_ms]},
+                    "layer_chunk": args.e2e_chunk, "ms_steps": [round(x, 4) for x in e2e_ms],
+                    "link": link},
             "gpu_launches": launches,
             "clocks": clk,
             "prefill_s": t_fill,

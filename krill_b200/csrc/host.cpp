@@ -105,7 +105,7 @@ struct Plan {
   std::vector<AttnItem> items;
   std::vector<int64_t> bucket;
   std::vector<int32_t> order, owner, count, fill;
-  std::vector<std::pair<int64_t, int32_t>> heap;
+  std::vector<uint64_t> heap;
   std::vector<uint8_t> dry;
   std::vector<int64_t> nsb;
   std::vector<int32_t> split_units;
@@ -796,25 +796,38 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   }
   pl.owner.resize((size_t)n_items);
   pl.count.assign((size_t)grid, 0);
+  // min-heap of (load << 20 | cta): one integer compare orders by load, then
+  // by CTA index
   pl.heap.resize((size_t)grid);
-  for (int c = 0; c < grid; ++c) pl.heap[c] = {0, c};  // already a min-heap
+  for (int c = 0; c < grid; ++c) pl.heap[c] = (uint64_t)c;  // already a min-heap
   auto sift_down = [&](size_t i) {
     const size_t n = pl.heap.size();
+    uint64_t* h = pl.heap.data();
+    const uint64_t v = h[i];
     for (;;) {
-      size_t m = i, l = 2 * i + 1, r = l + 1;
-      if (l < n && pl.heap[l] < pl.heap[m]) m = l;
-      if (r < n && pl.heap[r] < pl.heap[m]) m = r;
-      if (m == i) return;
-      std::swap(pl.heap[i], pl.heap[m]);
-      i = m;
+      size_t l = 2 * i + 1;
+      if (l >= n) break;
+      if (l + 1 < n && h[l + 1] < h[l]) ++l;
+      if (h[l] >= v) break;
+      h[i] = h[l];
+      i = l;
     }
+    h[i] = v;
   };
-  for (int32_t i : pl.order) {
-    auto& top = pl.heap[0];
-    pl.owner[i] = top.second;
-    pl.count[top.second] += 1;
-    top.first += pl.items[i].sb_end - pl.items[i].sb_begin;
-    sift_down(0);
+  if (n_items <= grid) {  // one item per CTA (latency-bound plans): no heap
+    for (int64_t r = 0; r < n_items; ++r) {
+      pl.owner[pl.order[r]] = (int32_t)r;
+      pl.count[r] = 1;
+    }
+  } else {
+    for (int32_t i : pl.order) {
+      uint64_t& top = pl.heap[0];
+      const int32_t c = (int32_t)(top & 0xfffffu);
+      pl.owner[i] = c;
+      pl.count[c] += 1;
+      top += (uint64_t)(pl.items[i].sb_end - pl.items[i].sb_begin) << 20;
+      sift_down(0);
+    }
   }
   // ---- metadata packet: units | items (grouped by CTA) | cta offsets | block tables ----
   const size_t units_bytes = align16((size_t)n_units * sizeof(AttnUnit));
