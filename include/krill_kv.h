@@ -298,8 +298,11 @@ krill_status_t krill_decode_step(krill_pool_t pool, int32_t n_seqs, const krill_
  * returns once the work is enqueued on `stream`; `out` is complete when
  * `stream` has finished. Page-locked host buffers (cudaHostAlloc or
  * cudaHostRegister) let the copies overlap; pageable ones work, without the
- * overlap. On an error after the first chunk, the layers of the chunks
- * already enqueued have been appended. */
+ * overlap. A page-locked q is not copied: the attention kernels read it in
+ * place through its device mapping, so its transfer overlaps the cache reads
+ * (q must then stay unchanged until `stream` has finished). On an error after
+ * the first chunk, the layers of the chunks already enqueued have been
+ * appended. */
 krill_status_t krill_decode_step_host(krill_pool_t pool, int32_t n_seqs, const krill_seq_t* seqs,
                                       int32_t layer_begin, int32_t layer_count, const void* k_new,
                                       const void* v_new, int32_t kv_dtype, const void* q,

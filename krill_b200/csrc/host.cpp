@@ -1431,6 +1431,17 @@ krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const kril
   cudaStream_t s = (cudaStream_t)stream;
   cudaEvent_t ev_start = p->io.ev[0], ev_end = p->io.ev[1];
   uint8_t* d = p->io.d;
+  // A query in page-locked host memory is read in place by the attention
+  // kernels through its device mapping: its transfer then overlaps the cache
+  // reads instead of preceding them. Other host memory is copied first.
+  const uint8_t* q_mapped = nullptr;
+  {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, q) == cudaSuccess && attr.type == cudaMemoryTypeHost &&
+        attr.devicePointer != nullptr && ((uintptr_t)attr.devicePointer & 15) == 0)
+      q_mapped = static_cast<const uint8_t*>(attr.devicePointer);
+    cudaGetLastError();  // an unregistered pointer leaves an error to clear
+  }
   // Everything earlier on `stream` (the previous step's reads of the staging
   // and its output copies, which it joined) precedes this step's uploads.
   CUDA_TRY(cudaEventRecord(ev_start, s));
@@ -1441,8 +1452,9 @@ krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const kril
                              cudaMemcpyHostToDevice, p->io.h2d));
     CUDA_TRY(cudaMemcpyAsync(d + v_off + c0 * kv_l, (const uint8_t*)v_new + c0 * kv_l, lc * kv_l,
                              cudaMemcpyHostToDevice, p->io.h2d));
-    CUDA_TRY(cudaMemcpyAsync(d + q_off + c0 * q_l, (const uint8_t*)q + c0 * q_l, lc * q_l,
-                             cudaMemcpyHostToDevice, p->io.h2d));
+    if (!q_mapped)
+      CUDA_TRY(cudaMemcpyAsync(d + q_off + c0 * q_l, (const uint8_t*)q + c0 * q_l, lc * q_l,
+                               cudaMemcpyHostToDevice, p->io.h2d));
     CUDA_TRY(cudaEventRecord(p->io.ev[2 + c], p->io.h2d));
     return KRILL_OK;
   };
@@ -1457,8 +1469,9 @@ krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const kril
     rc = do_append(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc, 1, d + k_off + c0 * kv_l,
                    d + v_off + c0 * kv_l, kv_dtype, s);
     if (rc == KRILL_OK)
-      rc = do_attention(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc, d + q_off + c0 * q_l, q_dtype,
-                        d + o_off + c0 * o_l, out_dtype, scale, s);
+      rc = do_attention(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc,
+                        (q_mapped ? q_mapped : d + q_off) + c0 * q_l, q_dtype, d + o_off + c0 * o_l,
+                        out_dtype, scale, s);
     if (rc != KRILL_OK) break;
     if (c + 1 < n_ch) {
       rc = copy_in(c + 1);

@@ -92,3 +92,51 @@ def test_host_step_layer_subrange_and_errors():
     with pytest.raises(kb.KrillError):
         kb.decode_step_host(pb, sb, 3, host_tensor(k1, dtype, True), host_tensor(v1, dtype, True),
                             host_tensor(qb, dtype, True), out_host, 0.125)
+
+
+def test_host_step_shared_prefix_cascade():
+    """Forks of one prefix-cache entry attend the shared blocks through the
+    tcgen05 cascade kernel, which then reads the query from mapped host
+    memory too; the host step must match the device step bit for bit."""
+    layers, hkv, hq, D, dtype = 2, 8, 32, 128, BF16
+    rng = np.random.default_rng(11)
+    P, suffixes = 1024, [5, 70, 300, 1]
+    kp = to_bits(kv_values(rng, (layers, hkv, P, D)), dtype)
+    vp = to_bits(kv_values(rng, (layers, hkv, P, D)), dtype)
+    ks = [to_bits(kv_values(rng, (layers, hkv, S, D)), dtype) for S in suffixes]
+    vs = [to_bits(kv_values(rng, (layers, hkv, S, D)), dtype) for S in suffixes]
+    pools, seqs = [], []
+    for _ in range(2):
+        pool = kb.KVPool(layers, hkv, hq, D, num_blocks=64, group_size=64)
+        pc = kb.PrefixCache(pool)
+        base = pool.create_sequence()
+        prefill(pool, base, kp, vp, dtype)
+        toks = list(range(P))
+        pc.store_quantized(toks, "m", base)
+        base.release()
+        hit = pc.lookup_quantized(toks, "m")
+        ss = []
+        for k, v in zip(ks, vs):
+            f = hit.fork(P)
+            prefill(pool, f, k, v, dtype)
+            ss.append(f)
+        hit.release()
+        pools.append((pool, pc))
+        seqs.append(ss)
+    n = len(suffixes)
+    (pa, _), (pb, _) = pools
+    for step in range(2):
+        k1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        v1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        qb = to_bits(kv_values(rng, (layers, n, hq, D)), dtype)
+        out_dev = torch.empty((layers, n, hq, D), dtype=torch.bfloat16, device="cuda")
+        kb.decode_step(pa, seqs[0], 0, dev_bits(k1, dtype), dev_bits(v1, dtype), dev_bits(qb, dtype),
+                       out_dev, 0.088)
+        assert pa.last_cascade()[0] >= 1, "the forks should form a cascade group"
+        out_host = torch.empty((layers, n, hq, D), dtype=torch.bfloat16, pin_memory=True)
+        kb.decode_step_host(pb, seqs[1], 0, host_tensor(k1, dtype, True), host_tensor(v1, dtype, True),
+                            host_tensor(qb, dtype, True), out_host, 0.088)
+        torch.cuda.synchronize()
+        assert pb.last_cascade()[0] >= 1
+        assert torch.equal(out_dev.cpu().view(torch.int16), out_host.view(torch.int16)), f"step {step}"
+    assert pa.device_error() == 0 and pb.device_error() == 0
