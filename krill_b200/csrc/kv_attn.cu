@@ -80,30 +80,46 @@ struct TCState {
 };
 
 
-// Load this lane's Qᵀ fragments for one unit: q[head = r][16*(tig+4hh) + 0..15].
-template <int D, int FMT = kFmtInt8>
-__device__ __forceinline__ void load_q(TCState<D>& st, const void* q, int q_dtype, int64_t row_elem,
-                                       int g, int lane) {
+// This lane's Qᵀ fragments for one (unit, head): q[head = r][16*(tig+4hh) +
+// 0..15], fetched as raw words ahead of use (fetch_q) so that the next item's
+// query arrives while the current one computes, then converted (set_q).
+template <int D>
+struct QRaw {
+  uint4 w[D / 64][2];
+};
+
+template <int D>
+__device__ __forceinline__ void fetch_q(QRaw<D>& qr, const void* q, int64_t row_elem, int g, int lane) {
   const int r = lane >> 2, tig = lane & 3;
 #pragma unroll
   for (int hh = 0; hh < D / 64; ++hh) {
     if (r < g) {
       const int64_t e = row_elem + (int64_t)r * D + 16 * (tig + 4 * hh);
       const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q) + e);
-      uint4 a = __ldg(p), b = __ldg(p + 1);
-      uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (FMT == kFmtInt8 && q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
-          __nv_bfloat162 bv = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
-          float2 f = __bfloat1622float2(bv);
-          w[i] = f2h2(f.x, f.y);
-        }
-        st.qf[hh][i] = w[i];
-      }
+      qr.w[hh][0] = __ldg(p);
+      qr.w[hh][1] = __ldg(p + 1);
     } else {
+      qr.w[hh][0] = make_uint4(0u, 0u, 0u, 0u);
+      qr.w[hh][1] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+// st.qf from fetched words (bf16 queries become f16 for the int8 path).
+template <int D, int FMT = kFmtInt8>
+__device__ __forceinline__ void set_q(TCState<D>& st, const QRaw<D>& qr, int q_dtype) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) st.qf[hh][i] = 0u;
+  for (int hh = 0; hh < D / 64; ++hh) {
+    const uint4 a = qr.w[hh][0], b = qr.w[hh][1];
+    uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (FMT == kFmtInt8 && q_dtype == 1) {  // bf16 -> f16 (exact in the f16 normal range)
+        __nv_bfloat162 bv = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
+        float2 f = __bfloat1622float2(bv);
+        w[i] = f2h2(f.x, f.y);
+      }
+      st.qf[hh][i] = w[i];
     }
   }
 }
@@ -643,10 +659,12 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 // warp (hr, r) takes the sub-blocks k = r, r + R, ...
 // Threads: NCW consumer warps (two warpgroups) + one producer warpgroup, of
 // which one warp issues the copies. At start the producer warpgroup gives its
-// registers back (setmaxnreg.dec to 40) and the consumers take them
-// (setmaxnreg.inc to 232): 128*40 + 256*232 = 384*168, the launch budget.
-constexpr int kProducerRegs = 40;
-constexpr int kConsumerRegs = 232;
+// registers back (setmaxnreg.dec to 56) and the consumers take them
+// (setmaxnreg.inc to 224): 128*56 + 256*224 = 384*168, the launch budget.
+// (With 40 the producer's metadata prefetch spilled; 224 still holds every
+// consumer without spills.)
+constexpr int kProducerRegs = 56;
+constexpr int kConsumerRegs = 224;
 
 // Consumer warps of attn_tc_kernel. FAST selects the one-fma dequantization,
 // exact only while every scale in the pool is below 64 in magnitude; the
@@ -665,9 +683,18 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   uint32_t J = 0;
   AttnItem item_next{};
   AttnUnit un_next{};
+  // The query of the next (item, round) is fetched while this one computes:
+  // the next item's unit after this warp's first sub-block (the item record
+  // has arrived by then), its q words after the second, so neither load
+  // stalls the warp. qr always holds the q of the (item, round) about to run.
+  QRaw<D> qr;
+  auto q_row = [&](const AttnUnit& u, int hh) {
+    return ((int64_t)u.qo_row * p.Hq + (int64_t)hh * p.g) * D;
+  };
   if (it0 < it1) {
     item_next = p.items[it0];
     un_next = p.units[item_next.unit];
+    fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, lane);
   }
   for (int it = it0; it < it1; ++it) {
     const AttnItem item = item_next;
@@ -677,9 +704,23 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
     for (int rd = 0; rd < rounds; ++rd) {
       const int h = item.h0 + rd * HPR + hr;
       reset_state(st);
-      if (rr < n_sb)
-        load_q<D, FMT>(st, p.q, p.q_dtype, ((int64_t)un.qo_row * p.Hq + (int64_t)h * p.g) * D, p.g,
-                       lane);
+      set_q<D, FMT>(st, qr, p.q_dtype);
+      // prefetch state: 0 nothing yet, 1 next unit requested, 2 next q fetched
+      int pf = 0;
+      auto prefetch_step = [&]() {
+        if (rd + 1 < rounds) {  // next round: same unit, the next head group
+          fetch_q<D>(qr, p.q, q_row(un, h + HPR), p.g, lane);
+          pf = 2;
+        } else if (it + 1 >= it1) {
+          pf = 2;
+        } else if (pf == 0) {
+          un_next = p.units[item_next.unit];
+          pf = 1;
+        } else {
+          fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, lane);
+          pf = 2;
+        }
+      };
       for (int k = rr; k < n_sb; k += R) {
         const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
@@ -696,9 +737,10 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
           tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
+        if (pf < 2) prefetch_step();
       }
+      while (pf < 2) prefetch_step();
       J += (uint32_t)n_sb * HPR;
-      if (rd == rounds - 1 && it + 1 < it1) un_next = p.units[item_next.unit];
 
       float l0 = st.l[0], l1 = st.l[1];
 #pragma unroll
@@ -788,14 +830,46 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
     // The lanes fetch an item's block ids together (one coalesced load per 32
     // blocks); lane 0 issues the bulk copies with no dependent global load in
     // the issue loop.
+    // The next item's record, unit and first 32 block ids are fetched while
+    // this item's copies are issued (one step per issued sub-block), so that
+    // the chain item -> unit -> block table never idles the copy engine
+    // between items.
     const int64_t blk_stride = (int64_t)p.L * Hkv * p.page_bytes;
+    constexpr int SPB = SubGeom<D, NG, FMT>::SPB;
+    auto first_blocks = [&](const AttnItem& itm, const AttnUnit& u) {
+      const int b0 = itm.sb_begin / SPB;
+      const int nblk = (itm.sb_end - 1) / SPB - b0 + 1;
+      int bi = b0 + lane;
+      if (p.ring > 0) bi %= p.ring;
+      return lane < nblk ? p.bt[(int64_t)u.si * p.bt_stride + bi] : 0;
+    };
+    AttnItem item_n{};
+    AttnUnit un_n{};
+    int blk_n = 0;
+    if (it0 < it1) {
+      item_n = p.items[it0];
+      un_n = p.units[item_n.unit];
+      blk_n = first_blocks(item_n, un_n);
+    }
     uint32_t J = 0;
     for (int it = it0; it < it1; ++it) {
-      const AttnItem item = p.items[it];
-      const AttnUnit un = p.units[item.unit];
+      const AttnItem item = item_n;
+      const AttnUnit un = un_n;
+      const int blk_first = blk_n;
+      const bool more = it + 1 < it1;
+      if (more) item_n = p.items[it + 1];
+      int pf = more ? 0 : 2;  // 0: next record requested, 1: its unit, 2: its block ids
+      auto prefetch_step = [&]() {
+        if (pf == 0) {
+          un_n = p.units[item_n.unit];
+          pf = 1;
+        } else if (pf == 1) {
+          blk_n = first_blocks(item_n, un_n);
+          pf = 2;
+        }
+      };
       const int32_t* bt = p.bt + (int64_t)un.si * p.bt_stride;
       const int n_sb = item.sb_end - item.sb_begin;
-      constexpr int SPB = SubGeom<D, NG, FMT>::SPB;
       const int b0 = item.sb_begin / SPB;
       const int nblk = (item.sb_end - 1) / SPB - b0 + 1;
       for (int rd = 0; rd < rounds; ++rd) {
@@ -804,7 +878,7 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
         for (int c0 = 0; c0 < nblk; c0 += 32) {
           int bi = b0 + c0 + lane;
           if (p.ring > 0) bi %= p.ring;
-          const int blk = (c0 + lane < nblk) ? bt[bi] : 0;
+          const int blk = c0 == 0 ? blk_first : (c0 + lane < nblk) ? bt[bi] : 0;
           const int jlo = max(item.sb_begin, (b0 + c0) * SPB);
           const int jhi = min(item.sb_end, (b0 + c0 + 32) * SPB);
           for (int j = jlo; j < jhi; ++j) {
@@ -824,10 +898,12 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
                          SB, full);
               }
             }
+            if (pf < 2) prefetch_step();
           }
         }
         J += (uint32_t)n_sb * HPR;
       }
+      while (pf < 2) prefetch_step();
     }
     return;
   }
