@@ -550,6 +550,10 @@ def main():
     torch.cuda.set_device(local_rank)
     if world > 1:
         from datetime import timedelta
+        # stdout carries exactly one JSON line: keep NCCL's version banner
+        # (NCCL_DEBUG=VERSION) out of it
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
         # first collective up front, so NCCL's lazy setup never overlaps our kernels
@@ -574,7 +578,7 @@ def main():
     mine = [lengths_all[i] for i in parts[rank]]
     layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
-    total_steps = args.warmup + args.steps * 2 + 2
+    total_steps = args.warmup + args.steps * 3 + 2
     blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4
     raw = args.kv == "bf16"
     if raw and cfg["dtype"] != "bf16":
@@ -642,15 +646,16 @@ def main():
     flush = None
     if step_bytes([L + 1 for L in len_before], cfg, raw)[1] < L2_FLUSH_BYTES:
         flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-    # per-kernel CUDA events recorded by the library around each launch, on
-    # the launching stream
-    pool.set_profiling(True)
-    pool.kernel_times()
-    pool.kernel_count()
     n_pairs = 1 if flush is None else args.steps
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_pairs)]
-    with ClockSampler(local_rank) as clocks:
+
+    def timed_steps(profile):
+        """K steps; with profile the library brackets each of its launches
+        with CUDA events on the launching stream (per-kernel device times)."""
+        pool.set_profiling(profile)
+        pool.kernel_times()
+        pool.kernel_count()
         torch.cuda.synchronize()
         for i in range(args.steps):
             if flush is not None:
@@ -661,24 +666,29 @@ def main():
             if flush is not None or i == args.steps - 1:
                 evs[min(i, n_pairs - 1)][1].record(stream)
         torch.cuda.synchronize()
+        res = (sum(a.elapsed_time(b) for a, b in evs), pool.kernel_count(), pool.kernel_times())
+        pool.set_profiling(False)
+        return res
+
+    # `value`: the step as a user runs it (no per-launch events); then the
+    # same number of steps again with the per-kernel events for the roofline
+    with ClockSampler(local_rank) as clocks:
+        total_ms, launches, _ = timed_steps(False)
     barrier()
-    launches = pool.kernel_count()
-    total_ms = sum(a.elapsed_time(b) for a, b in evs)
-    attn_total, attn_n, app_total, app_n = pool.kernel_times()
-    pool.set_profiling(False)
+    _, _, (attn_total, attn_n, app_total, app_n) = timed_steps(True)
+    barrier()
     attn_ms = [attn_total / max(1, attn_n)]
     app_ms = [app_total / max(1, app_n)]
     ms_step = max_over_ranks(total_ms / args.steps)
     tokens_per_step = n_total
     value = tokens_per_step / (ms_step / 1e3)
 
-    # algorithmic bytes: lengths after each step's append
+    # algorithmic bytes: lengths after each step's append (the profiled pass
+    # runs after the value pass, args.steps tokens further on)
     attn_bytes, step_b = 0, 0
     for i in range(args.steps):
-        la = [L + i + 1 for L in len_before]
-        a, s_ = step_bytes(la, cfg, raw)
-        attn_bytes += a
-        step_b += s_
+        step_b += step_bytes([L + i + 1 for L in len_before], cfg, raw)[1]
+        attn_bytes += step_bytes([L + args.steps + i + 1 for L in len_before], cfg, raw)[0]
     attn_bytes /= args.steps
     step_b /= args.steps
     attn_mean_ms = float(np.mean(attn_ms))
