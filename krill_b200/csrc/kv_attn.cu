@@ -541,10 +541,14 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
     if (un.n_pre > 0) {
       // merge the shared-prefix records the cascade kernel completed earlier
       // in the stream (heads beyond the GQA group hold no data and are unused)
+      // (loops unrolled and the O loads unconditional, so that the loads of
+      // a record, and of two records, are in flight together)
       const float* rec = p.partials + ((int64_t)un.first_split * Hkv + h) * partial_floats(D);
       const int64_t stride = (int64_t)Hkv * partial_floats(D);
+      const int n_pre = un.n_pre;
       float M0 = st.m[0], M1 = st.m[1];
-      for (int i = 0; i < un.n_pre; ++i) {
+#pragma unroll 4
+      for (int i = 0; i < n_pre; ++i) {
         M0 = fmaxf(M0, rec[i * stride + (h0 & 7)]);
         M1 = fmaxf(M1, rec[i * stride + (h1 & 7)]);
       }
@@ -559,26 +563,33 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
         st.o[mt][2] *= a0;
         st.o[mt][3] *= a1;
       }
-      for (int i = 0; i < un.n_pre; ++i) {
+      // Records of heads h0, h1 >= g are never written: their words are read
+      // (the buffer spans all 8 head slots) but always discarded by the
+      // selects, as are the words of empty records (b == 0).
+#pragma unroll 2
+      for (int i = 0; i < n_pre; ++i) {
         const float* ri = rec + i * stride;
         const float m0 = ri[h0 & 7], m1 = ri[h1 & 7];
+        const float lv0 = ri[8 + (h0 & 7)], lv1 = ri[8 + (h1 & 7)];
+        float ov[D / 16][4];
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          ov[mt][0] = ri[16 + (h0 & 7) * D + 16 * mt + r];
+          ov[mt][2] = ri[16 + (h0 & 7) * D + 16 * mt + r + 8];
+          ov[mt][1] = ri[16 + (h1 & 7) * D + 16 * mt + r];
+          ov[mt][3] = ri[16 + (h1 & 7) * D + 16 * mt + r + 8];
+        }
         const float b0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
         const float b1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
-        if (b0 != 0.f && h0 < g) {
-          l0 += ri[8 + h0] * b0;
+        const bool t0 = b0 != 0.f && h0 < g, t1 = b1 != 0.f && h1 < g;
+        l0 = t0 ? l0 + lv0 * b0 : l0;
+        l1 = t1 ? l1 + lv1 * b1 : l1;
 #pragma unroll
-          for (int mt = 0; mt < D / 16; ++mt) {
-            st.o[mt][0] += ri[16 + h0 * D + 16 * mt + r] * b0;
-            st.o[mt][2] += ri[16 + h0 * D + 16 * mt + r + 8] * b0;
-          }
-        }
-        if (b1 != 0.f && h1 < g) {
-          l1 += ri[8 + h1] * b1;
-#pragma unroll
-          for (int mt = 0; mt < D / 16; ++mt) {
-            st.o[mt][1] += ri[16 + h1 * D + 16 * mt + r] * b1;
-            st.o[mt][3] += ri[16 + h1 * D + 16 * mt + r + 8] * b1;
-          }
+        for (int mt = 0; mt < D / 16; ++mt) {
+          st.o[mt][0] = t0 ? st.o[mt][0] + ov[mt][0] * b0 : st.o[mt][0];
+          st.o[mt][2] = t0 ? st.o[mt][2] + ov[mt][2] * b0 : st.o[mt][2];
+          st.o[mt][1] = t1 ? st.o[mt][1] + ov[mt][1] * b1 : st.o[mt][1];
+          st.o[mt][3] = t1 ? st.o[mt][3] + ov[mt][3] * b1 : st.o[mt][3];
         }
       }
     }

@@ -4,10 +4,10 @@
 // Same work items and results as kv_shared.cu (forks of one prefix-cache
 // entry attend the common blocks once per (layer, kv head); see there for the
 // reference mapping), for head_dim 64 and 128. An item covers up to 256 query
-// rows as two 128-row halves that share every K/V tile. One CTA per SM, 16
+// rows as two 128-row halves that share every K/V tile. One CTA per SM, 20
 // warps:
 //   - warp 9 streams raw sub-blocks HBM -> shared memory (cp.async.bulk);
-//   - warps 10-15 dequantize each raw sub-block once (the reference's two
+//   - warps 10-19 dequantize each raw sub-block once (the reference's two
 //     fp16 roundings) into f16 K [64 tok][D] and V [D][64 tok] tiles laid out
 //     as the tensor core's canonical K-major 128-byte-swizzled operands;
 //   - warp 8 owns the tensor memory (512 columns) and one of its lanes issues
@@ -18,7 +18,8 @@
 //     overlaps S of tile j+1; each group of MMAs is committed to an mbarrier;
 //   - warps 4h .. 4h+3 (thread t = query row t of half h = tensor-memory
 //     lane t) read S with tcgen05.ld, run the online softmax in the exp2
-//     domain and write P_h as f16 into a swizzled shared tile. The running max
+//     domain (one ex2.approx.ftz and one fma per score) and write P_h as f16
+//     into a swizzled shared tile. The running max
 //     is only raised when a row's max grows by more than 8 (log2 units); the
 //     rare O rescale is a tcgen05.ld / st round trip after the previous P·V
 //     has completed. At the end of an item they read O and write the fp32
@@ -34,8 +35,14 @@ namespace {
 
 constexpr int kUmNF = 3;         // f16 K/V tile stages
 constexpr int kUmNR = 2;         // raw sub-block stages
-constexpr int kUmDeqWarps = 6;   // warps 10-15
-constexpr int kUmThreads = 512;  // 16 warps
+constexpr int kUmDeqWarps = 10;  // warps 10-19
+constexpr int kUmThreads = 640;  // 20 warps
+// Register split (setmaxnreg): the two softmax warpgroups hold a 64-column S
+// row per thread and take 120; the MMA, copy and dequantizer warpgroups give
+// theirs back to 80. 256*120 + 384*80 = 61,440 = 640*96, the launch budget.
+// (Of the splits that fit, this one spills least.)
+constexpr int kUmSoftmaxRegs = 120;
+constexpr int kUmOtherRegs = 80;
 // tensor memory: half h owns columns [256h, 256h + 256): O_h at +0 (D columns),
 // S_h double buffer at +128 and +192
 constexpr uint32_t kUmCols = 512;
@@ -262,6 +269,14 @@ __device__ __forceinline__ void um_dequant(const uint8_t* __restrict__ raw, uint
   }
 }
 
+// 2^x by the special-function unit (ex2.approx.ftz.f32: one instruction;
+// results below 2^-126 flush to zero, immaterial next to a row sum >= 1).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float max64(const float (&a)[32], const float (&b)[32]) {
   float m[8];
 #pragma unroll
@@ -323,6 +338,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
   const int it0 = p.sh_cta_off[blockIdx.x], it1 = p.sh_cta_off[blockIdx.x + 1];
   const int Hkv = p.Hkv;
 
+  // Each warpgroup adjusts its registers at one point of its own branch
+  // (setmaxnreg is .sync.aligned over the warpgroup): warpgroups 2-4 (MMA,
+  // copies, dequantizers) give registers back, 0-1 (softmax) take them.
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kUmOtherRegs));
   if (warp == 9) {
     // ---------------- copy issuer ----------------
     if (lane == 0) {
@@ -368,8 +388,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         }
       }
     }
-  } else if (warp == 8) {
-    // ---------------- MMA issuer ----------------
+  } else {
+    // ---------------- MMA issuer (warp 8) ----------------
     if (lane == 0) {
       constexpr uint32_t idS = umma_idesc(128, 64), idO = umma_idesc(128, D);
       uint32_t cnt0 = 0, cnt1 = 0;  // tiles processed by each half
@@ -458,7 +478,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       umma_commit(bar(SM::B_FIN));
       mbar_wait(bar(SM::B_FIN), 0, cta_abort, p.err);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kUmSoftmaxRegs));
     // ---------------- softmax / epilogue: half h, thread t = its query row t ----------------
     const int h = warp >> 2;
     const int t = tid & 127;
@@ -509,10 +531,18 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
         float s0[32], s1[32];
         tmem_ld32(lane_addr + kUmS0 + 64u * (c & 1), s0);
         tmem_ld32(lane_addr + kUmS0 + 64u * (c & 1) + 32u, s1);
+        // The scale enters the exponent through one fma per score; the max
+        // is taken unscaled (scaling by sc > 0 keeps the order and rounds
+        // monotonically, so max(s) * sc == max(s * sc)). A non-positive
+        // scale is applied up front instead.
+        float sc = p.scale_log2;
+        if (!(sc > 0.f)) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s0[i] *= p.scale_log2;
-          s1[i] *= p.scale_log2;
+          for (int i = 0; i < 32; ++i) {
+            s0[i] *= sc;
+            s1[i] *= sc;
+          }
+          sc = 1.f;
         }
         if (item.causal >= 0) {  // tokens after this row's own position
           const int pos0 = (item.sb_begin + j) * 64;
@@ -525,7 +555,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
             }
           }
         }
-        const float mx = max64(s0, s1);
+        const float mx = max64(s0, s1) * sc;
         // O_h and P_h were last used by the P·V of tile c-1: wait for it only
         // where they are touched (rare O rescale, then the P write)
         bool pv_done = j == 0;
@@ -555,11 +585,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
 #pragma unroll
         for (int k = 0; k < 8; ++k) ps[k] = 0.f;
         // a row that has seen no visible token yet (causal) keeps m = -inf
-        const float base = m == -INFINITY ? 0.f : m;
+        const float nb = m == -INFINITY ? 0.f : -m;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          s0[i] = exp2f(s0[i] - base);
-          s1[i] = exp2f(s1[i] - base);
+          s0[i] = ex2_ftz(fmaf(s0[i], sc, nb));
+          s1[i] = ex2_ftz(fmaf(s1[i], sc, nb));
           ps[i & 7] += s0[i] + s1[i];
         }
         l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
@@ -637,6 +667,13 @@ cudaError_t launch_um(const AttnParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
+    // setmaxnreg.inc waits until the released registers cover it: refuse to
+    // launch a build whose register count would not balance
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, attn_shared_umma_kernel<D, NG>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs * kUmThreads < 256 * kUmSoftmaxRegs + (kUmThreads - 256) * kUmOtherRegs)
+      return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(attn_shared_umma_kernel<D, NG>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
