@@ -38,7 +38,8 @@ def half_ulp(ref: np.ndarray, out_dtype) -> np.ndarray:
 def run_case(D, G, hq, hkv, dtype, lengths, scale, out_dtype=torch.float32, window=0, split=256,
              outliers=False, layers=2, seed=0, impl=kb.ATTN_TENSOR_CORE, steps=2):
     rng = np.random.default_rng(seed)
-    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=64, group_size=G, window=window,
+    blocks = max(64, sum((L + steps) // 256 + 2 for L in lengths) + 8)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, window=window,
                      split_tokens=split, attn_impl=impl)
     seqs, kb_all, vb_all = [], [], []
     for L in lengths:
@@ -101,6 +102,21 @@ def test_attention_ragged(D, G, hq, hkv, dtype, scale):
 def test_attention_long_split():
     # several split-K items per unit, combined by the last CTA
     run_case(128, 64, 32, 8, BF16, [3000, 1100], 1 / math.sqrt(128), split=512, layers=1)
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,lengths,layers", [
+    (128, 64, 32, 8, BF16, [20000], 1),   # one long sequence: pieces merged by the last arriver
+    (64, 64, 32, 8, F16, [2048], 16),     # configs[0] shape: one kv head per item, whole sequence
+    (256, 64, 8, 4, F16, [9000, 70], 2),  # D = 256, GQA 2, ragged
+    (128, 128, 16, 16, F16, [5000], 1),   # MHA: several head rounds per item
+    (64, 64, 8, 1, F16, [12000], 1),      # MQA: 8 warps share the one head
+])
+def test_attention_latency_bound_adaptive(D, G, hq, hkv, dtype, lengths, layers):
+    """Adaptive splitting on small batches: the planner's latency-bound regime
+    (head-split items, pieces merged in the decode kernel by the piece that
+    arrives last, one item per CTA)."""
+    scale = 1 / math.sqrt(D)
+    run_case(D, G, hq, hkv, dtype, lengths, scale, split=0, layers=layers, steps=2)
 
 
 def test_attention_outliers_gqa8():
