@@ -42,8 +42,9 @@ CONFIGS = {
     # name: layers, hq, hkv, D, G, dtype, seqs/GPU, length sampler, scale
     "llama31_8b_batch32": dict(layers=32, hq=32, hkv=8, D=128, G=64, dtype="bf16", seqs=32,
                                lens=("uniform", 512, 8192, 1), scale=1 / math.sqrt(128)),
+    # configs[0] is quoted on 128 decode steps: its default step count
     "llama32_1b_single": dict(layers=16, hq=32, hkv=8, D=64, G=64, dtype="f16", seqs=1,
-                              lens=("fixed", 2048, 2048, 0), scale=1 / 8.0),
+                              lens=("fixed", 2048, 2048, 0), scale=1 / 8.0, steps=128),
     "qwen3_30b_longctx": dict(layers=48, hq=32, hkv=4, D=128, G=64, dtype="bf16", seqs=16,
                               lens=("fixed", 32768, 32768, 3), scale=1 / math.sqrt(128)),
     # 64 requests = one shared 4096-token prefix + a unique 256-token suffix
@@ -516,7 +517,8 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 20; the workload's own count where it has one)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="krill", choices=["krill", "reference"])
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
@@ -532,6 +534,8 @@ def main():
     ap.add_argument("--diag", action="store_true",
                     help="per-rank, per-step kernel times and device error flags on stderr")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = CONFIGS[args.config].get("steps", 20)
     args.warmup = max(3, args.warmup)
     cfg = dict(CONFIGS[args.config])
     if args.seqs:
