@@ -266,8 +266,10 @@ krill_status_t krill_prefill_attention(krill_pool_t pool, int32_t n_seqs, const 
  *     with KRILL_ERR_INVALID and a message giving the bytes it would need.
  *   - The first call on a device looks up the scratch's device address (with
  *     that device current); make that first call before any stream capture.
- *   - All calls share the one scratch and every call writes all of the scratch
- *     it reads (nothing has to start zeroed), so calls serialise on the host,
+ *   - All calls share the one scratch. Every call writes the metadata and
+ *     partial results it reads; the arrival counters that merge split
+ *     sequences carry a per-call tag, so values left by an earlier call count
+ *     as zero (nothing has to be cleared between calls). Calls serialise on the host,
  *     and calls whose GPU work overlaps (different streams, no ordering
  *     between them) race on the scratch: order them on one stream or
  *     synchronise between them. */

@@ -96,6 +96,16 @@ constexpr int kStageSlots = 16;
 // pool, so no call allocates staging until a packet outgrows its slice.
 constexpr size_t kStageSliceBytes = 1 << 20;
 
+// An append whose destinations were planned but whose upload and launch are
+// left to the caller (see do_append).
+struct DeferredAppend {
+  std::vector<AppendDst> dst;
+  int32_t lb = 0, lc = 0, n_seqs = 0, n_new = 0, dtype = 0;
+  const void* k = nullptr;
+  const void* v = nullptr;
+  bool pending = false;  // planned, not launched yet
+};
+
 // Decode-attention planner buffers, reused across calls.
 __global__ void or_flag_kernel(int* dst, const int* src) { *dst |= *src; }
 
@@ -160,6 +170,7 @@ struct krill_pool_s {
   std::vector<Timed> timed;
   std::vector<cudaEvent_t> spare_events;
   Plan plan;
+  DeferredAppend deferred;  // krill_decode_step's append, folded into the attention packet
   // krill_decode_step_host: device staging for the step's inputs and output,
   // the two copy streams and the per-chunk events that order them.
   struct HostIo {
@@ -361,9 +372,16 @@ krill_status_t check_layers(krill_pool_t p, int32_t lb, int32_t lc) {
 // ---------------------------------------------------------------- append
 // On a host-only (dry-run) pool the block accounting, copy-on-write decisions
 // and length updates run, and the device work is skipped.
+// With `deferred` the destinations go to deferred->dst (host) and the upload
+// and launch are left to the caller (krill_decode_step folds them into the
+// attention's metadata packet); the bookkeeping is the same.
+krill_status_t launch_deferred_append(krill_pool_t p, DeferredAppend& da, const AppendDst* d_dst,
+                                      cudaStream_t stream);
+
 krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                          int32_t lc, int32_t n_new, const void* k, const void* v, int32_t dtype,
-                         cudaStream_t stream, RopeTable rope = RopeTable{nullptr, nullptr, 0}) {
+                         cudaStream_t stream, RopeTable rope = RopeTable{nullptr, nullptr, 0},
+                         DeferredAppend* deferred = nullptr) {
   TRY(check_layers(p, lb, lc));
   TRY(check_dtype16(dtype, "k/v"));
   if (rope.cos) {
@@ -395,7 +413,10 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
   StageSlot* slot = nullptr;
   std::vector<AppendDst> dry;
   AppendDst* dst;
-  if (p->host_only) {
+  if (deferred && !p->host_only) {
+    deferred->dst.resize(n_dst);
+    dst = deferred->dst.data();
+  } else if (p->host_only) {
     dry.resize(n_dst);
     dst = dry.data();
   } else {
@@ -422,7 +443,16 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
       }
     }
   }
-  if (!p->host_only) {
+  if (deferred && !p->host_only) {
+    deferred->lb = lb;
+    deferred->lc = lc;
+    deferred->n_seqs = n_seqs;
+    deferred->n_new = n_new;
+    deferred->dtype = dtype;
+    deferred->k = k;
+    deferred->v = v;
+    deferred->pending = true;
+  } else if (!p->host_only) {
     TRY(stage_upload(slot, n_dst * sizeof(AppendDst), stream));
     CUDA_TRY(timed_launch(p, 1, stream, [&] {
       return launch_append(p->geom, p->d_pool, reinterpret_cast<const AppendDst*>(slot->d), lb, lc,
@@ -443,6 +473,32 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
     }
   }
   return KRILL_OK;
+}
+
+// The append kernel of a deferred append, its destinations at d_dst (device).
+krill_status_t launch_deferred_append(krill_pool_t p, DeferredAppend& da, const AppendDst* d_dst,
+                                      cudaStream_t stream) {
+  da.pending = false;
+  CUDA_TRY(timed_launch(p, 1, stream, [&] {
+    return launch_append(p->geom, p->d_pool, d_dst, da.lb, da.lc, da.n_seqs, da.n_new, da.k, da.v,
+                         da.dtype, p->d_err + 1, RopeTable{nullptr, nullptr, 0}, stream);
+  }));
+  p->kernels += 1;
+  return KRILL_OK;
+}
+
+// A deferred append that its attention call did not launch (it failed before
+// its launches): uploaded and launched on its own, so that the advanced
+// lengths always have their K/V.
+krill_status_t flush_deferred_append(krill_pool_t p, DeferredAppend& da, cudaStream_t stream) {
+  if (!da.pending) return KRILL_OK;
+  StageSlot* slot = nullptr;
+  const size_t bytes = da.dst.size() * sizeof(AppendDst);
+  TRY(stage_acquire(p, bytes, &slot));
+  std::memcpy(slot->h, da.dst.data(), bytes);
+  TRY(stage_upload(slot, bytes, stream));
+  TRY(launch_deferred_append(p, da, reinterpret_cast<const AppendDst*>(slot->d), stream));
+  return stage_release(slot, stream);
 }
 
 // ---------------------------------------------------------------- attention
@@ -469,7 +525,7 @@ krill_status_t ensure_scratch(krill_pool_t p, int64_t records, int64_t /*unused*
 krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs, int32_t lb,
                             int32_t lc, const void* q, int32_t q_dtype, void* out,
                             int32_t out_dtype, float scale, cudaStream_t stream,
-                            int32_t n_query = 1) {
+                            int32_t n_query = 1, DeferredAppend* pre = nullptr) {
   TRY(check_layers(p, lb, lc));
   if (n_query < 1) return fail(KRILL_ERR_INVALID, "n_query must be positive");
   if (n_query > 1 && p->windowed())
@@ -839,7 +895,10 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   const size_t shc_bytes = align16(pl.sh_cta.size() * sizeof(int32_t));
   const size_t shm_bytes = align16(pl.sh_members.size() * sizeof(int32_t));
   const size_t sh_off = units_bytes + items_bytes + off_bytes + bt_bytes + su_bytes;
-  const size_t total = sh_off + shi_bytes + shc_bytes + shm_bytes;
+  // a deferred append's destinations ride in the same packet (one upload)
+  const size_t pre_off = sh_off + shi_bytes + shc_bytes + shm_bytes;
+  const size_t pre_bytes = pre && pre->pending ? align16(pre->dst.size() * sizeof(AppendDst)) : 0;
+  const size_t total = pre_off + pre_bytes;
   StageSlot* slot = nullptr;
   uint8_t* h;
   if (p->host_only) {
@@ -872,6 +931,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     std::memcpy(h + sh_off + shi_bytes + shc_bytes, pl.sh_members.data(),
                 pl.sh_members.size() * sizeof(int32_t));
   }
+  if (pre_bytes) std::memcpy(h + pre_off, pre->dst.data(), pre->dst.size() * sizeof(AppendDst));
   pl.last_groups = n_groups;
   pl.last_pslots = n_pslots;
   pl.last_sh_grid = sh_grid;
@@ -916,6 +976,14 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.sh_members = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes + shc_bytes);
     ap.sh_grid = sh_grid;
     ap.n_pslots = n_pslots;
+  }
+  if (pre_bytes) {
+    const krill_status_t st =
+        launch_deferred_append(p, *pre, reinterpret_cast<const AppendDst*>(slot->d + pre_off), stream);
+    if (st != KRILL_OK) {
+      stage_release(slot, stream);
+      return st;
+    }
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
   p->kernels += (grid > 0 ? 1 : 0) + (attn_needs_combine(ap, grid, p->cfg.attn_impl) ? 1 : 0) +
@@ -1374,10 +1442,21 @@ krill_status_t krill_decode_step(krill_pool_t p, int32_t n_seqs, const krill_seq
   if (!p) return fail(KRILL_ERR_INVALID, "null pool");
   std::lock_guard<std::recursive_mutex> lk(p->mu);
   DeviceGuard dg(p->device);
+  // The append's destinations travel in the attention's metadata packet: one
+  // upload per step, then the append and attention launches.
+  DeferredAppend& da = p->deferred;
+  da.pending = false;
   TRY(do_append(p, n_seqs, seqs, layer_begin, layer_count, 1, k_new, v_new, kv_dtype,
-                (cudaStream_t)stream));
-  return do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out, out_dtype, scale,
-                      (cudaStream_t)stream);
+                (cudaStream_t)stream, RopeTable{nullptr, nullptr, 0}, &da));
+  const krill_status_t st = do_attention(p, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out,
+                                         out_dtype, scale, (cudaStream_t)stream, 1, &da);
+  if (da.pending) {
+    // keep the error of the attention call, whatever the fallback returns
+    const std::string msg = krill_last_error_string();
+    flush_deferred_append(p, da, (cudaStream_t)stream);
+    if (st != KRILL_OK) set_error(st, msg.c_str());
+  }
+  return st;
 }
 
 krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs,
