@@ -984,6 +984,9 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       stage_release(slot, stream);
       return st;
     }
+    // the decode kernel follows the append directly (no cascade kernel
+    // between them): let it start while the append runs
+    ap.pdl = (sh_grid == 0 && grid > 0 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE) ? 1 : 0;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
   p->kernels += (grid > 0 ? 1 : 0) + (attn_needs_combine(ap, grid, p->cfg.attn_impl) ? 1 : 0) +

@@ -123,6 +123,9 @@ struct AttnParams {
   const int32_t* sh_members;  // unit ids
   int sh_grid;
   int n_pslots;               // prefix record slots per cascaded unit
+  // host side only: launch the decode kernel as the programmatic dependent of
+  // the append kernel launched just before it on the stream
+  int pdl;
 };
 
 // Rotary table for the fused RoPE append: cos / sin [rows][D/2] f32 (device),

@@ -829,6 +829,11 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  // Launched as the programmatic dependent of a decode step's append (see
+  // launch_tc), this grid may start while the append runs: wait for it to
+  // complete before reading the pool or the large-scale flag it writes.
+  // Without that launch attribute this returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int it0 = p.cta_off[blockIdx.x], it1 = p.cta_off[blockIdx.x + 1];
   const int Hkv = p.Hkv;
@@ -953,6 +958,20 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
+  }
+  if (p.pdl) {
+    // programmatic dependent of the append launched just before it
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((NCW + 4) * 32);
+    cfg.dynamicSmemBytes = SM::TOTAL;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>, p);
   }
   attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
   return cudaGetLastError();

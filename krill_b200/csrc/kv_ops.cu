@@ -94,6 +94,10 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
                                                               const void* __restrict__ v, int dtype,
                                                               int* __restrict__ large_scale,
                                                               RopeTable rope) {
+  // A decode step's attention kernel may be launched as this kernel's
+  // programmatic dependent: let it be scheduled now (it waits for this grid's
+  // completion before it reads the pool).
+  asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
@@ -159,6 +163,7 @@ __global__ void append_raw_kernel(uint8_t* __restrict__ pool, Geom geom,
                                   const AppendDst* __restrict__ dst, int layer_begin,
                                   int layer_count, int n_seqs, int n_new,
                                   const uint16_t* __restrict__ k, const uint16_t* __restrict__ v) {
+  asm volatile("griddepcontrol.launch_dependents;");  // as in append_quantize_kernel
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total = (int64_t)layer_count * n_seqs * geom.Hkv * n_new;
