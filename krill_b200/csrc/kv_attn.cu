@@ -21,7 +21,12 @@
 //     with Pᵀ obtained from the Sᵀ accumulators by movmatrix.trans, online
 //     softmax in the exp2 domain;
 //   - warps of one head combine in shared memory; a unit split over several
-//     items writes fp32 partial records that attn_combine_kernel merges.
+//     items writes fp32 partial records, merged by attn_combine_kernel in
+//     bandwidth-bound plans and, in latency-bound plans, by the item that
+//     arrives last (an epoch-tagged counter per unit and head).
+//   - in a decode step the kernel may be launched as the append kernel's
+//     programmatic dependent; every thread waits for that grid
+//     (griddepcontrol.wait) before reading the pool.
 // Every mbarrier wait is bounded; on timeout the kernel raises an error flag
 // and runs to completion instead of hanging.
 #include <atomic>
