@@ -56,6 +56,18 @@ CONFIGS = {
                                 lens=("fixed", 4352, 4352, 2), scale=1 / math.sqrt(128),
                                 prefix=4096, suffix=256),
 }
+# The rows after the decode path (each measured on one GPU, at the
+# Llama-3.1-8B KV shape): the prefix-cache disk tier, the fused RoPE append,
+# speculative verify and chunked prefill attention.
+NEXT_ROWS = {
+    "next_prefix_disk": dict(layers=32, hq=32, hkv=8, D=128, G=64, prefix=4096, steps=5),
+    "next_rope_append": dict(layers=32, hq=32, hkv=8, D=128, G=64, seqs=32, chunk=256),
+    "next_verify4": dict(layers=32, hq=32, hkv=8, D=128, G=64, seqs=32, n_query=4,
+                         lens=("uniform", 512, 8192, 1), scale=1 / math.sqrt(128)),
+    "next_prefill512": dict(layers=32, hq=32, hkv=8, D=128, G=64, seqs=8, prefix=4096, chunk=512,
+                            scale=1 / math.sqrt(128), steps=5),
+}
+CONFIGS.update(NEXT_ROWS)
 DEFAULT_CONFIG = "llama31_8b_batch32"
 L2_FLUSH_BYTES = 256 << 20  # 2 x the B200's 126 MB L2, rounded up
 
@@ -144,6 +156,16 @@ def measured_peak():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 burst TFLOP/s from MEASURED_PEAKS.json (kernels timed alone)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 def profiled_traffic(workload, algo_bytes):
@@ -336,6 +358,252 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     pool.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_next_row(args, cfg, kb, torch, rank, world, local_rank):
+    """The rows after the decode path, one GPU each (rank 0; other ranks exit):
+    - next_prefix_disk: a 4096-token entry stored to the disk tier (gather +
+      safetensors write, write-behind then waited for) and served after a
+      restart (a fresh cache on the same directory: file read + restore
+      kernel into pool blocks); GB/s of entry bytes each way.
+    - next_rope_append: 256-token chunks appended to 32 sequences with the
+      fused RoPE (krill_append_quantize_rope) and without it; appended
+      tokens/s and HBM GB/s of the append kernel.
+    - next_verify4: speculative verify of 4 tokens per sequence (append 4, then
+      krill_verify_attention with n_query = 4) over the configs[1] batch;
+      verified tokens/s against the unique cache bytes.
+    - next_prefill512: 512-token chunks of prefill over a 4096-token int8
+      cache per sequence (append the chunk, then krill_prefill_attention);
+      prefill tokens/s and tensor FLOP/s of the causal attention."""
+    if rank != 0:
+        return
+    import tempfile, shutil
+    layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
+    per_tok = hkv * (2 * D + 8 * D // G)  # int8 codes + f16 scales/zeros per token-layer
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = measured_peak()
+    base = {"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+
+    def rnd(*shape):
+        return torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+
+    if args.config == "next_prefix_disk":
+        P = cfg["prefix"]
+        pool = kb.KVPool(layers, hkv, hq, D, num_blocks=3 * P // 256 + 8, group_size=G, device=local_rank)
+        d = tempfile.mkdtemp(prefix="krill_disk_")
+        try:
+            src = pool.create_sequence()
+            kb.append_quantize(pool, [src], 0, rnd(layers, 1, hkv, P, D), rnd(layers, 1, hkv, P, D))
+            torch.cuda.synchronize()
+            entry_bytes = layers * P * per_tok
+            w_s, r_s = [], []
+            for i in range(args.warmup + args.steps):
+                toks = [i * 1_000_000 + t for t in range(P)]
+                pc = kb.PrefixCache(pool, cache_dir=d, disk_budget_bytes=-1)
+                t0 = time.perf_counter()
+                pc.store_quantized(toks, "m", src)
+                pc.wait_for_disk_writes()
+                t1 = time.perf_counter()
+                pc.close()
+                pc2 = kb.PrefixCache(pool, cache_dir=d, disk_budget_bytes=-1)  # after a restart
+                t2 = time.perf_counter()
+                hit = pc2.lookup_quantized(toks, "m")
+                torch.cuda.synchronize()
+                t3 = time.perf_counter()
+                assert hit is not None and hit.prefix_length == P, "disk tier missed"
+                hit.release()
+                pc2.close()
+                if i >= args.warmup:
+                    w_s.append(t1 - t0)
+                    r_s.append(t3 - t2)
+            w, r = float(np.mean(w_s)), float(np.mean(r_s))
+            line = dict(metric="prefix-cache disk tier restore GB/s (restart hit)",
+                        value=entry_bytes / r / 1e9, unit="GB/s", ms_per_step=r * 1e3,
+                        dtype="u8", **base,
+                        config={"workload": args.config, "prefix_tokens": P, "layers": layers,
+                                "kv_heads": hkv, "head_dim": D, "group_size": G,
+                                "entry_bytes": entry_bytes, "file_system": "tempfile.mkdtemp() on the box"},
+                        write={"GBps": entry_bytes / w / 1e9, "ms": w * 1e3},
+                        roofline=None,
+                        note="host-bound (file I/O and page cache); the restore kernel's HBM work is a small part")
+            print(json.dumps(line), flush=True)
+        finally:
+            shutil.rmtree(d, ignore_errors=True)
+            pool.close()
+        return
+
+    if args.config == "next_rope_append":
+        n, C = cfg["seqs"], cfg["chunk"]
+        total = (args.warmup + args.steps) * C
+        rows = total + C
+        pos = torch.arange(rows, device=dev, dtype=torch.float64)
+        inv = 10000.0 ** (-torch.arange(0, D, 2, device=dev, dtype=torch.float64) / D)
+        ang = pos[:, None] * inv[None, :]
+        cos, sin = torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
+        k, v = rnd(layers, n, hkv, C, D), rnd(layers, n, hkv, C, D)
+        res = {}
+        for mode in ("rope", "plain"):
+            pool = kb.KVPool(layers, hkv, hq, D, num_blocks=n * ((total + 255) // 256 + 1) + 4,
+                             group_size=G, device=local_rank)
+            seqs = [pool.create_sequence() for _ in range(n)]
+            rope = (cos, sin) if mode == "rope" else None
+            for _ in range(args.warmup):
+                kb.append_quantize(pool, seqs, 0, k, v, stream=stream, rope=rope)
+            torch.cuda.synchronize()
+            pool.set_profiling(True)
+            pool.kernel_times()
+            pool.kernel_count()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local_rank) as clocks:
+                ev0.record(stream)
+                for _ in range(args.steps):
+                    kb.append_quantize(pool, seqs, 0, k, v, stream=stream, rope=rope)
+                ev1.record(stream)
+                torch.cuda.synchronize()
+            _, _, app_total, app_n = pool.kernel_times()
+            res[mode] = dict(ms=ev0.elapsed_time(ev1) / args.steps, kernel_ms=app_total / max(1, app_n),
+                             launches=pool.kernel_count(), clocks=clocks.summary(),
+                             err=pool.device_error())
+            pool.close()
+        tokens = n * C
+        algo = tokens * layers * (hkv * D * 2 * 2 + per_tok)  # read new K, V bf16; write codes + meta
+        r = res["rope"]
+        line = dict(metric="fused RoPE + int8 quantize + append tokens/s", value=tokens / (r["ms"] / 1e3),
+                    unit="tokens/s", ms_per_step=r["ms"], dtype="u8", **base,
+                    config={"workload": args.config, "seqs": n, "chunk_tokens": C, "layers": layers,
+                            "kv_heads": hkv, "head_dim": D, "group_size": G, "kv_in_dtype": "bf16",
+                            "rope": "rotate-half, base 10000, caller-owned f32 cos/sin table"},
+                    roofline={"bound": "hbm", "kernel": "append_quantize_kernel (RoPE)",
+                              "achieved": algo / (r["kernel_ms"] / 1e3) / 1e9, "peak": peak,
+                              "unit": "GB/s", "peak_kind": peak_kind,
+                              "frac": algo / (r["kernel_ms"] / 1e3) / 1e9 / peak,
+                              "algo_bytes": algo, "kernel_ms": r["kernel_ms"]},
+                    plain_append={"tokens_per_s": tokens / (res["plain"]["ms"] / 1e3),
+                                  "kernel_ms": res["plain"]["kernel_ms"],
+                                  "frac": algo / (res["plain"]["kernel_ms"] / 1e3) / 1e9 / peak},
+                    gpu_launches=r["launches"], clocks=r["clocks"], device_error_flag=r["err"])
+        print(json.dumps(line), flush=True)
+        return
+
+    if args.config == "next_verify4":
+        n, nq = cfg["seqs"], cfg["n_query"]
+        lens = sample_lengths(cfg, n)
+        total_new = (args.warmup + args.steps) * nq
+        pool = kb.KVPool(layers, hkv, hq, D, num_blocks=sum((L + total_new + 255) // 256 for L in lens) + 4,
+                         group_size=G, device=local_rank)
+        seqs = [pool.create_sequence() for _ in lens]
+        for s_, L in zip(seqs, lens):
+            for l0 in range(0, layers, 8):
+                kb.append_quantize(pool, [s_], l0, rnd(8, 1, hkv, L, D), rnd(8, 1, hkv, L, D))
+        k1, v1 = rnd(layers, n, hkv, nq, D), rnd(layers, n, hkv, nq, D)
+        q = rnd(layers, n, nq, hq, D)
+        out = torch.empty_like(q)
+        for _ in range(args.warmup):
+            kb.append_quantize(pool, seqs, 0, k1, v1, stream=stream)
+            kb.verify_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+        torch.cuda.synchronize()
+        len0 = [s_.length(0) for s_ in seqs]
+        pool.set_profiling(True)
+        pool.kernel_times()
+        pool.kernel_count()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            ev0.record(stream)
+            for _ in range(args.steps):
+                kb.append_quantize(pool, seqs, 0, k1, v1, stream=stream)
+                kb.verify_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        am, an, _, _ = pool.kernel_times()
+        ms = ev0.elapsed_time(ev1) / args.steps
+        attn_ms = am / max(1, an)
+        # unique bytes: each sequence's cache once per layer (lengths after the
+        # step's append), plus q and out; logical: query j reads its prefix
+        uniq, logical = 0.0, 0.0
+        for i in range(args.steps):
+            for L0 in len0:
+                L = L0 + (i + 1) * nq
+                uniq += layers * (L * per_tok + 2 * nq * hq * D * 2)
+                logical += layers * (sum(L - nq + 1 + j for j in range(nq)) * per_tok + 2 * nq * hq * D * 2)
+        uniq /= args.steps
+        logical /= args.steps
+        line = dict(metric="int8-KV speculative verify tokens/s (4 queries per sequence)",
+                    value=n * nq / (ms / 1e3), unit="tokens/s", ms_per_step=ms, dtype="u8", **base,
+                    config={"workload": args.config, "seqs": n, "n_query": nq, "layers": layers,
+                            "q_heads": hq, "kv_heads": hkv, "head_dim": D, "group_size": G,
+                            "mean_len": float(np.mean(lens)), "path": "one decode unit per query (n_query x GQA < 64 rows)"},
+                    roofline={"bound": "hbm", "kernel": "attn_tc_kernel", "attn_ms": attn_ms,
+                              "achieved_unique": uniq / (attn_ms / 1e3) / 1e9,
+                              "achieved_logical": logical / (attn_ms / 1e3) / 1e9,
+                              "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                              "frac_unique": uniq / (attn_ms / 1e3) / 1e9 / peak,
+                              "frac_logical": logical / (attn_ms / 1e3) / 1e9 / peak,
+                              "algo_bytes_unique": uniq, "algo_bytes_logical": logical},
+                    gpu_launches=pool.kernel_count(), clocks=clocks.summary(),
+                    device_error_flag=pool.device_error())
+        pool.close()
+        print(json.dumps(line), flush=True)
+        return
+
+    if args.config == "next_prefill512":
+        n, P, C = cfg["seqs"], cfg["prefix"], cfg["chunk"]
+        total = P + (args.warmup + args.steps) * C
+        pool = kb.KVPool(layers, hkv, hq, D, num_blocks=n * ((total + 255) // 256 + 1) + 4, group_size=G,
+                         device=local_rank)
+        seqs = [pool.create_sequence() for _ in range(n)]
+        for s_ in seqs:
+            for l0 in range(0, layers, 8):
+                kb.append_quantize(pool, [s_], l0, rnd(8, 1, hkv, P, D), rnd(8, 1, hkv, P, D))
+        kc, vc = rnd(layers, n, hkv, C, D), rnd(layers, n, hkv, C, D)
+        q = rnd(layers, n, C, hq, D)
+        out = torch.empty_like(q)
+        for _ in range(args.warmup):
+            kb.append_quantize(pool, seqs, 0, kc, vc, stream=stream)
+            kb.prefill_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+        torch.cuda.synchronize()
+        len0 = seqs[0].length(0)
+        pool.set_profiling(True)
+        pool.kernel_times()
+        pool.kernel_count()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            ev0.record(stream)
+            for _ in range(args.steps):
+                kb.append_quantize(pool, seqs, 0, kc, vc, stream=stream)
+                kb.prefill_attention(pool, seqs, 0, q, out, cfg["scale"], stream=stream)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        am, an, pm, pn = pool.kernel_times()
+        ms = ev0.elapsed_time(ev1) / args.steps
+        attn_ms = am / max(1, an)
+        # causal attention FLOPs: query j of a chunk ending at length L sees
+        # L - C + j + 1 keys; q·kᵀ and p·v are 2·D FLOPs each per (query head, key)
+        flops = 0.0
+        for i in range(args.steps):
+            L = len0 + (i + 1) * C
+            keys = C * (L - C) + C * (C + 1) / 2
+            flops += n * layers * hq * 4 * D * keys
+        flops /= args.steps
+        tpeak, tpeak_kind = measured_tensor_peak()
+        line = dict(metric="int8-KV chunked-prefill attention tokens/s (512-token chunks)",
+                    value=n * C / (ms / 1e3), unit="tokens/s", ms_per_step=ms, dtype="u8", **base,
+                    config={"workload": args.config, "seqs": n, "prefix_tokens": P, "chunk_tokens": C,
+                            "layers": layers, "q_heads": hq, "kv_heads": hkv, "head_dim": D,
+                            "group_size": G, "path": "causal tcgen05 cascade items"},
+                    roofline={"bound": "tensor", "kernel": "attn_shared_umma_kernel (causal)",
+                              "attn_ms": attn_ms, "append_ms": pm / max(1, pn),
+                              "achieved": flops / (attn_ms / 1e3) / 1e12, "peak": tpeak,
+                              "unit": "TFLOP/s", "peak_kind": tpeak_kind,
+                              "frac": flops / (attn_ms / 1e3) / 1e12 / tpeak, "algo_flops": flops},
+                    gpu_launches=pool.kernel_count(), clocks=clocks.summary(),
+                    device_error_flag=pool.device_error())
+        pool.close()
+        print(json.dumps(line), flush=True)
+        return
 
 
 def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
@@ -546,6 +814,12 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
+        if args.config in NEXT_ROWS:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "no CPU restatement is timed for "
+                                  "the rows after the decode path; their oracles are test-only"}),
+                      flush=True)
+            return
         run_reference_arm(args, cfg, rank, world)
         return
 
@@ -567,6 +841,11 @@ def main():
 
     import krill_b200 as kb
 
+    if args.config in NEXT_ROWS:
+        run_next_row(args, cfg, kb, torch, rank, world, local_rank)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if "prefix" in cfg:
         run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank)
         return
