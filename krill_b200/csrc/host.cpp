@@ -409,7 +409,10 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
         if (sv[i]->len[lb + li] + n_new > rope.rows)
           return fail(KRILL_ERR_INVALID, "position %lld beyond the %lld-row rope table",
                       (long long)(sv[i]->len[lb + li] + n_new - 1), (long long)rope.rows);
-  const size_t n_dst = (size_t)lc * n_seqs * n_new;
+  // tiled appends (int8 pools) take one entry per touched sub-block
+  const bool tiled = append_uses_tiles(n_new) && p->geom.fmt == kFmtInt8;
+  const int n_chunks = append_tile_chunks(n_new, p->geom.subt);
+  const size_t n_dst = (size_t)lc * n_seqs * (tiled ? n_chunks : n_new);
   StageSlot* slot = nullptr;
   std::vector<AppendDst> dry;
   AppendDst* dst;
@@ -435,6 +438,16 @@ krill_status_t do_append(krill_pool_t p, int32_t n_seqs, const krill_seq_t* seqs
     }
     for (int li = 0; li < lc; ++li) {
       int64_t p0 = s.len[lb + li];
+      if (tiled) {
+        const int64_t T = p->geom.subt, base = p0 - p0 % T;
+        for (int c = 0; c < n_chunks; ++c) {
+          const int64_t pos = std::max<int64_t>(p0, base + c * T);
+          AppendDst& d = dst[((size_t)li * n_seqs + si) * n_chunks + c];
+          d.block = pos < p0 + n_new ? s.blocks[block_index(p, pos)] : -1;
+          d.pos = (int32_t)std::min<int64_t>(pos, INT32_MAX);
+        }
+        continue;
+      }
       for (int t = 0; t < n_new; ++t) {
         int64_t pos = p0 + t;
         AppendDst& d = dst[((size_t)li * n_seqs + si) * n_new + t];

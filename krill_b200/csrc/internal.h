@@ -136,6 +136,14 @@ struct RopeTable {
   int64_t rows;
 };
 
+// Appends of at least this many tokens per (layer, sequence) into an int8
+// pool run the tiled append kernel (one CTA per destination sub-block). Their
+// destination list is compact: per (layer, sequence), append_tile_chunks
+// entries, entry c giving the block and position of the first new token in
+// the c-th sub-block the call touches (unused entries past the last one).
+inline bool append_uses_tiles(int n_new) { return n_new >= 16; }
+inline int append_tile_chunks(int n_new, int subt) { return (n_new + subt - 1) / subt + 1; }
+
 // Kernels that store scales raise *large_scale when one has |s| >= 64 (the
 // one-fma dequantization is exact only below that).
 cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, int layer_begin,

@@ -14,6 +14,7 @@
 namespace krill {
 namespace {
 
+
 template <int EPL>
 struct VecIn;  // EPL 16-bit inputs per lane
 template <> struct VecIn<2> { using T = uint32_t; };
@@ -83,8 +84,75 @@ __device__ inline void store_kcodes(uint8_t* sb, int D, int t, int lane, const u
   }
 }
 
+// One token's K and V rows (input row elem_off / D), K rotated at `pos` when a
+// rotary table is given, quantized per group: the per-token core shared by
+// both append kernels, so both produce the same bits.
+template <int EPL>
+__device__ __forceinline__ typename VecIn<EPL>::T load_raw(const void* src, int64_t elem_off,
+                                                            int lane) {
+  using T = typename VecIn<EPL>::T;
+  return *(reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(src) + elem_off) + lane);
+}
+template <int EPL>
+__device__ __forceinline__ void raw_to_float(const typename VecIn<EPL>::T& r, int dtype,
+                                             float (&x)[EPL]) {
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(&r);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) x[e] = bits_to_float(h[e], dtype);
+}
+
+template <int EPL, int LPG>
+__device__ __forceinline__ void quant_values(float (&xk)[EPL], float (&xv)[EPL], int64_t pos, int D,
+                                             int lane, int dtype, int variant,
+                                             const RopeTable& rope, uint8_t (&ck)[EPL],
+                                             uint8_t (&cv)[EPL], uint16_t& sk, uint16_t& zk,
+                                             uint16_t& sv, uint16_t& zv);
+
+template <int EPL, int LPG>
+__device__ __forceinline__ void quant_token(const void* __restrict__ k, const void* __restrict__ v,
+                                            int64_t elem_off, int64_t pos, int D, int lane,
+                                            int dtype, int variant, const RopeTable& rope,
+                                            uint8_t (&ck)[EPL], uint8_t (&cv)[EPL], uint16_t& sk,
+                                            uint16_t& zk, uint16_t& sv, uint16_t& zv) {
+  float xk[EPL], xv[EPL];
+  load_row<EPL>(k, elem_off, lane, dtype, xk);
+  load_row<EPL>(v, elem_off, lane, dtype, xv);
+  quant_values<EPL, LPG>(xk, xv, pos, D, lane, dtype, variant, rope, ck, cv, sk, zk, sv, zv);
+}
+
+template <int EPL, int LPG>
+__device__ __forceinline__ void quant_values(float (&xk)[EPL], float (&xv)[EPL], int64_t pos, int D,
+                                             int lane, int dtype, int variant,
+                                             const RopeTable& rope, uint8_t (&ck)[EPL],
+                                             uint8_t (&cv)[EPL], uint16_t& sk, uint16_t& zk,
+                                             uint16_t& sv, uint16_t& zv) {
+  if (rope.cos) {
+    // Rotate-half RoPE at the token's absolute position (MLXFast.RoPE with
+    // traditional: false): element d < D/2 pairs with d + D/2, which lives 16
+    // lanes away. Unfused f32 products and sum, then the input-dtype rounding
+    // the reference's rotated K carries before it is quantized.
+    const int half = D / 2;
+    const float* cr = rope.cos + pos * half;
+    const float* sr = rope.sin + pos * half;
+    float other[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, xk[e], 16);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int i = (lane * EPL + e) % half;
+      const float c = __ldg(cr + i), sn = __ldg(sr + i);
+      const float y = lane < 16 ? __fsub_rn(__fmul_rn(xk[e], c), __fmul_rn(other[e], sn))
+                                : __fadd_rn(__fmul_rn(other[e], sn), __fmul_rn(xk[e], c));
+      xk[e] = round_in(y, dtype);
+    }
+  }
+  quantize_lane<EPL, LPG>(xk, dtype, variant, ck, sk, zk);
+  quantize_lane<EPL, LPG>(xv, dtype, variant, cv, sv, zv);
+}
+
 // One warp per (layer, seq, kv-head, new token): quantize its K row and V row
-// and write codes + meta straight into the destination sub-block.
+// and write codes + meta straight into the destination sub-block (appends of
+// a few tokens, i.e. decode steps).
 template <int EPL, int LPG>
 __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restrict__ pool, Geom geom,
                                                               const AppendDst* __restrict__ dst,
@@ -114,34 +182,10 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
   uint8_t* sb = pool + (((int64_t)d.block * geom.L + (layer_begin + li)) * geom.Hkv + h) * geom.page_bytes +
                 (int64_t)(slot / geom.subt) * geom.sb_bytes;
 
-  const int64_t elem_off = w * D;
-  float xk[EPL], xv[EPL];
-  load_row<EPL>(k, elem_off, lane, dtype, xk);
-  load_row<EPL>(v, elem_off, lane, dtype, xv);
-  if (rope.cos) {
-    // Rotate-half RoPE at the token's absolute position (MLXFast.RoPE with
-    // traditional: false): element d < D/2 pairs with d + D/2, which lives 16
-    // lanes away. Unfused f32 products and sum, then the input-dtype rounding
-    // the reference's rotated K carries before it is quantized.
-    const int half = D / 2;
-    const float* cr = rope.cos + (int64_t)d.pos * half;
-    const float* sr = rope.sin + (int64_t)d.pos * half;
-    float other[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, xk[e], 16);
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const int i = (lane * EPL + e) % half;
-      const float c = __ldg(cr + i), sn = __ldg(sr + i);
-      const float y = lane < 16 ? __fsub_rn(__fmul_rn(xk[e], c), __fmul_rn(other[e], sn))
-                                : __fadd_rn(__fmul_rn(other[e], sn), __fmul_rn(xk[e], c));
-      xk[e] = round_in(y, dtype);
-    }
-  }
   uint8_t ck[EPL], cv[EPL];
   uint16_t sk, zk, sv, zv;
-  quantize_lane<EPL, LPG>(xk, dtype, geom.quant_variant, ck, sk, zk);
-  quantize_lane<EPL, LPG>(xv, dtype, geom.quant_variant, cv, sv, zv);
+  quant_token<EPL, LPG>(k, v, w * D, d.pos, D, lane, dtype, geom.quant_variant, rope, ck, cv, sk, zk,
+                        sv, zv);
 
   store_kcodes<EPL>(sb, D, t, lane, ck);
 #pragma unroll
@@ -154,6 +198,110 @@ __global__ void __launch_bounds__(256) append_quantize_kernel(uint8_t* __restric
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = sv;
     *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = zv;
     if ((sk & 0x7fffu) >= 0x5400u || (sv & 0x7fffu) >= 0x5400u) atomicOr(large_scale, 1);
+  }
+}
+
+// Appends of many tokens (prefill chunks): one CTA of 8 warps per (layer, seq,
+// kv head, destination sub-block). Each warp quantizes tokens with the same
+// per-token core and writes its K row directly (one coalesced row), but the
+// transposed V codes and the scales / zeros, which the one-warp-per-token
+// kernel scatters as single bytes and halves, are staged in shared memory and
+// written row by row: 16-byte stores when the call covers the whole sub-block,
+// else only the covered slots (other tokens of the sub-block stay untouched).
+template <int EPL, int LPG>
+__global__ void __launch_bounds__(256) append_tile_kernel(uint8_t* __restrict__ pool, Geom geom,
+                                                          const AppendDst* __restrict__ dst,
+                                                          int layer_begin, int n_seqs, int n_new,
+                                                          int n_chunks, const void* __restrict__ k,
+                                                          const void* __restrict__ v, int dtype,
+                                                          int* __restrict__ large_scale,
+                                                          RopeTable rope) {
+  asm volatile("griddepcontrol.launch_dependents;");  // as in append_quantize_kernel
+  extern __shared__ __align__(16) uint8_t app_smem[];
+  const int D = geom.D, T = geom.subt, NG = geom.NG;
+  int64_t b = blockIdx.x;
+  const int c = (int)(b % n_chunks);
+  b /= n_chunks;
+  const int h = (int)(b % geom.Hkv);
+  const int64_t ls = b / geom.Hkv;  // li * n_seqs + si
+  // positions of the call's tokens for this (layer, seq): [p0, p0 + n_new);
+  // chunk c is the c-th sub-block they touch
+  const int64_t p0 = dst[ls * n_chunks].pos;
+  const int64_t cs = p0 - p0 % T + (int64_t)c * T;  // first position of the sub-block
+  const int64_t s0 = max(p0, cs), e0 = min(p0 + n_new, cs + T);
+  if (s0 >= e0) return;
+  const int t_lo = (int)(s0 - cs), t_hi = (int)(e0 - cs);
+  const AppendDst d0 = dst[ls * n_chunks + c];
+  const int slot0 = d0.pos & (kBlockTokens - 1);
+  uint8_t* sb = pool + (((int64_t)d0.block * geom.L + (layer_begin + (ls / n_seqs))) * geom.Hkv + h) *
+                           geom.page_bytes +
+                (int64_t)(slot0 / T) * geom.sb_bytes;
+  // V codes token-major, rows of D + 4 bytes: a lane stores its EPL codes of a
+  // token as one packed word (consecutive lanes, consecutive words), and the
+  // odd word count per row spreads the column reads of the write-out over
+  // the banks
+  const int S = D + 4;
+  uint8_t* vtile = app_smem;                                                   // [T][S]
+  uint16_t* mtile = reinterpret_cast<uint16_t*>(app_smem + (size_t)T * S);  // [4][NG][T]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool large = false;
+  for (int t = t_lo + warp; t < t_hi; t += 8) {
+    uint8_t ck[EPL], cv[EPL];
+    uint16_t sk, zk, sv, zv;
+    quant_token<EPL, LPG>(k, v, ((ls * geom.Hkv + h) * n_new + (cs + t - p0)) * D, cs + t, D, lane,
+                          dtype, geom.quant_variant, rope, ck, cv, sk, zk, sv, zv);
+    store_kcodes<EPL>(sb, D, t, lane, ck);
+    {
+      uint8_t* vp = vtile + t * S + lane * EPL;
+      if constexpr (EPL == 2) {
+        *reinterpret_cast<uint16_t*>(vp) = (uint16_t)(cv[0] | (cv[1] << 8));
+      } else {
+#pragma unroll
+        for (int w4 = 0; w4 < EPL / 4; ++w4)
+          reinterpret_cast<uint32_t*>(vp)[w4] =
+              (uint32_t)cv[4 * w4] | ((uint32_t)cv[4 * w4 + 1] << 8) |
+              ((uint32_t)cv[4 * w4 + 2] << 16) | ((uint32_t)cv[4 * w4 + 3] << 24);
+      }
+    }
+    if ((lane % LPG) == 0) {
+      const int gi = lane / LPG;
+      mtile[(0 * NG + gi) * T + t] = sk;
+      mtile[(1 * NG + gi) * T + t] = zk;
+      mtile[(2 * NG + gi) * T + t] = sv;
+      mtile[(3 * NG + gi) * T + t] = zv;
+      large |= (sk & 0x7fffu) >= 0x5400u || (sv & 0x7fffu) >= 0x5400u;
+    }
+  }
+  if (large) atomicOr(large_scale, 1);
+  __syncthreads();
+  uint8_t* vdst = sb + sb_voff(D);
+  uint16_t* mdst = reinterpret_cast<uint16_t*>(sb + sb_meta_off(D));
+  if (t_lo == 0 && t_hi == T) {
+    // 16 tokens of one V row per 16-byte store, gathered from the token-major tile
+    const int cpr = T / 16, nv = D * cpr, nm = 4 * NG * T * 2 / 16;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      const int r = i / cpr, t0 = (i % cpr) * 16;
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint8_t* c = vtile + (t0 + 4 * q) * S + r;
+        w[q] = (uint32_t)c[0] | ((uint32_t)c[S] << 8) | ((uint32_t)c[2 * S] << 16) |
+               ((uint32_t)c[3 * S] << 24);
+      }
+      reinterpret_cast<uint4*>(vdst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (int i = threadIdx.x; i < nm; i += blockDim.x)
+      reinterpret_cast<uint4*>(mdst)[i] = reinterpret_cast<const uint4*>(mtile)[i];
+  } else {
+    const int wdt = t_hi - t_lo;
+    for (int i = threadIdx.x; i < D * wdt; i += blockDim.x) {
+      const int r = i / wdt, t = t_lo + i % wdt;
+      vdst[r * T + t] = vtile[t * S + r];
+    }
+    for (int i = threadIdx.x; i < 4 * NG * wdt; i += blockDim.x) {
+      const int r = i / wdt, t = t_lo + i % wdt;
+      mdst[r * T + t] = mtile[r * T + t];
+    }
   }
 }
 
@@ -311,11 +459,23 @@ cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, 
   }
   const int epl = g.D / 32;
   const int lpg = g.G / epl;
+  // Multi-token appends take the tiled kernel (whole sub-blocks per CTA);
+  // decode-sized ones keep one warp per token.
+  const bool tiled = append_uses_tiles(n_new);
+  const int n_chunks = append_tile_chunks(n_new, g.subt);
+  const int64_t tiles = (int64_t)layer_count * n_seqs * g.Hkv * n_chunks;
+  const size_t tile_smem = (size_t)g.subt * (g.D + 4) + (size_t)4 * g.NG * g.subt * 2;
 #define KRILL_APPEND(E, P)                                                                    \
   if (epl == E && lpg == P) {                                                                  \
-    append_quantize_kernel<E, P><<<(unsigned)blocks, threads, 0, stream>>>(                    \
-        pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype, large_scale,     \
-        rope);                                                                                 \
+    if (tiled) {                                                                               \
+      append_tile_kernel<E, P><<<(unsigned)tiles, threads, tile_smem, stream>>>(               \
+          pool, g, d_dst, layer_begin, n_seqs, n_new, n_chunks, k, v, dtype, large_scale,      \
+          rope);                                                                               \
+    } else {                                                                                   \
+      append_quantize_kernel<E, P><<<(unsigned)blocks, threads, 0, stream>>>(                  \
+          pool, g, d_dst, layer_begin, layer_count, n_seqs, n_new, k, v, dtype, large_scale,   \
+          rope);                                                                               \
+    }                                                                                          \
     return cudaGetLastError();                                                                 \
   }
   KRILL_APPEND(2, 32)   // D=64,  G=64
