@@ -828,10 +828,9 @@ def main():
     torch.cuda.set_device(local_rank)
     if world > 1:
         from datetime import timedelta
-        # stdout carries exactly one JSON line: keep NCCL's version banner
-        # (NCCL_DEBUG=VERSION) out of it
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # stdout carries exactly one JSON line: NCCL's log (its version banner
+        # included, printed at the VERSION and WARN levels) goes to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
         # first collective up front, so NCCL's lazy setup never overlaps our kernels
