@@ -1561,12 +1561,20 @@ krill_status_t krill_decode_step_host(krill_pool_t p, int32_t n_seqs, const kril
     const int64_t c0 = (int64_t)c * chunk;
     const int32_t lc = (int32_t)std::min<int64_t>(chunk, layer_count - c0);
     CUDA_TRY(cudaStreamWaitEvent(s, p->io.ev[2 + c], 0));
+    // as krill_decode_step: the append rides in the attention's packet
+    DeferredAppend& da = p->deferred;
+    da.pending = false;
     rc = do_append(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc, 1, d + k_off + c0 * kv_l,
-                   d + v_off + c0 * kv_l, kv_dtype, s);
+                   d + v_off + c0 * kv_l, kv_dtype, s, RopeTable{nullptr, nullptr, 0}, &da);
     if (rc == KRILL_OK)
       rc = do_attention(p, n_seqs, seqs, layer_begin + (int32_t)c0, lc,
                         (q_mapped ? q_mapped : d + q_off) + c0 * q_l, q_dtype, d + o_off + c0 * o_l,
-                        out_dtype, scale, s);
+                        out_dtype, scale, s, 1, &da);
+    if (da.pending) {
+      const std::string msg = krill_last_error_string();
+      flush_deferred_append(p, da, s);
+      if (rc != KRILL_OK) set_error(rc, msg.c_str());
+    }
     if (rc != KRILL_OK) break;
     if (c + 1 < n_ch) {
       rc = copy_in(c + 1);
