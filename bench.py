@@ -828,15 +828,23 @@ def main():
     torch.cuda.set_device(local_rank)
     if world > 1:
         from datetime import timedelta
-        # stdout carries exactly one JSON line: NCCL's log (its version banner
-        # included, printed at the VERSION and WARN levels) goes to stderr
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-        # first collective up front, so NCCL's lazy setup never overlaps our kernels
-        warm = torch.ones(1, device=torch.device("cuda", local_rank))
-        dist.all_reduce(warm)
-        torch.cuda.synchronize()
+        # stdout carries exactly one JSON line: while NCCL initialises (its
+        # version banner is printed to stdout when the environment sets
+        # NCCL_DEBUG=VERSION), file descriptor 1 points at stderr
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+            # first collective up front, so NCCL's lazy setup never overlaps our kernels
+            warm = torch.ones(1, device=torch.device("cuda", local_rank))
+            dist.all_reduce(warm)
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
     import krill_b200 as kb
 
