@@ -641,15 +641,20 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
   const AttnUnit un = p.units[u];
   const float* base = p.partials + ((int64_t)un.first_split * Hkv + h) * partial_floats(D);
   const int64_t stride = (int64_t)Hkv * partial_floats(D);
+  // (loops unrolled so that several records' loads are in flight; the sums
+  // keep record order)
   __shared__ float sm[8], sinv[8];
   if (threadIdx.x < g) {
     const int hq = threadIdx.x;
     float M = -INFINITY;
+#pragma unroll 8
     for (int i = 0; i < un.n_split; ++i) M = fmaxf(M, base[i * stride + hq]);
     float Ls = 0.f;
+#pragma unroll 8
     for (int i = 0; i < un.n_split; ++i) {
       const float mi = base[i * stride + hq];
-      Ls += (mi == -INFINITY) ? 0.f : base[i * stride + 8 + hq] * exp2f(mi - M);
+      const float li = base[i * stride + 8 + hq];
+      Ls += (mi == -INFINITY) ? 0.f : li * exp2f(mi - M);
     }
     sm[hq] = M;
     sinv[hq] = 1.f / Ls;
@@ -660,9 +665,11 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
     const int hq = idx / D, d = idx - hq * D;
     const float M = sm[hq];
     float Os = 0.f;
+#pragma unroll 4
     for (int i = 0; i < un.n_split; ++i) {
       const float mi = base[i * stride + hq];
-      if (mi != -INFINITY) Os += base[i * stride + 16 + hq * D + d] * exp2f(mi - M);
+      const float oi = base[i * stride + 16 + hq * D + d];
+      Os = (mi != -INFINITY) ? Os + oi * exp2f(mi - M) : Os;
     }
     store_out(p.out, p.out_dtype, orow + idx, Os * sinv[hq]);
   }
