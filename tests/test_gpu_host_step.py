@@ -140,3 +140,36 @@ def test_host_step_shared_prefix_cascade():
         assert pb.last_cascade()[0] >= 1
         assert torch.equal(out_dev.cpu().view(torch.int16), out_host.view(torch.int16)), f"step {step}"
     assert pa.device_error() == 0 and pb.device_error() == 0
+
+
+def test_decode_step_keeps_its_append_when_attention_fails():
+    """krill_decode_step carries the append's destinations in the attention's
+    metadata upload. When the attention call then fails (here: an invalid
+    output dtype, rejected before any launch), the append is still uploaded
+    and launched on its own: the cache must equal a twin pool that appended
+    the same token normally, bit for bit."""
+    import ctypes as C
+    from krill_b200 import _lib as L
+    layers, hkv, hq, D, dtype = 2, 8, 32, 128, BF16
+    rng = np.random.default_rng(21)
+    (pa, pb), (sa, sb) = twin_pools(layers, hkv, hq, D, [300, 1000], dtype, rng)
+    n = 2
+    k1 = dev_bits(to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype), dtype)
+    v1 = dev_bits(to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype), dtype)
+    q = dev_bits(to_bits(kv_values(rng, (layers, n, hq, D)), dtype), dtype)
+    out = torch.empty((layers, n, hq, D), dtype=torch.float32, device="cuda")
+    arr = (C.c_uint64 * n)(*[s.handle for s in sa])
+    st = L.lib.krill_decode_step(pa.handle, n, arr, 0, layers, k1.data_ptr(), v1.data_ptr(), L.DTYPE_BF16,
+                                 q.data_ptr(), L.DTYPE_BF16, out.data_ptr(), 9, 0.088, None)
+    assert st == L.KRILL_ERR_INVALID
+    kb.append_quantize(pb, sb, 0, k1, v1)
+    torch.cuda.synchronize()
+    for a, b in zip(sa, sb):
+        for layer in range(layers):
+            assert a.length(layer) == b.length(layer)
+    oa, ob = torch.empty_like(out), torch.empty_like(out)
+    kb.decode_attention(pa, sa, 0, q, oa, 0.088)
+    kb.decode_attention(pb, sb, 0, q, ob, 0.088)
+    torch.cuda.synchronize()
+    assert torch.equal(oa.cpu().view(torch.int32), ob.cpu().view(torch.int32))
+    assert pa.device_error() == 0 and pb.device_error() == 0
