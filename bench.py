@@ -182,6 +182,33 @@ def profiled_traffic(workload, algo_bytes):
     return None
 
 
+def pinned_copy(torch, t):
+    """A page-locked host copy of device tensor `t`."""
+    return torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
+
+
+def host_step_seconds(torch, dist, world, dev, stream, step_fn, steps):
+    """Seconds per step of `step_fn` (public calls whose inputs and outputs
+    are host buffers), by the wall clock from the call until the host holds
+    the outputs; one untimed step first, mean over `steps`, max over ranks."""
+    step_fn()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    total = 0.0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step_fn()
+        stream.synchronize()
+        total += time.perf_counter() - t0
+    sec = total / steps
+    if world > 1:
+        t = torch.tensor([sec], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t.item())
+    return sec
+
+
 def cpu_baseline(cfg, lengths, steps, threads, layer_sample):
     """Time the oracle's reference-dataflow restatement on a bounded sample:
     all sequences, `layer_sample` of the layers, `steps` steps; scaled to the
@@ -252,7 +279,8 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     P, S, n = cfg["prefix"], cfg["suffix"], cfg["seqs"]
     tdt = torch.bfloat16
     dev = torch.device("cuda", local_rank)
-    steps_total = args.warmup + args.steps + 2
+    e2e_steps = max(3, args.steps // 2)
+    steps_total = args.warmup + args.steps + e2e_steps + 3
     blocks = P // 256 + n * ((P + S + steps_total + 255) // 256 - P // 256 + 1) + 4
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, device=local_rank)
     pc = kb.PrefixCache(pool)
@@ -316,6 +344,17 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     total_ms = start.elapsed_time(stop)
     am, an, pm, pn = pool.kernel_times()
     launches = pool.kernel_count()
+    pool.set_profiling(False)
+    # end to end: the same step through krill_decode_step_host with
+    # page-locked host inputs and output
+    h_k, h_v, h_q = pinned_copy(torch, k1), pinned_copy(torch, v1), pinned_copy(torch, q)
+    h_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    e2e_s = host_step_seconds(
+        torch, dist, world, dev, stream,
+        lambda: kb.decode_step_host(pool, seqs, 0, h_k, h_v, h_q, h_out, cfg["scale"], stream=stream),
+        e2e_steps)
+    h2d = sum(t.numel() * t.element_size() for t in (h_k, h_v, h_q))
+    d2h = h_out.numel() * h_out.element_size()
     ms = total_ms / args.steps
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -349,6 +388,9 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                          "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
                          "frac_unique": unique / (attn_ms / 1e3) / 1e9 / peak,
                          "algo_bytes_logical": logical, "algo_bytes_unique": unique},
+            "e2e": {"value": n * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
+                    "ms_per_step": e2e_s * 1e3, "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "device_error_flag": pool.device_error(),
@@ -626,7 +668,8 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     shared = set(i for i in range(n) if rng.random() < cfg["shared_frac"] and mine[i] > cfg["shared_prefix"])
     P = cfg["shared_prefix"]
     dev = torch.device("cuda", local_rank)
-    steps_total = args.warmup + args.steps + 2
+    e2e_steps = max(3, args.steps // 2)
+    steps_total = args.warmup + args.steps + e2e_steps + 3
     blocks_g = sum((L + steps_total + 255) // 256 for L in mine) + 8
     glob = kb.KVPool(Lg, hkv, hq, D, num_blocks=blocks_g, group_size=G, device=local_rank)
     slid = kb.KVPool(Ls, hkv, hq, D, num_blocks=n * 5 + 8, group_size=G, window=W, max_append=256,
@@ -736,6 +779,24 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     launches = glob.kernel_count() + slid.kernel_count()
     ag, _, pg, _ = glob.kernel_times()
     as_, _, ps, _ = slid.kernel_times()
+    glob.set_profiling(False)
+    slid.set_profiling(False)
+    # end to end: both pools' steps through krill_decode_step_host with
+    # page-locked host inputs and outputs
+    hkg, hks = pinned_copy(torch, kg), pinned_copy(torch, ks)
+    hqg, hqs = pinned_copy(torch, qg), pinned_copy(torch, qs)
+    hog = torch.empty(og.shape, dtype=og.dtype, pin_memory=True)
+    hos = torch.empty(os_.shape, dtype=os_.dtype, pin_memory=True)
+
+    def host_step():
+        kb.decode_step_host(glob, gseqs, 0, hkg, hkg, hqg, hog, cfg["scale"], stream=stream)
+        kb.decode_step_host(slid, sseqs, 0, hks, hks, hqs, hos, cfg["scale"], stream=stream)
+
+    e2e_s = host_step_seconds(torch, dist, world, dev, stream, host_step, e2e_steps)
+    # K and V of a step are the same host tensor, copied once per use
+    h2d = sum(2 * t.numel() * t.element_size() for t in (hkg, hks))
+    h2d += sum(t.numel() * t.element_size() for t in (hqg, hqs))
+    d2h = sum(t.numel() * t.element_size() for t in (hog, hos))
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -770,6 +831,9 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                          "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
                          "frac": (glob_b + slid_b + qo) / (attn_ms / 1e3) / 1e9 / peak,
                          "algo_bytes": glob_b + slid_b + qo},
+            "e2e": {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
+                    "ms_per_step": e2e_s * 1e3, "steps": e2e_steps},
             "gpu_launches": launches, "fill_s": t_fill, "clocks": clocks.summary(),
             "prefix_peer_fetch": [f for f in fetches if f],
             "device_error_flag": glob.device_error() | slid.device_error(),

@@ -94,6 +94,42 @@ def test_host_step_layer_subrange_and_errors():
                             host_tensor(qb, dtype, True), out_host, 0.125)
 
 
+@pytest.mark.parametrize("chunk", [0, 1])
+def test_host_step_sliding_window_pool(chunk):
+    """A sliding-window pool (ring of blocks, RotatingKVCache semantics):
+    the host-buffer step must match the device step bit for bit while the
+    ring wraps."""
+    layers, hkv, hq, D, dtype, window = 2, 4, 8, 256, F16, 128
+    rng = np.random.default_rng(21 + chunk)
+    lengths = [10, 300, 700]
+    pools = [kb.KVPool(layers, hkv, hq, D, num_blocks=32, group_size=64, window=window, split_tokens=256)
+             for _ in range(2)]
+    seqs = [[], []]
+    for L in lengths:
+        k = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        v = to_bits(kv_values(rng, (layers, hkv, L, D)), dtype)
+        for i in range(2):
+            s = pools[i].create_sequence()
+            prefill(pools[i], s, k, v, dtype, chunk=256)
+            seqs[i].append(s)
+    (pa, pb), (sa, sb) = pools, seqs
+    n = len(lengths)
+    for step in range(3):
+        k1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        v1 = to_bits(kv_values(rng, (layers, n, hkv, 1, D)), dtype)
+        qb = to_bits(kv_values(rng, (layers, n, hq, D)), dtype)
+        out_dev = torch.empty((layers, n, hq, D), dtype=torch.float16, device="cuda")
+        kb.decode_step(pa, sa, 0, dev_bits(k1, dtype), dev_bits(v1, dtype), dev_bits(qb, dtype), out_dev, 1.0)
+        out_host = torch.empty((layers, n, hq, D), dtype=torch.float16, pin_memory=True)
+        out_host.fill_(float("nan"))
+        kb.decode_step_host(pb, sb, 0, host_tensor(k1, dtype, True), host_tensor(v1, dtype, True),
+                            host_tensor(qb, dtype, True), out_host, 1.0, layer_chunk=chunk)
+        torch.cuda.synchronize()
+        assert torch.equal(out_dev.cpu().view(torch.int16), out_host.view(torch.int16)), f"step {step}"
+    assert [s.length(0) for s in sb] == [L + 3 for L in lengths]
+    assert pa.device_error() == 0 and pb.device_error() == 0
+
+
 def test_host_step_shared_prefix_cascade():
     """Forks of one prefix-cache entry attend the shared blocks through the
     tcgen05 cascade kernel, which then reads the query from mapped host
