@@ -46,7 +46,8 @@ CONFIGS = {
     "llama32_1b_single": dict(layers=16, hq=32, hkv=8, D=64, G=64, dtype="f16", seqs=1,
                               lens=("fixed", 2048, 2048, 0), scale=1 / 8.0, steps=128),
     "qwen3_30b_longctx": dict(layers=48, hq=32, hkv=4, D=128, G=64, dtype="bf16", seqs=16,
-                              lens=("fixed", 32768, 32768, 3), scale=1 / math.sqrt(128)),
+                              lens=("fixed", 32768, 32768, 3), scale=1 / math.sqrt(128),
+                              values="N(0,0.5)+1%N(0,8)"),
     # 64 requests = one shared 4096-token prefix + a unique 256-token suffix
     # 26 layers = 22 sliding (window 1024) + 4 global, D=256, 256 ragged seqs
     "gemma_mixed_256": dict(layers=26, layers_global=4, layers_sliding=22, window=1024, hq=8, hkv=4,
@@ -70,6 +71,12 @@ NEXT_ROWS = {
 CONFIGS.update(NEXT_ROWS)
 DEFAULT_CONFIG = "llama31_8b_batch32"
 L2_FLUSH_BYTES = 256 << 20  # 2 x the B200's 126 MB L2, rounded up
+# The timed region (K steps) is repeated this many times; `value` comes from
+# the median repetition.
+REPEATS = 5
+# At N > 1 rank 0 stores a prefix entry of this many tokens and every other
+# rank imports it over NVLink (outside the timed region) and checks it.
+PEER_PREFIX = 4096
 
 
 def algo_bytes_attn(L, hkv, D, G):
@@ -86,6 +93,18 @@ def step_bytes(lengths_after, cfg, raw=False):
     qo = len(lengths_after) * layers * 2 * hq * D * 2
     append = len(lengths_after) * layers * (hkv * D * 4 + hkv * per_tok)
     return attn + qo, attn + qo + append
+
+
+def kv_randn(torch, cfg, shape, gen, dev):
+    """Seeded synthetic K/V in fp32: N(0,1), or for configs[3] N(0, 0.5) with
+    1% outliers N(0, 8) (a Bernoulli mask)."""
+    x = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32)
+    if cfg.get("values") != "N(0,0.5)+1%N(0,8)":
+        return x
+    x.mul_(math.sqrt(0.5))
+    mask = torch.rand(shape, generator=gen, device=dev) < 0.01
+    out = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32).mul_(math.sqrt(8.0))
+    return torch.where(mask, out, x)
 
 
 def sample_lengths(cfg, n, seed_offset=0):
@@ -110,10 +129,16 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # the timed region starts once sampling is live (nvidia-smi takes
+            # a moment to print its first row)
+            t0 = time.perf_counter()
+            while not self.rows and time.perf_counter() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.first = len(self.rows)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -126,7 +151,8 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.25)
+            self.stop = len(self.rows)  # rows printed while the region ran
+            time.sleep(0.06)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -134,19 +160,23 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
+        # the rows printed while the timed region ran, plus the one that was
+        # live when it started
+        lo = max(0, getattr(self, "first", 1) - 1)
+        rows = self.rows[lo:getattr(self, "stop", len(self.rows)) + 1] or self.rows
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for r in self.rows:
+        for r in rows:
             for name, val in zip(names, r[5:9]):
                 if val.strip().lower() in ("active", "1"):
                     reasons.add(name)
         return {"sm_mhz": float(np.median(sm)) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+                "reasons": sorted(reasons), "samples": len(rows)}
 
 
 def measured_peak():
@@ -233,37 +263,121 @@ def cpu_baseline(cfg, lengths, steps, threads, layer_sample):
     return len(lengths) / per_step_full, el
 
 
+def headline_config(args, cfg, world, lengths_all, mine, raw):
+    """The `config` object of the decode-step workloads' JSON line; the
+    reference arm prints the same one."""
+    step_b = step_bytes([L + 1 for L in mine], cfg, raw)[1]
+    return {"workload": args.config, "kv_format": args.kv, "layers": cfg["layers"], "q_heads": cfg["hq"],
+            "kv_heads": cfg["hkv"], "head_dim": cfg["D"], "group_size": cfg["G"],
+            "kv_in_dtype": cfg["dtype"], "kv_values": cfg.get("values", "N(0,1)"),
+            "seqs_per_gpu": cfg["seqs"], "global_seqs": len(lengths_all),
+            "mean_len": float(np.mean(lengths_all)),
+            "l2": (f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)" if step_b >= L2_FLUSH_BYTES
+                   else f"L2 flushed between steps ({step_b / 1e9:.3f} GB/step < "
+                        f"{L2_FLUSH_BYTES / 1e9:.2f} GB; each step timed alone)"),
+            "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"}
+
+
 def run_reference_arm(args, cfg, rank, world):
     """--impl reference: the reference's CPU dataflow (oracle port), all host
-    threads, rank 0 only."""
+    threads, rank 0 only. The sample is the batch share of one GPU's rank
+    (rank 0's sequences): at N GPUs the driver's ratio then compares N GPUs
+    with one host's cores on the same per-GPU work."""
     if rank != 0:
         return
-    import oracle
     threads = os.cpu_count() or 1
-    lengths = sample_lengths(cfg, cfg["seqs"] * world)
-    # bounded sample per step: every sequence, 1 of the layers
+    from krill_b200.shard import lpt_partition
+    lengths_all = sample_lengths(cfg, cfg["seqs"] * world)
+    mine = [lengths_all[i] for i in lpt_partition(lengths_all, world)[0]]
+    # bounded sample per step: rank 0's sequences, 1 of the layers
     values = []
     t_all = time.perf_counter()
     for _ in range(args.warmup):
-        cpu_baseline(cfg, lengths, 1, threads, 1)
+        cpu_baseline(cfg, mine, 1, threads, 1)
     for _ in range(args.steps):
-        v, _ = cpu_baseline(cfg, lengths, 1, threads, 1)
+        v, _ = cpu_baseline(cfg, mine, 1, threads, 1)
         values.append(v)
     value = float(np.median(values))
+    if "prefix" in cfg or "window" in cfg:
+        config = {"workload": args.config, "seqs": len(mine), "layers": cfg["layers"]}
+    else:
+        config = headline_config(args, cfg, world, lengths_all, mine, False)
     line = {
         "impl": "reference", "metric": "int8-KV decode-attn+append tokens/s", "value": value,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "u8", "data": "synthetic",
-        "config": {"workload": args.config, "seqs": len(lengths), "layers": cfg["layers"]},
+        "config": config,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{len(lengths)} seqs x 1 of {cfg['layers']} layers per step, "
-                                   f"scaled x{cfg['layers']}; oracle/ C++ restatement of "
-                                   "QuantizedKVCache.update + SDPA (MLX CPU path unavailable)"},
+                         "sample": f"{len(mine)} seqs (rank 0's share of {len(lengths_all)}) x 1 of "
+                                   f"{cfg['layers']} layers per step, scaled x{cfg['layers']}; oracle/ "
+                                   "C++ restatement of QuantizedKVCache.update + SDPA (MLX CPU path "
+                                   "unavailable)"},
+        "normalisation": ("one host's cores on one GPU rank's share of the batch; at N GPUs the GPU "
+                          "arm's value covers all N shares"),
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t_all,
     }
     print(json.dumps(line), flush=True)
+
+
+def peer_prefix_check(kb, torch, dist, pool, cfg, rank, world, dev, gen, tdt, stream):
+    """N > 1, outside the timed region: rank 0 stores a PEER_PREFIX-token
+    prefix entry; every other rank imports it from rank 0's pool over NVLink
+    (CUDA IPC handle + entry descriptor, then a peer copy into its own pool,
+    krill_prefix_import) and checks that every layer's codes, scales and zeros
+    are bit-identical to the owner's (krill_seq_snapshot_quantized on both
+    sides; the owner's tensors reach the other ranks by NCCL broadcast).
+    Returns this rank's record (None on rank 0)."""
+    P, layers, hkv, D = PEER_PREFIX, cfg["layers"], cfg["hkv"], cfg["D"]
+    tokens = list(range(1_000_000, 1_000_000 + P))
+    pc = kb.PrefixCache(pool)
+    obj = [None]
+    if rank == 0:
+        base = pool.create_sequence()
+        for l0 in range(0, layers, 4):
+            lc = min(4, layers - l0)
+            kb.append_quantize(pool, [base], l0, kv_randn(torch, cfg, (lc, 1, hkv, P, D), gen, dev).to(tdt),
+                               kv_randn(torch, cfg, (lc, 1, hkv, P, D), gen, dev).to(tdt))
+        pc.store_quantized(tokens, "bench-peer", base)
+        base.release()
+        entry = pc.lookup_quantized(tokens, "bench-peer")
+        torch.cuda.synchronize()
+        obj = [(pool.ipc_handle(), pc.describe(entry))]
+    dist.broadcast_object_list(obj, src=0)
+    rec = None
+    if rank != 0:
+        handle, desc = obj[0]
+        t0 = time.perf_counter()
+        entry = pc.import_entry(handle, desc, stream=stream)  # maps rank 0's pool once
+        torch.cuda.synchronize()
+        first_ms = (time.perf_counter() - t0) * 1e3
+        entry.release()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        entry = pc.import_entry(handle, desc, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        nbytes = (P // 256) * pool.block_bytes
+        rec = {"rank": rank, "bytes": nbytes, "first_import_ms_incl_mapping": first_ms,
+               "copy_ms": e0.elapsed_time(e1), "GB/s": nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9}
+    seq = entry.fork(P)
+    same = True
+    for layer in range(layers):
+        snap = seq.quantized_snapshot(layer)
+        for t in (snap.keys, snap.values, snap.key_scales, snap.key_zeros, snap.value_scales,
+                  snap.value_zeros):
+            ref = t.clone() if rank == 0 else torch.empty_like(t)
+            dist.broadcast(ref, src=0)
+            same = same and torch.equal(ref, t)
+    torch.cuda.synchronize()
+    seq.release()
+    dist.barrier()  # the owner keeps its blocks until every copy is done
+    entry.release()
+    pc.close()
+    if rec is not None:
+        rec["bit_identical"] = bool(same)
+    return rec
 
 
 def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
@@ -280,7 +394,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     tdt = torch.bfloat16
     dev = torch.device("cuda", local_rank)
     e2e_steps = max(3, args.steps // 2)
-    steps_total = args.warmup + args.steps + e2e_steps + 3
+    steps_total = args.warmup + REPEATS * args.steps + e2e_steps + 3
     blocks = P // 256 + n * ((P + S + steps_total + 255) // 256 - P // 256 + 1) + 4
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, device=local_rank)
     pc = kb.PrefixCache(pool)
@@ -321,7 +435,6 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     v1 = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
     q = torch.randn((layers, n, hq, D), generator=gen, device=dev).to(tdt)
     out = torch.empty((layers, n, hq, D), dtype=tdt, device=dev)
-    stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
     torch.cuda.synchronize()
@@ -332,18 +445,25 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     pool.kernel_times()
     pool.kernel_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = []
     with ClockSampler(local_rank) as clocks:
-        torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
-            kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
-        stop.record(stream)
-        torch.cuda.synchronize()
+        for _ in range(REPEATS):
+            torch.cuda.synchronize()
+            start.record(stream)
+            for _ in range(args.steps):
+                kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
+            stop.record(stream)
+            torch.cuda.synchronize()
+            ms = start.elapsed_time(stop) / args.steps
+            if world > 1:
+                t = torch.tensor([ms], dtype=torch.float64, device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            reps.append(ms)
     if world > 1:
         dist.barrier()
-    total_ms = start.elapsed_time(stop)
     am, an, pm, pn = pool.kernel_times()
-    launches = pool.kernel_count()
+    launches = pool.kernel_count() // REPEATS
     pool.set_profiling(False)
     # end to end: the same step through krill_decode_step_host with
     # page-locked host inputs and output
@@ -355,13 +475,9 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
         e2e_steps)
     h2d = sum(t.numel() * t.element_size() for t in (h_k, h_v, h_q))
     d2h = h_out.numel() * h_out.element_size()
-    ms = total_ms / args.steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = float(np.median(reps))
     per_tok = hkv * (2 * D + 8 * D // G)
-    mean_len = len0 + (args.steps + 1) / 2
+    mean_len = len0 + (REPEATS * args.steps + 1) / 2
     logical = n * layers * mean_len * per_tok + n * layers * 2 * hq * D * 2
     unique = layers * (P + n * (mean_len - P)) * per_tok + n * layers * 2 * hq * D * 2
     attn_ms = am / max(1, an)
@@ -393,6 +509,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                     "ms_per_step": e2e_s * 1e3, "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
+            "ms_per_step_repeats": reps,
             "device_error_flag": pool.device_error(),
         }
         print(json.dumps(line), flush=True)
@@ -655,8 +772,9 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     U[1024, 16384]; 30% of them fork a shared 2048-token prefix in the global
     pool (in the sliding layers the prefix's window is overwritten once a
     sequence is 1024 tokens past it). One step = append + attention in both
-    pools. The cache is filled with f16 N(0,1) K/V through the append kernel
-    (sliding layers receive only their last window of tokens)."""
+    pools. The cache is filled with f16 N(0,1) K/V through the append kernel;
+    the sliding layers receive every token of each sequence, 256 per call, so
+    their rings have wrapped as in a long-running request."""
     from krill_b200.shard import lpt_partition
     Lg, Ls, W = cfg["layers_global"], cfg["layers_sliding"], cfg["window"]
     hq, hkv, D, G = cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
@@ -669,7 +787,7 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     P = cfg["shared_prefix"]
     dev = torch.device("cuda", local_rank)
     e2e_steps = max(3, args.steps // 2)
-    steps_total = args.warmup + args.steps + e2e_steps + 3
+    steps_total = args.warmup + REPEATS * args.steps + e2e_steps + 3
     blocks_g = sum((L + steps_total + 255) // 256 for L in mine) + 8
     glob = kb.KVPool(Lg, hkv, hq, D, num_blocks=blocks_g, group_size=G, device=local_rank)
     slid = kb.KVPool(Ls, hkv, hq, D, num_blocks=n * 5 + 8, group_size=G, window=W, max_append=256,
@@ -737,8 +855,9 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     sv = torch.randn((Ls * hkv * 256 * D,), generator=gen, device=dev).to(torch.float16)
     for L in mine:
         s = slid.create_sequence()
-        for _ in range(min(L, W) // 256):
-            kb.append_quantize(slid, [s], 0, chunk(sk, Ls, 256), chunk(sv, Ls, 256))
+        for t0 in range(0, L, 256):  # every token, 256 per call: the ring wraps
+            nt = min(256, L - t0)
+            kb.append_quantize(slid, [s], 0, chunk(sk, Ls, nt), chunk(sv, Ls, nt))
         sseqs.append(s)
     del bufk, bufv
     torch.cuda.synchronize()
@@ -766,19 +885,28 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     glob.kernel_count()
     slid.kernel_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = []
     with ClockSampler(local_rank) as clocks:
-        torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        stop.record(stream)
-        torch.cuda.synchronize()
+        for _ in range(REPEATS):
+            torch.cuda.synchronize()
+            start.record(stream)
+            for _ in range(args.steps):
+                step()
+            stop.record(stream)
+            torch.cuda.synchronize()
+            ms = start.elapsed_time(stop) / args.steps
+            if world > 1:
+                t = torch.tensor([ms], dtype=torch.float64, device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            reps.append(ms)
     if world > 1:
         dist.barrier()
-    ms = start.elapsed_time(stop) / args.steps
-    launches = glob.kernel_count() + slid.kernel_count()
+    ms = float(np.median(reps))
+    launches = (glob.kernel_count() + slid.kernel_count()) // REPEATS
     ag, _, pg, _ = glob.kernel_times()
     as_, _, ps, _ = slid.kernel_times()
+    ag, pg, as_, ps = ag / REPEATS, pg / REPEATS, as_ / REPEATS, ps / REPEATS
     glob.set_profiling(False)
     slid.set_profiling(False)
     # end to end: both pools' steps through krill_decode_step_host with
@@ -797,12 +925,8 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     h2d = sum(2 * t.numel() * t.element_size() for t in (hkg, hks))
     h2d += sum(t.numel() * t.element_size() for t in (hqg, hqs))
     d2h = sum(t.numel() * t.element_size() for t in (hog, hos))
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     per_tok = hkv * (2 * D + 8 * D // G)
-    mid = (args.steps + 1) / 2
+    mid = (REPEATS * args.steps + 1) / 2
     glob_b = sum(L + mid for L in lg0) * Lg * per_tok
     glob_unique = glob_b - len(shared) * P * Lg * per_tok + P * Lg * per_tok
     slid_b = n * min(W, W) * Ls * per_tok
@@ -835,6 +959,9 @@ def run_mixed_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
                     "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
                     "ms_per_step": e2e_s * 1e3, "steps": e2e_steps},
             "gpu_launches": launches, "fill_s": t_fill, "clocks": clocks.summary(),
+            "ms_per_step_repeats": reps,
+            "plan_sliding": {"plan": list(slid.last_plan()), "kernels": slid.last_kernels()},
+            "plan_global": {"plan": list(glob.last_plan()), "kernels": glob.last_kernels()},
             "prefix_peer_fetch": [f for f in fetches if f],
             "device_error_flag": glob.device_error() | slid.device_error(),
         }
@@ -932,8 +1059,9 @@ def main():
     mine = [lengths_all[i] for i in parts[rank]]
     layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
-    total_steps = args.warmup + args.steps * 3 + 2
-    blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4
+    total_steps = args.warmup + args.steps * (REPEATS + 2) + 4
+    # at N > 1 the pool also holds one imported prefix entry (4096 tokens)
+    blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4 + (PEER_PREFIX // 256 if world > 1 else 0)
     raw = args.kv == "bf16"
     if raw and cfg["dtype"] != "bf16":
         raise SystemExit("--kv bf16 needs a workload with bf16 K/V")
@@ -950,16 +1078,20 @@ def main():
     for s, L in zip(seqs, mine):
         for l0 in range(0, layers, chunk_layers):
             lc = min(chunk_layers, layers - l0)
-            k = torch.randn((lc, 1, hkv, L, D), generator=gen, device=dev, dtype=torch.float32).to(tdt)
-            v = torch.randn((lc, 1, hkv, L, D), generator=gen, device=dev, dtype=torch.float32).to(tdt)
+            k = kv_randn(torch, cfg, (lc, 1, hkv, L, D), gen, dev).to(tdt)
+            v = kv_randn(torch, cfg, (lc, 1, hkv, L, D), gen, dev).to(tdt)
             kb.append_quantize(pool, [s], l0, k, v)
             del k, v
     torch.cuda.synchronize()
     t_fill = time.perf_counter() - t_fill
+    stream = torch.cuda.current_stream()
+    peer = None
+    if world > 1:
+        peer = peer_prefix_check(kb, torch, dist, pool, cfg, rank, world, dev, gen, tdt, stream)
 
     n = len(seqs)
-    k_new = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
-    v_new = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
+    k_new = kv_randn(torch, cfg, (layers, n, hkv, 1, D), gen, dev).to(tdt)
+    v_new = kv_randn(torch, cfg, (layers, n, hkv, 1, D), gen, dev).to(tdt)
     q = torch.randn((layers, n, hq, D), generator=gen, device=dev).to(tdt)
     out = torch.empty((layers, n, hq, D), dtype=tdt, device=dev)
     stream = torch.cuda.current_stream()
@@ -1026,29 +1158,36 @@ def main():
 
     # `value`: the step as a user runs it (no per-launch events); then the
     # same number of steps again with the per-kernel events for the roofline
+    # the K-step region is repeated REPEATS times, each the max over ranks;
+    # `value` uses the median repetition
+    reps = []
     with ClockSampler(local_rank) as clocks:
-        total_ms, launches, _ = timed_steps(False)
+        for _ in range(REPEATS):
+            total_ms, launches, _ = timed_steps(False)
+            reps.append(max_over_ranks(total_ms / args.steps))
+    plan, kernels = pool.last_plan(), pool.last_kernels()
     barrier()
     _, _, (attn_total, attn_n, app_total, app_n) = timed_steps(True)
     barrier()
     attn_ms = [attn_total / max(1, attn_n)]
     app_ms = [app_total / max(1, app_n)]
-    ms_step = max_over_ranks(total_ms / args.steps)
+    ms_step = float(np.median(reps))
     tokens_per_step = n_total
     value = tokens_per_step / (ms_step / 1e3)
 
     # algorithmic bytes: lengths after each step's append (the profiled pass
     # runs after the value pass, args.steps tokens further on)
     attn_bytes, step_b = 0, 0
+    mid = (REPEATS // 2) * args.steps  # tokens appended before the median repetition
     for i in range(args.steps):
-        step_b += step_bytes([L + i + 1 for L in len_before], cfg, raw)[1]
-        attn_bytes += step_bytes([L + args.steps + i + 1 for L in len_before], cfg, raw)[0]
+        step_b += step_bytes([L + mid + i + 1 for L in len_before], cfg, raw)[1]
+        attn_bytes += step_bytes([L + REPEATS * args.steps + i + 1 for L in len_before], cfg, raw)[0]
     attn_bytes /= args.steps
     step_b /= args.steps
     attn_mean_ms = float(np.mean(attn_ms))
     peak, peak_kind = measured_peak()
     achieved = attn_bytes / (attn_mean_ms / 1e3) / 1e9
-    step_gbs = step_b / (total_ms / args.steps / 1e3) / 1e9
+    step_gbs = step_b / (ms_step / 1e3) / 1e9
 
     # ---- end to end through the C ABI with host buffers ----
     h_k = torch.empty(k_new.shape, dtype=tdt, pin_memory=True).copy_(k_new.cpu())
@@ -1095,6 +1234,9 @@ def main():
     h2d = (h_k.numel() + h_v.numel() + h_q.numel()) * h_k.element_size()
     d2h = h_out.numel() * h_out.element_size()
     err_flag = pool.device_error()
+    peers = [None] * world
+    if world > 1:
+        dist.all_gather_object(peers, peer)
 
     if rank == 0:
         cpu = None
@@ -1120,15 +1262,10 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16" if raw else "u8",
             "data": "synthetic",
-            "config": {"workload": args.config, "kv_format": args.kv, "layers": layers, "q_heads": hq,
-                       "kv_heads": hkv,
-                       "head_dim": D, "group_size": G, "kv_in_dtype": cfg["dtype"],
-                       "seqs_per_gpu": cfg["seqs"], "global_seqs": n_total,
-                       "mean_len": float(np.mean(lengths_all)),
-                       "l2": (f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)" if flush is None
-                              else f"L2 flushed between steps ({step_b / 1e9:.3f} GB/step < "
-                                   f"{L2_FLUSH_BYTES / 1e9:.2f} GB; each step timed alone)"),
-                       "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"},
+            "config": headline_config(args, cfg, world, lengths_all, mine, raw),
+            "plan": {"pieces_subblocks": plan[0], "kv_heads_per_item": plan[1], "items": plan[2],
+                     "ctas": plan[3], "kernels": kernels},
+            "ms_per_step_repeats": reps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": None if raw else profiled_traffic(args.config, attn_bytes),
@@ -1139,9 +1276,12 @@ def main():
             "e2e": {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "krill_decode_step_host",
                     "layer_chunk": args.e2e_chunk, "ms_steps": [round(x, 4) for x in e2e_ms],
-                    "link": link},
+                    "link": link, "over_value": (n_total / e2e_s) / value,
+                    "bound": ("host link: the step moves h2d + d2h bytes over PCIe each step, "
+                              "the query read in place by the attention kernel")},
             "gpu_launches": launches,
             "clocks": clk,
+            "prefix_peer_import": [x for x in peers if x],
             "prefill_s": t_fill,
             "device_error_flag": err_flag,
         }

@@ -156,6 +156,13 @@ krill_status_t krill_pool_kernel_count(krill_pool_t pool, int64_t* kernels);
  * sub-blocks, kv heads per work item, number of items and of persistent CTAs. */
 krill_status_t krill_pool_last_plan(krill_pool_t pool, int32_t* piece_subblocks,
                                     int32_t* heads_per_item, int64_t* items, int32_t* ctas);
+/* Introspection (no reference counterpart): the kernel instances the last
+ * krill_decode_attention (or verify / prefill / step) on this pool launched,
+ * in order, joined by '+', e.g. "attn_tc_kernel<128,2,8,1,13,0>+
+ * attn_combine_kernel<128>" (template arguments: head_dim, groups per head,
+ * consumer warps, warps per head, pipeline stages, pool format). Written into
+ * buf (NUL-terminated, truncated to cap bytes). */
+krill_status_t krill_pool_last_kernels(krill_pool_t pool, char* buf, int32_t cap);
 /* Introspection (no reference counterpart): the shared-prefix part of the last
  * krill_decode_attention — number of sequence groups attended together, their
  * cascade work items, partial-record slots per member and persistent CTAs
@@ -264,8 +271,13 @@ krill_status_t krill_prefill_attention(krill_pool_t pool, int32_t n_seqs, const 
  *   - Limit: a call whose metadata plus split partials exceed the scratch
  *     (roughly: many sequences longer than 4096 tokens at once) is rejected
  *     with KRILL_ERR_INVALID and a message giving the bytes it would need.
- *   - The first call on a device looks up the scratch's device address (with
- *     that device current); make that first call before any stream capture.
+ *   - The scratch is reserved on a device when the first pool on it is
+ *     created (krill_pool_create looks up its device address with the device
+ *     current, which under lazy module loading is when the driver loads it),
+ *     not during a decode call.
+ *   - A call on a stream that is being captured is rejected with
+ *     KRILL_ERR_INVALID: the metadata is copied from a host buffer that the
+ *     next call overwrites.
  *   - All calls share the one scratch. Every call writes the metadata and
  *     partial results it reads; the arrival counters that merge split
  *     sequences carry a per-call tag, so values left by an earlier call count

@@ -82,6 +82,7 @@ _SIGS = {
     "krill_pool_kernel_times": (i32, [vp, C.POINTER(C.c_double), P_i32, C.POINTER(C.c_double), P_i32]),
     "krill_pool_last_plan": (i32, [vp, P_i32, P_i32, P_i64, P_i32]),
     "krill_pool_last_cascade": (i32, [vp, P_i32, P_i64, P_i32, P_i32]),
+    "krill_pool_last_kernels": (i32, [vp, C.c_char_p, i32]),
     "krill_pool_kernel_count": (i32, [vp, P_i64]),
     "krill_seq_create": (i32, [vp, P_u64]),
     "krill_seq_release": (i32, [vp, u64]),

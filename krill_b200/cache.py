@@ -136,6 +136,13 @@ class KVPool:
         check(L.lib.krill_pool_last_plan(self.handle, C.byref(c), C.byref(hg), C.byref(n), C.byref(g)))
         return c.value, hg.value, n.value, g.value
 
+    def last_kernels(self) -> str:
+        """Kernel instances of the last decode-attention launch, joined by '+'
+        (e.g. 'attn_tc_kernel<128,2,8,1,13,0>+attn_combine_kernel<128>')."""
+        buf = C.create_string_buffer(192)
+        check(L.lib.krill_pool_last_kernels(self.handle, buf, len(buf)))
+        return buf.value.decode()
+
     def ipc_handle(self) -> bytes:
         """This pool's CUDA IPC handle (64 bytes) for krill_prefix_import."""
         buf = C.create_string_buffer(64)

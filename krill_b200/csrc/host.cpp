@@ -134,6 +134,7 @@ struct Plan {
   int64_t last_items = 0;
   int last_groups = 0, last_pslots = 0, last_sh_grid = 0;
   int64_t last_sh_items = 0;
+  char last_kernels[192] = {0};  // kernel instances of the last launch
 };
 
 }  // namespace
@@ -953,6 +954,18 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.last_HG = HG;
   pl.last_items = n_items;
   pl.last_grid = grid;
+  {
+    // the kernel instances this plan launches (dry runs included); only the
+    // fields the description reads are set
+    static unsigned long long ctr_tag;
+    AttnParams dp{};
+    dp.hg = HG;
+    dp.g = g.g;
+    dp.n_split_units = (int)pl.split_units.size();
+    dp.split_ctr = merge_in_kernel ? &ctr_tag : nullptr;
+    dp.sh_grid = sh_grid;
+    describe_attention(g, dp, grid, p->cfg.attn_impl, pl.last_kernels, sizeof(pl.last_kernels));
+  }
   if (p->host_only) return KRILL_OK;  // dry run: planned, nothing launched
   TRY(stage_upload(slot, total, stream));
   AttnParams ap{};
@@ -1145,6 +1158,10 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
         p->stage[i].d = p->stage_arena_d + (size_t)i * kStageSliceBytes;
         p->stage[i].cap = kStageSliceBytes;
       }
+    // The allocation-free entry point's scratch is resolved here, with the
+    // pool's device current, so that the driver reserves it (a module load
+    // under lazy loading) at pool creation rather than inside a decode call.
+    if (e == cudaSuccess) e = krill::noalloc_prepare(device);
     if (e != cudaSuccess) {
       krill_status_t code = (e == cudaErrorMemoryAllocation) ? KRILL_ERR_OOM : KRILL_ERR_CUDA;
       if (p->d_pool) cudaFree(p->d_pool);
@@ -1271,6 +1288,13 @@ krill_status_t krill_pool_last_plan(krill_pool_t p, int32_t* piece_subblocks, in
   if (heads_per_item) *heads_per_item = p->plan.last_HG;
   if (items) *items = p->plan.last_items;
   if (ctas) *ctas = p->plan.last_grid;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_last_kernels(krill_pool_t p, char* buf, int32_t cap) {
+  if (!p || !buf || cap <= 0) return fail(KRILL_ERR_INVALID, "null pool or buffer");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  snprintf(buf, (size_t)cap, "%s", p->plan.last_kernels);
   return KRILL_OK;
 }
 
@@ -3050,5 +3074,7 @@ void count_kernels(krill_pool_t p, int n) {
   std::lock_guard<std::recursive_mutex> lk(p->mu);
   p->kernels += n;
 }
+
+std::recursive_mutex& pool_mutex(krill_pool_t p) { return p->mu; }
 
 }  // namespace krill

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/krill_kv.h"
 #include "kv_common.cuh"
 
@@ -158,6 +160,9 @@ cudaError_t launch_scatter(const Geom& g, uint8_t* pool, int layer, const int32_
 // some unit is split, the combine kernel.
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,
                              cudaStream_t stream);
+// Names the kernel instances launch_attention would run for these arguments.
+void describe_attention(const Geom& g, const AttnParams& p, int grid, int impl, char* buf,
+                        size_t cap);
 cudaError_t launch_shared(const Geom& g, const AttnParams& p, cudaStream_t stream);
 // Merge the partial records of p.split_units (attn_combine_kernel) on its own.
 cudaError_t launch_combine(const Geom& g, const AttnParams& p, cudaStream_t stream);
@@ -191,6 +196,14 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
                             float scale, uint8_t* buf, size_t buf_cap, NoAllocPlan* np);
 // Adds n to the pool's launched-kernel count (krill_pool_kernel_count).
 void count_kernels(krill_pool_t p, int n);
+// The pool's call mutex (recursive): held across planning and launch so that
+// no other thread frees or appends to a planned sequence in between.
+std::recursive_mutex& pool_mutex(krill_pool_t p);
+// Resolves the allocation-free entry point's device scratch on `device`
+// (which must be current). Under lazy module loading this is the moment the
+// driver loads the module and reserves the scratch, so pool creation calls it
+// instead of the first decode call. Idempotent; thread-safe.
+cudaError_t noalloc_prepare(int device);
 // Sets the thread-local message returned by krill_last_error_string().
 krill_status_t set_error(krill_status_t code, const char* msg);
 

@@ -29,7 +29,9 @@
 //     (griddepcontrol.wait) before reading the pool.
 // Every mbarrier wait is bounded; on timeout the kernel raises an error flag
 // and runs to completion instead of hanging.
+#include <algorithm>
 #include <atomic>
+#include <cstdio>
 
 #include "kv_device.cuh"
 
@@ -1185,6 +1187,53 @@ cudaError_t launch_combine(const Geom& g, const AttnParams& p, cudaStream_t stre
   else if (g.D == 256) attn_combine_kernel<256><<<blocks, 128, 0, stream>>>(p);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
+}
+
+namespace {
+template <int D, int NG, int NCW, int R, int FMT>
+int tc_desc(char* buf, size_t cap) {
+  return snprintf(buf, cap, "attn_tc_kernel<%d,%d,%d,%d,%d,%d>", D, NG, NCW, R,
+                  stages_for<D, NG, NCW, R, FMT>(), FMT);
+}
+template <int D, int NG, int FMT = kFmtInt8>
+int tc_desc_r(const AttnParams& p, char* buf, size_t cap) {
+  const int hpr = p.hg < 8 ? p.hg : 8;
+  if (hpr <= 0 || 8 % hpr != 0) return snprintf(buf, cap, "none");
+  switch (8 / hpr) {
+    case 1: return tc_desc<D, NG, 8, 1, FMT>(buf, cap);
+    case 2: return tc_desc<D, NG, 8, 2, FMT>(buf, cap);
+    case 4: return tc_desc<D, NG, 8, 4, FMT>(buf, cap);
+    default: return tc_desc<D, NG, 8, 8, FMT>(buf, cap);
+  }
+}
+}  // namespace
+
+// Names the kernel instances launch_attention(g, p, grid, impl) runs, in
+// launch order, joined by '+'. For introspection (krill_pool_last_kernels).
+void describe_attention(const Geom& g, const AttnParams& p, int grid, int impl, char* buf,
+                        size_t cap) {
+  size_t n = 0;
+  auto put = [&](int w) { n = std::min(cap - 1, n + (size_t)(w > 0 ? w : 0)); };
+  if (cap == 0) return;
+  buf[0] = 0;
+  if (p.sh_grid > 0)
+    put(snprintf(buf + n, cap - n, "%s<%d,%d>+", shared_uses_umma(g, impl) ? "attn_shared_umma_kernel"
+                                                                          : "attn_shared_kernel",
+                 g.D, g.NG));
+  if (grid > 0) {
+    if (impl == 1) put(snprintf(buf + n, cap - n, "attn_cc_kernel<%d,%d,%d>", g.D, g.NG, p.g));
+    else if (g.fmt == kFmtBf16 && g.D == 64) put(tc_desc_r<64, 1, kFmtBf16>(p, buf + n, cap - n));
+    else if (g.fmt == kFmtBf16) put(tc_desc_r<128, 1, kFmtBf16>(p, buf + n, cap - n));
+    else if (g.D == 64) put(tc_desc_r<64, 1>(p, buf + n, cap - n));
+    else if (g.D == 128 && g.NG == 2) put(tc_desc_r<128, 2>(p, buf + n, cap - n));
+    else if (g.D == 128) put(tc_desc_r<128, 1>(p, buf + n, cap - n));
+    else if (g.NG == 4) put(tc_desc_r<256, 4>(p, buf + n, cap - n));
+    else put(tc_desc_r<256, 1>(p, buf + n, cap - n));
+    if (p.split_ctr != nullptr && p.n_split_units > 0 && impl != 1)
+      put(snprintf(buf + n, cap - n, "[merge in kernel]"));
+  }
+  if (attn_needs_combine(p, grid, impl)) put(snprintf(buf + n, cap - n, "+attn_combine_kernel<%d>", g.D));
+  if (n > 0 && buf[n - 1] == '+') buf[--n] = 0;
 }
 
 cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int impl,

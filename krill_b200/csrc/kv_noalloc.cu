@@ -16,8 +16,11 @@
 //
 // The array's name in host code is only a stand-in for the device symbol, not
 // a device address, so the address kernels receive comes from
-// cudaGetSymbolAddress, looked up once per device with that device current
-// (on the first call that uses the device).
+// cudaGetSymbolAddress, looked up once per device with that device current.
+// krill_pool_create does that lookup for its device (noalloc_prepare): under
+// lazy module loading (the CUDA default since 12.2) the lookup is what makes
+// the driver load this module and reserve the scratch, so that reservation
+// happens when a pool is created, not in the middle of decoding.
 #include <mutex>
 
 #include "internal.h"
@@ -41,6 +44,27 @@ alignas(64) uint8_t g_host_packet[KRILL_NOALLOC_SCRATCH_BYTES];  // host side of
 
 }  // namespace
 
+// Looks up both symbols' device addresses for `device` (current), once.
+// Caller holds g_mu.
+static cudaError_t resolve_locked(int device) {
+  if (g_scratch_addr[device] && g_ctr_addr[device]) return cudaSuccess;
+  void* a = nullptr;
+  void* c = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&c, g_noalloc_ctr);
+  if (e != cudaSuccess) return e;
+  if (!a || !c) return cudaErrorInvalidSymbol;
+  g_scratch_addr[device] = a;
+  g_ctr_addr[device] = c;
+  return cudaSuccess;
+}
+
+cudaError_t krill::noalloc_prepare(int device) {
+  if (device < 0 || device >= kMaxDevices) return cudaSuccess;  // no-alloc calls reject it
+  std::lock_guard<std::mutex> lk(g_mu);
+  return resolve_locked(device);
+}
+
 extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int32_t n_seqs,
                                                          const krill_seq_t* seqs,
                                                          int32_t layer_begin, int32_t layer_count,
@@ -49,38 +73,45 @@ extern "C" krill_status_t krill_decode_attention_noalloc(krill_pool_t pool, int3
                                                          void* stream) {
   using namespace krill;
   if (!pool) return set_error(KRILL_ERR_INVALID, "null pool");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Lock order: g_mu, then the pool's mutex, held across planning and launch
+  // so that no other thread changes a planned sequence before its launch.
   std::lock_guard<std::mutex> lk(g_mu);
+  std::lock_guard<std::recursive_mutex> plk(pool_mutex(pool));
   NoAllocPlan np;
   krill_status_t st = noalloc_plan(pool, n_seqs, seqs, layer_begin, layer_count, q, q_dtype, out,
                                    out_dtype, scale, g_host_packet, sizeof(g_host_packet), &np);
   if (st != KRILL_OK) return st;
   if (np.device < 0 || np.device >= kMaxDevices)
     return set_error(KRILL_ERR_INVALID, "device index out of range for the no-alloc scratch");
+  // The metadata is copied from g_host_packet, which the next call rewrites.
+  // A copy recorded into a graph would read it at replay time, so a call on a
+  // stream under capture is refused.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) {
+    cudaError_t e = cudaGetLastError();
+    return set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (cap != cudaStreamCaptureStatusNone)
+    return set_error(KRILL_ERR_INVALID,
+                     "krill_decode_attention_noalloc cannot be called on a stream under capture "
+                     "(its metadata comes from a host buffer that later calls overwrite)");
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != np.device) cudaSetDevice(np.device);
   krill_status_t rc = KRILL_OK;
   do {
-    if (!g_scratch_addr[np.device]) {
-      void* addr = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
-      if (e != cudaSuccess || !addr) {
-        rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
-        break;
-      }
-      g_scratch_addr[np.device] = addr;
-      e = cudaGetSymbolAddress(&addr, g_noalloc_ctr);
-      if (e != cudaSuccess || !addr) {
-        rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
-        break;
-      }
-      g_ctr_addr[np.device] = addr;
+    // normally done by krill_pool_create already
+    cudaError_t e = resolve_locked(np.device);
+    if (e != cudaSuccess) {
+      rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
+      break;
     }
     uint8_t* base = static_cast<uint8_t*>(g_scratch_addr[np.device]);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // Pageable source: the call returns once g_host_packet has been read, so
-    // the next call may overwrite it.
-    cudaError_t e = cudaMemcpyAsync(base, g_host_packet, np.packet_bytes, cudaMemcpyHostToDevice, s);
+    // Pageable source: for a host-to-device cudaMemcpyAsync from pageable
+    // memory the runtime stages the bytes before the call returns, so the
+    // next call may overwrite g_host_packet.
+    e = cudaMemcpyAsync(base, g_host_packet, np.packet_bytes, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) {
       rc = set_error(KRILL_ERR_CUDA, cudaGetErrorString(e));
       break;
