@@ -174,8 +174,12 @@ class ClockSampler:
             for name, val in zip(names, r[5:9]):
                 if val.strip().lower() in ("active", "1"):
                     reasons.add(name)
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         return {"sm_mhz": float(np.median(sm)) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
+                "sm_mhz_min": min(sm) if sm else None,
+                "power_w_median": float(np.median(pw)) if pw else None,
+                "power_w_max": max(pw) if pw else None,
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
@@ -435,6 +439,7 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     v1 = torch.randn((layers, n, hkv, 1, D), generator=gen, device=dev).to(tdt)
     q = torch.randn((layers, n, hq, D), generator=gen, device=dev).to(tdt)
     out = torch.empty((layers, n, hq, D), dtype=tdt, device=dev)
+    stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         kb.decode_step(pool, seqs, 0, k1, v1, q, out, cfg["scale"], stream=stream)
     torch.cuda.synchronize()
@@ -1094,7 +1099,6 @@ def main():
     v_new = kv_randn(torch, cfg, (layers, n, hkv, 1, D), gen, dev).to(tdt)
     q = torch.randn((layers, n, hq, D), generator=gen, device=dev).to(tdt)
     out = torch.empty((layers, n, hq, D), dtype=tdt, device=dev)
-    stream = torch.cuda.current_stream()
 
     def barrier():
         if world > 1:
