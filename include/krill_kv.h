@@ -115,6 +115,13 @@ typedef struct {
                              implementation and split_tokens = 0.           */
   int32_t kv_format;      /* KRILL_KV_INT8 (default) or KRILL_KV_BF16           */
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
+  int32_t wait_timeout_us; /* bound of every device-side wait in this pool's
+                             kernels (a stage copy, a stage release), in
+                             microseconds; 0 -> 100000 (100 ms). A wait that
+                             runs out sets KRILL_DEVICE_ERR_TIMEOUT in the
+                             device error flag and the kernel runs to its end
+                             instead of hanging; that launch's outputs are
+                             then not valid.                                */
 } krill_pool_cfg;
 
 /* ---- errors ------------------------------------------------------------- */
@@ -135,8 +142,17 @@ krill_status_t krill_pool_block_bytes(krill_pool_t pool, int64_t* bytes);
 krill_status_t krill_pool_free_blocks(krill_pool_t pool, int64_t* n);
 krill_status_t krill_pool_block_refcount(krill_pool_t pool, int32_t block, int32_t* refcount);
 /* Device error flag set by a kernel whose bounded wait gave up (and cleared
- * by reading it). */
+ * by reading it): a bit mask of KRILL_DEVICE_ERR_*. Reading it synchronises
+ * with the pool's device. */
+#define KRILL_DEVICE_ERR_TIMEOUT 1
 krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
+/* Testing only (no reference counterpart): while enabled, CTA 0 of each
+ * decode-attention launch on this pool leaves its last stage copy unissued,
+ * so that the stage's consumer reaches its bounded wait with no copy in
+ * flight and the wait runs out (KRILL_DEVICE_ERR_TIMEOUT; that launch's
+ * outputs are not valid). Synchronises with the device. For tests of the
+ * failure path; never enabled otherwise. */
+krill_status_t krill_pool_test_stall(krill_pool_t pool, int32_t enable);
 
 /* Measurement hook (no reference counterpart): while enabled, every attention
  * and append kernel the pool launches is bracketed by a CUDA event pair on its

@@ -25,6 +25,7 @@ DTYPE_F16, DTYPE_BF16, DTYPE_F32, DTYPE_U8 = 0, 1, 2, 3
 QUANT_F32, QUANT_INPUT_DTYPE = 0, 1
 ATTN_TENSOR_CORE, ATTN_CUDA_CORE, ATTN_TENSOR_CORE_SYNC = 0, 1, 2
 KV_INT8, KV_BF16 = 0, 1
+DEVICE_ERR_TIMEOUT = 1
 
 _STATUS_NAMES = {
     1: "KRILL_ERR_INVALID", 2: "KRILL_ERR_OOM", 3: "KRILL_ERR_CUDA", 4: "KRILL_ERR_PEER",
@@ -53,6 +54,7 @@ class PoolCfg(C.Structure):
         ("cascade_min_tokens", C.c_int32),
         ("kv_format", C.c_int32),
         ("num_blocks", C.c_int64),
+        ("wait_timeout_us", C.c_int32),
     ]
 
 
@@ -78,6 +80,7 @@ _SIGS = {
     "krill_pool_free_blocks": (i32, [vp, P_i64]),
     "krill_pool_block_refcount": (i32, [vp, i32, P_i32]),
     "krill_pool_device_error": (i32, [vp, P_i32]),
+    "krill_pool_test_stall": (i32, [vp, i32]),
     "krill_pool_set_profiling": (i32, [vp, i32]),
     "krill_pool_kernel_times": (i32, [vp, C.POINTER(C.c_double), P_i32, C.POINTER(C.c_double), P_i32]),
     "krill_pool_last_plan": (i32, [vp, P_i32, P_i32, P_i64, P_i32]),

@@ -65,10 +65,10 @@ class KVPool:
                  num_blocks: int, group_size: int = 64, window: int = 0, max_append: int = 0,
                  quant_variant: int = L.QUANT_F32, attn_impl: int = L.ATTN_TENSOR_CORE,
                  split_tokens: int = 0, cascade_min_tokens: int = 0, kv_format: int = L.KV_INT8,
-                 device: int = 0):
+                 device: int = 0, wait_timeout_us: int = 0):
         cfg = L.PoolCfg(num_layers, num_kv_heads, num_q_heads, head_dim, group_size, window,
                         max_append, quant_variant, attn_impl, split_tokens, cascade_min_tokens,
-                        kv_format, num_blocks)
+                        kv_format, num_blocks, wait_timeout_us)
         h = C.c_void_p()
         check(L.lib.krill_pool_create(C.byref(cfg), device, C.byref(h)))
         self.handle = h
@@ -111,6 +111,11 @@ class KVPool:
         v = C.c_int32()
         check(L.lib.krill_pool_device_error(self.handle, C.byref(v)))
         return v.value
+
+    def test_stall(self, enable: bool = True):
+        """Testing only: make the next decode launches' bounded wait run out
+        (krill_pool_test_stall)."""
+        check(L.lib.krill_pool_test_stall(self.handle, 1 if enable else 0))
 
     def set_profiling(self, enable: bool = True):
         check(L.lib.krill_pool_set_profiling(self.handle, 1 if enable else 0))

@@ -1117,6 +1117,7 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");
   if (cfg.num_blocks <= 0 || cfg.num_blocks > INT32_MAX)
     return fail(KRILL_ERR_INVALID, "num_blocks out of range");
+  if (cfg.wait_timeout_us < 0) return fail(KRILL_ERR_INVALID, "wait_timeout_us must be >= 0");
   if (cfg.kv_format != KRILL_KV_INT8 && cfg.kv_format != KRILL_KV_BF16)
     return fail(KRILL_ERR_INVALID, "kv_format must be KRILL_KV_INT8 or KRILL_KV_BF16");
   if (cfg.kv_format == KRILL_KV_BF16) {
@@ -1147,8 +1148,12 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     if (e == cudaSuccess) e = cudaMalloc(&p->d_pool, bytes);
     if (e == cudaSuccess) e = cudaMemset(p->d_pool, 0, bytes);
     // [0] error flag, [1] large-scale flag (a stored scale with |s| >= 64)
-    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, 4 * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, kDevWords * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, kDevWords * sizeof(int));
+    if (e == cudaSuccess) {
+      const int us = cfg.wait_timeout_us > 0 ? cfg.wait_timeout_us : kDefaultWaitUs;
+      e = cudaMemcpy(p->d_err + kDevWaitUs, &us, sizeof(int), cudaMemcpyHostToDevice);
+    }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaMallocHost(&p->stage_arena_h, kStageSlots * kStageSliceBytes);
     if (e == cudaSuccess) e = cudaMalloc(&p->stage_arena_d, kStageSlots * kStageSliceBytes);
@@ -1238,6 +1243,17 @@ krill_status_t krill_pool_device_error(krill_pool_t p, int32_t* flag) {
   CUDA_TRY(cudaMemcpy(&v, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (v) CUDA_TRY(cudaMemset(p->d_err, 0, sizeof(int)));
   *flag = v;
+  return KRILL_OK;
+}
+
+krill_status_t krill_pool_test_stall(krill_pool_t p, int32_t enable) {
+  if (!p) return fail(KRILL_ERR_INVALID, "null pool");
+  if (p->host_only) return fail(KRILL_ERR_NO_DEVICE, "test stall on a host-only pool");
+  std::lock_guard<std::recursive_mutex> lk(p->mu);
+  DeviceGuard dg(p->device);
+  const int v = enable ? 1 : 0;
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(p->d_err + kDevTestStall, &v, sizeof(int), cudaMemcpyHostToDevice));
   return KRILL_OK;
 }
 

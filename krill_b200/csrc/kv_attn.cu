@@ -45,7 +45,7 @@ namespace {
 // first waits (bounded) for its own tag, after which the parity wait is exact.
 __device__ bool wait_tag(volatile uint32_t* tag, uint32_t want, volatile int* cta_abort, int* err) {
   if (*tag == want) return true;
-  const uint64_t limit = *cta_abort ? 20000ull : 10000000000ull;
+  const uint64_t limit = wait_limit_ns(err, cta_abort);
   const uint64_t t0 = globaltimer();
   while (*tag != want) {
     if (globaltimer() - t0 > limit) {
@@ -881,6 +881,11 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
       un_n = p.units[item_n.unit];
       blk_n = first_blocks(item_n, un_n);
     }
+    // Testing only (the pool's kDevTestStall word): CTA 0 leaves its last
+    // stage copy unissued, so that the consumer of that stage reaches its
+    // bounded wait with no copy in flight and the wait runs out.
+    const bool stall =
+        blockIdx.x == 0 && reinterpret_cast<volatile const int*>(p.err)[kDevTestStall] != 0;
     uint32_t J = 0;
     for (int it = it0; it < it1; ++it) {
       const AttnItem item = item_n;
@@ -923,6 +928,8 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
                             p.err);
                 const uint32_t full = bar_base + 8 * stage;
                 tags[stage] = Jh;  // released by the arrive below
+                if (stall && !more && rd + 1 == rounds && j + 1 == item.sb_end && hr + 1 == HPR)
+                  continue;
                 mbar_expect_tx(full, SB);
                 bulk_g2s(smem_u32(stages + (size_t)stage * SB), sb_src + (int64_t)hr * p.page_bytes,
                          SB, full);

@@ -98,6 +98,14 @@ __host__ __device__ inline int64_t raw_voff(int D, int T, int t, int d) {
 // Error flag bits written by kernels (pool-owned int, read + cleared by host).
 constexpr int kErrTimeout = 1;
 constexpr int kErrBadArg = 2;
+// The pool's device words (int32): [0] error flag bits, [1] large-scale flag,
+// [2] scratch of the peer fetch, [4] bound of every device-side wait in
+// microseconds, [5] testing only: non-zero makes CTA 0 of the next decode
+// launch leave its last stage copy unissued (its consumer's wait runs out).
+constexpr int kDevWords = 8;
+constexpr int kDevWaitUs = 4;
+constexpr int kDevTestStall = 5;
+constexpr int kDefaultWaitUs = 100000;  // 100 ms
 
 #ifdef __CUDACC__
 __device__ inline float load_in(const void* p, int64_t i, int dtype) {

@@ -33,13 +33,21 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: gives up after ~10 s (20 us once the CTA has already seen a
-// timeout), records the error and returns false. The bound is far above any
-// legitimate wait (a 17 KB copy) yet short enough that a fault ends the
-// launch instead of hanging the GPU.
+// Bound of a device-side wait in ns: the pool's configured limit (its device
+// word kDevWaitUs, next to the error flag `err`), or 20 us once the CTA has
+// already seen a timeout.
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* err, volatile int* cta_abort) {
+  if (*cta_abort) return 20000ull;
+  const int us = reinterpret_cast<volatile const int*>(err)[kDevWaitUs];
+  return (uint64_t)(us > 0 ? us : kDefaultWaitUs) * 1000ull;
+}
+// Bounded wait: gives up after the pool's limit (100 ms by default), records
+// the error and returns false. The bound is far above any legitimate wait (a
+// 17 KB copy) yet short enough that a fault ends the launch instead of
+// hanging the GPU.
 __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t limit = *cta_abort ? 20000ull : 10000000000ull;
+  const uint64_t limit = wait_limit_ns(err, cta_abort);
   const uint64_t t0 = globaltimer();
   for (;;) {
     // the clock is read once per 16 polls: it is off the wake-up path

@@ -460,10 +460,10 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
           if (progressed) {
             spins = 0;
             idle_since = 0;
-          } else if ((++spins & 63u) == 0) {  // bounded: no progress for 10 s (20 us after an abort)
+          } else if ((++spins & 63u) == 0) {  // bounded: no progress within the pool's wait limit
             const uint64_t now = globaltimer();
             if (idle_since == 0) idle_since = now;
-            if (now - idle_since > (*cta_abort ? 20000ull : 10000000000ull)) {
+            if (now - idle_since > wait_limit_ns(p.err, cta_abort)) {
               *cta_abort = 1;
               atomicOr(p.err, kErrTimeout);
               break;

@@ -185,3 +185,13 @@ def test_entry_descriptor_and_ipc_need_devices():
     assert e.value.status == L.KRILL_ERR_NO_DEVICE
     hit.release()
     pc.close()
+
+
+def test_pool_wait_limit_is_validated():
+    """krill_pool_cfg.wait_timeout_us: 0 takes the default, negative is refused."""
+    import krill_b200 as kb
+    kb.KVPool(2, 8, 32, 128, num_blocks=4, device=-1, wait_timeout_us=0).close()
+    kb.KVPool(2, 8, 32, 128, num_blocks=4, device=-1, wait_timeout_us=1000).close()
+    with pytest.raises(L.KrillError) as ei:
+        kb.KVPool(2, 8, 32, 128, num_blocks=4, device=-1, wait_timeout_us=-1)
+    assert ei.value.status == L.KRILL_ERR_INVALID
