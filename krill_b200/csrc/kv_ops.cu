@@ -28,6 +28,43 @@ __device__ inline float bits_to_float(uint16_t b, int dtype) {
 // Quantize EPL elements held by this lane; lanes [k*LPG, (k+1)*LPG) form one
 // group. Returns codes packed little-endian in `codes`, plus the group's f16
 // scale / zero bits.
+// code = trunc(clip(RN(a / s), 0, 255)) for a = rn_in(x - mn) >= 0, bit for bit
+// as with the IEEE divide the reference performs, without a divide per
+// element.
+//   qa = RN(a * rinv), rinv = RN(1 / s), is within 2^-23 (relative: two
+//   roundings of 2^-24) of the exact quotient q, i.e. within 3.1e-5 for
+//   q <= 256. trunc(RN(q)) only changes where q crosses m_k = k - h_k, the
+//   midpoint below an integer k (h_k = half the spacing of the floats just
+//   below k, 2^(E-24) with 2^E the binade of k - 0.5; h_k <= 2^-17 for
+//   k <= 256). So when qa lies at least 1e-4 from the nearest integer k,
+//   trunc(qa) = trunc(RN(q)).
+//   Otherwise RN(q) >= k exactly when q >= m_k (a tie rounds to k, whose
+//   significand is even), i.e. when a - k s + h_k s >= 0. r = fma(-k, s, a)
+//   is exact there (|a - k s| < 1.4e-4 s, a multiple of the smaller of the
+//   two operands' spacings, needs fewer than 24 bits), h_k s is exact (a
+//   power-of-two scaling), and the sign of RN(r + h_k s) is the sign of the
+//   exact sum (no underflow: both are multiples of 2^-75 at these
+//   magnitudes). About 0.2 % (f16) to 2 % (bf16) of N(0,1) elements take
+//   that branch; the group minimum (a = 0) gives 0. Non-finite or
+//   out-of-range quotients fall back to the divide.
+// s24 = s * 2^-24.
+__device__ __forceinline__ uint8_t code_of(float a, float s, float rinv, float s24) {
+  if (a == 0.0f) return 0;
+  const float qa = a * rinv;
+  const float k = rintf(qa);
+  if (!(qa < 512.0f)) {  // NaN / inf / out of range: the divide decides
+    const float n = fminf(fmaxf(__fdiv_rn(a, s), 0.0f), 255.0f);
+    return (uint8_t)__float2int_rz(n);
+  }
+  if (fabsf(qa - k) >= 1e-4f) return (uint8_t)__float2int_rz(fminf(qa, 255.0f));
+  if (k >= 256.0f) return 255;
+  if (k <= 0.0f) return 0;
+  const float r = fmaf(-k, s, a);
+  const float p2 = __uint_as_float(__float_as_uint(k - 0.5f) & 0x7f800000u);
+  const float up = r + s24 * p2;
+  return (uint8_t)(__float2int_rz(k) - (up >= 0.0f ? 0 : 1));
+}
+
 template <int EPL, int LPG>
 __device__ inline void quantize_lane(const float (&x)[EPL], int dtype, int variant,
                                      uint8_t (&codes)[EPL], uint16_t& s16, uint16_t& z16) {
@@ -46,12 +83,18 @@ __device__ inline void quantize_lane(const float (&x)[EPL], int dtype, int varia
   } else {
     scale = fmaxf(round_in(__fdiv_rn(d, 255.0f), dtype), round_in(1e-8f, dtype));
   }
+  if (variant == 0) {
+    const float rinv = __frcp_rn(scale);
+    const float s24 = scale * 5.9604644775390625e-08f;  // 2^-24
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    float n = __fdiv_rn(round_in(x[e] - mn, dtype), scale);
-    if (variant != 0) n = round_in(n, dtype);
-    n = fminf(fmaxf(n, 0.0f), 255.0f);
-    codes[e] = (uint8_t)__float2int_rz(n);
+    for (int e = 0; e < EPL; ++e) codes[e] = code_of(round_in(x[e] - mn, dtype), scale, rinv, s24);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      float n = round_in(__fdiv_rn(round_in(x[e] - mn, dtype), scale), dtype);
+      n = fminf(fmaxf(n, 0.0f), 255.0f);
+      codes[e] = (uint8_t)__float2int_rz(n);
+    }
   }
   s16 = __half_as_ushort(__float2half_rn(scale));
   z16 = __half_as_ushort(__float2half_rn(mn));

@@ -227,3 +227,62 @@ def test_rope_restatement_against_float64():
         ref = np.concatenate([xf[..., :h] * c - xf[..., h:] * s, xf[..., :h] * s + xf[..., h:] * c], -1)
         rel = 2.0 ** (-10 if dtype == F16 else -7)
         assert np.all(np.abs(oracle.bits_to_f64(y, dtype) - ref) <= rel * np.abs(ref) + 1e-6)
+
+
+def _code_by_reciprocal(a, s):
+    """numpy float32 restatement of the append kernels' quotient rule
+    (code_of in kv_ops.cu): trunc(qa) for qa = RN(a * RN(1/s)) at least 1e-4
+    from an integer k; else k or k - 1 by the sign of fma(-k, s, a) + h_k s
+    (the exact test q >= k - h_k). fma(-k, s, a) is exact there; numpy
+    evaluates it in float64, which is exact for these operands."""
+    a = a.astype(np.float32)
+    s = np.broadcast_to(s, a.shape).astype(np.float32)
+    rinv = (np.float32(1.0) / s).astype(np.float32)
+    qa = (a * rinv).astype(np.float32)
+    k = np.rint(qa).astype(np.float32)
+    far = np.abs(qa - k) >= np.float32(1e-4)
+    r = (a.astype(np.float64) - k.astype(np.float64) * s.astype(np.float64)).astype(np.float32)
+    km = (k - np.float32(0.5)).astype(np.float32)
+    p2 = (km.view(np.uint32) & np.uint32(0x7F800000)).view(np.float32)
+    up = (r + (s * np.float32(2.0 ** -24)).astype(np.float32) * p2).astype(np.float32)
+    near_code = np.where(k >= 256, 255, np.where(k <= 0, 0, k.astype(np.int64) - (up < 0)))
+    code = np.where(far, np.trunc(np.minimum(qa, 255)).astype(np.int64), near_code)
+    return np.where(a == 0, 0, code).astype(np.uint8), ~far & (a != 0)
+
+
+def test_quotient_by_reciprocal_matches_the_divide():
+    """The append kernels compute trunc(clip(RN(a / s), 0, 255)) without a
+    divide per element (code_of in kv_ops.cu). Check the rule against the
+    IEEE divide on the quantizer's own operands: f16 and bf16 groups of 64
+    (N(0,1), N(0,8), tiny and wide values, constant groups), a = rn_in(x - mn),
+    s = max(RN(rn_in(mx - mn) / 255), 1e-8), float32 throughout
+    (QuantizedKVCache.swift:185-194)."""
+    rng = np.random.default_rng(123)
+    checked = 0
+    for dtype in (F16, BF16):
+        for sigma in (1.0, 8.0, 1e-3, 300.0):
+            x = rng.standard_normal((40000, 64)).astype(np.float32) * np.float32(sigma)
+            x[:100] = x[:100, :1]  # constant groups
+            xb = oracle.bits_to_f64(to_bits(x, dtype), dtype).astype(np.float32)
+
+            def rn_in(v):
+                return oracle.bits_to_f64(to_bits(v, dtype), dtype).astype(np.float32)
+
+            mn = xb.min(axis=1, keepdims=True)
+            d = rn_in(xb.max(axis=1, keepdims=True) - mn)
+            s = np.maximum(d / np.float32(255.0), np.float32(1e-8)).astype(np.float32)
+            a = rn_in(xb - mn)
+            exact = np.trunc(np.clip(a / s, 0, 255)).astype(np.uint8)
+            got, near = _code_by_reciprocal(a, s)
+            assert np.array_equal(got, exact)
+            if sigma >= 1.0:
+                assert near.mean() < 0.05, near.mean()
+            checked += a.size
+    # every representable quotient near each integer boundary, both sides
+    s = np.float32(1.0) / np.float32(255.0)
+    for k in range(1, 257):
+        q = np.float32(k) * s
+        a = q + (np.arange(-20, 21, dtype=np.float32) * np.spacing(q))
+        got, _ = _code_by_reciprocal(a.astype(np.float32), s)
+        assert np.array_equal(got, np.trunc(np.clip(a / s, 0, 255)).astype(np.uint8))
+    assert checked > 10_000_000
