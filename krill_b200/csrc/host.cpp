@@ -1003,7 +1003,20 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.sh_grid = sh_grid;
     ap.n_pslots = n_pslots;
   }
-  if (pre_bytes) {
+  // A decode step's one-token append runs inside the decode kernel (one
+  // launch per step) where that kernel carries it: int8 pools, tensor-core
+  // decode kernel, head_dim <= 128. Every unit's new token lies in one of
+  // its decode items (shared-prefix parts end below each member's length).
+  const bool fuse = pre_bytes && pre->n_new == 1 && grid > 0 && g.fmt == kFmtInt8 &&
+                    p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE && fused_append_supported(g.D);
+  if (fuse) {
+    ap.app_dst = reinterpret_cast<const AppendDst*>(slot->d + pre_off);
+    ap.app_k = pre->k;
+    ap.app_v = pre->v;
+    ap.app_dtype = pre->dtype;
+    ap.app_variant = g.quant_variant;
+    ap.app_large = p->d_err + 1;
+  } else if (pre_bytes) {
     const krill_status_t st =
         launch_deferred_append(p, *pre, reinterpret_cast<const AppendDst*>(slot->d + pre_off), stream);
     if (st != KRILL_OK) {
@@ -1015,6 +1028,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.pdl = (sh_grid == 0 && grid > 0 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE) ? 1 : 0;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
+  if (fuse) pre->pending = false;  // the decode kernel wrote the appended tokens
   p->kernels += (grid > 0 ? 1 : 0) + (attn_needs_combine(ap, grid, p->cfg.attn_impl) ? 1 : 0) +
                 (sh_grid > 0 ? 1 : 0);
   TRY(stage_release(slot, stream));
