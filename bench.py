@@ -1064,7 +1064,7 @@ def main():
     mine = [lengths_all[i] for i in parts[rank]]
     layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
-    total_steps = args.warmup + args.steps * (REPEATS + 2) + 4
+    total_steps = args.warmup + args.steps + 4  # repetitions rewind to the same lengths
     # at N > 1 the pool also holds one imported prefix entry (4096 tokens)
     blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4 + (PEER_PREFIX // 256 if world > 1 else 0)
     raw = args.kv == "bf16"
@@ -1164,14 +1164,24 @@ def main():
     # same number of steps again with the per-kernel events for the roofline
     # the K-step region is repeated REPEATS times, each the max over ranks;
     # `value` uses the median repetition
+    # every repetition (and the profiled pass) starts from the same cache
+    # lengths: the sequences are truncated back between them, outside the
+    # timed region (the workload is K steps from the configured lengths)
+    def rewind():
+        torch.cuda.synchronize()
+        for s_, L_ in zip(seqs, len_before):
+            s_.truncate(L_)
+
     reps = []
     with ClockSampler(local_rank) as clocks:
         for _ in range(REPEATS):
             total_ms, launches, _ = timed_steps(False)
             reps.append(max_over_ranks(total_ms / args.steps))
-    plan, kernels = pool.last_plan(), pool.last_kernels()
+            plan, kernels = pool.last_plan(), pool.last_kernels()
+            rewind()
     barrier()
     _, _, (attn_total, attn_n, app_total, app_n) = timed_steps(True)
+    rewind()
     barrier()
     attn_ms = [attn_total / max(1, attn_n)]
     app_ms = [app_total / max(1, app_n)]
@@ -1182,10 +1192,9 @@ def main():
     # algorithmic bytes: lengths after each step's append (the profiled pass
     # runs after the value pass, args.steps tokens further on)
     attn_bytes, step_b = 0, 0
-    mid = (REPEATS // 2) * args.steps  # tokens appended before the median repetition
-    for i in range(args.steps):
-        step_b += step_bytes([L + mid + i + 1 for L in len_before], cfg, raw)[1]
-        attn_bytes += step_bytes([L + REPEATS * args.steps + i + 1 for L in len_before], cfg, raw)[0]
+    for i in range(args.steps):  # every repetition runs from len_before
+        step_b += step_bytes([L + i + 1 for L in len_before], cfg, raw)[1]
+        attn_bytes += step_bytes([L + i + 1 for L in len_before], cfg, raw)[0]
     attn_bytes /= args.steps
     step_b /= args.steps
     attn_mean_ms = float(np.mean(attn_ms))
@@ -1270,6 +1279,10 @@ def main():
             "plan": {"pieces_subblocks": plan[0], "kv_heads_per_item": plan[1], "items": plan[2],
                      "ctas": plan[3], "kernels": kernels},
             "ms_per_step_repeats": reps,
+            "timing": (f"{REPEATS} repetitions of the {args.steps}-step region from the same cache "
+                       "lengths (rewound between them, untimed), each the max over ranks; value and "
+                       "ms_per_step from the median one (sustained load: later repetitions may run "
+                       "at power-capped clocks, see clocks)"),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": None if raw else profiled_traffic(args.config, attn_bytes),

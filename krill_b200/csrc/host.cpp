@@ -995,6 +995,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   if (++p->attn_epoch == 0) p->attn_epoch = 1;
   ap.epoch = p->attn_epoch;
   ap.err = p->d_err;
+  ap.wait_us = p->cfg.wait_timeout_us;
   ap.large_scale = p->d_err + 1;
   if (sh_grid > 0) {
     ap.sh_items = reinterpret_cast<const ShItem*>(slot->d + sh_off);
@@ -1003,20 +1004,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.sh_grid = sh_grid;
     ap.n_pslots = n_pslots;
   }
-  // A decode step's one-token append runs inside the decode kernel (one
-  // launch per step) where that kernel carries it: int8 pools, tensor-core
-  // decode kernel, head_dim <= 128. Every unit's new token lies in one of
-  // its decode items (shared-prefix parts end below each member's length).
-  const bool fuse = pre_bytes && pre->n_new == 1 && grid > 0 && g.fmt == kFmtInt8 &&
-                    p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE && fused_append_supported(g.D);
-  if (fuse) {
-    ap.app_dst = reinterpret_cast<const AppendDst*>(slot->d + pre_off);
-    ap.app_k = pre->k;
-    ap.app_v = pre->v;
-    ap.app_dtype = pre->dtype;
-    ap.app_variant = g.quant_variant;
-    ap.app_large = p->d_err + 1;
-  } else if (pre_bytes) {
+  if (pre_bytes) {
     const krill_status_t st =
         launch_deferred_append(p, *pre, reinterpret_cast<const AppendDst*>(slot->d + pre_off), stream);
     if (st != KRILL_OK) {
@@ -1028,7 +1016,6 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.pdl = (sh_grid == 0 && grid > 0 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE) ? 1 : 0;
   }
   CUDA_TRY(timed_launch(p, 0, stream, [&] { return launch_attention(g, ap, grid, p->cfg.attn_impl, stream); }));
-  if (fuse) pre->pending = false;  // the decode kernel wrote the appended tokens
   p->kernels += (grid > 0 ? 1 : 0) + (attn_needs_combine(ap, grid, p->cfg.attn_impl) ? 1 : 0) +
                 (sh_grid > 0 ? 1 : 0);
   TRY(stage_release(slot, stream));
@@ -1164,10 +1151,6 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     // [0] error flag, [1] large-scale flag (a stored scale with |s| >= 64)
     if (e == cudaSuccess) e = cudaMalloc(&p->d_err, kDevWords * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, kDevWords * sizeof(int));
-    if (e == cudaSuccess) {
-      const int us = cfg.wait_timeout_us > 0 ? cfg.wait_timeout_us : kDefaultWaitUs;
-      e = cudaMemcpy(p->d_err + kDevWaitUs, &us, sizeof(int), cudaMemcpyHostToDevice);
-    }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaMallocHost(&p->stage_arena_h, kStageSlots * kStageSliceBytes);
     if (e == cudaSuccess) e = cudaMalloc(&p->stage_arena_d, kStageSlots * kStageSliceBytes);
@@ -3092,6 +3075,7 @@ krill_status_t noalloc_plan(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.out_dtype = out_dtype;
   ap.scale_log2 = scale * 1.4426950408889634f;
   ap.err = p->d_err;
+  ap.wait_us = p->cfg.wait_timeout_us;
   ap.large_scale = p->d_err + 1;
   o.geom = g;
   o.grid = grid;

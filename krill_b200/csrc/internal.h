@@ -118,6 +118,7 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   float* partials;   // [splits * Hkv][16 + 8*D]
   int* err;
+  int wait_us;       // bound of every device-side wait, microseconds (0: default)
   const int* large_scale;  // non-zero once the pool holds a scale with |s| >= 64
   // cascade items (sh_grid = 0: none)
   const ShItem* sh_items;
@@ -128,15 +129,6 @@ struct AttnParams {
   // host side only: launch the decode kernel as the programmatic dependent of
   // the append kernel launched just before it on the stream
   int pdl;
-  // Fused append (decode steps): when app_dst is set, the decode kernel
-  // quantizes and writes each unit's one new token itself (input row
-  // (qo_row * Hkv + h) of app_k / app_v, destination app_dst[qo_row]) before
-  // it copies the sub-block that holds it: one launch per step.
-  const AppendDst* app_dst;
-  const void* app_k;
-  const void* app_v;
-  int app_dtype, app_variant;
-  int* app_large;  // the pool's large-scale flag, raised for a scale >= 64
 };
 
 // Rotary table for the fused RoPE append: cos / sin [rows][D/2] f32 (device),
@@ -221,9 +213,6 @@ inline int attn_warps(int /*D*/) { return 8; }
 // Resident CTAs per SM the planner targets: one persistent tensor-core CTA
 // (it fills the shared memory), four of the lighter CUDA-core variant.
 inline int attn_ctas_per_sm(int impl) { return impl == 1 ? 4 : 1; }
-// Head dims whose decode kernel can carry a decode step's append (the fused
-// append; AttnParams::app_dst).
-__host__ __device__ constexpr bool fused_append_supported(int D) { return D <= 128; }
 // Floats per partial record for head_dim D.
 __host__ __device__ inline int64_t partial_floats(int D) { return 16 + 8 * (int64_t)D; }
 

@@ -34,7 +34,6 @@
 #include <cstdio>
 
 #include "kv_device.cuh"
-#include "kv_quant.cuh"
 
 namespace krill {
 namespace {
@@ -46,10 +45,10 @@ namespace {
 // first waits (bounded) for its own tag, after which the parity wait is exact.
 __device__ bool wait_tag(volatile uint32_t* tag, uint32_t want, volatile int* cta_abort, int* err) {
   if (*tag == want) return true;
-  const uint64_t limit = wait_limit_ns(err, cta_abort);
+  const uint32_t limit = wait_limit_units(cta_abort);
   const uint64_t t0 = globaltimer();
   while (*tag != want) {
-    if (globaltimer() - t0 > limit) {
+    if (((globaltimer() - t0) >> 10) > limit) {
       *cta_abort = 1;
       atomicOr(err, kErrTimeout);
       return false;
@@ -58,25 +57,19 @@ __device__ bool wait_tag(volatile uint32_t* tag, uint32_t want, volatile int* ct
   return true;
 }
 
-// Head dims whose decode kernel carries the fused append (at head_dim 256 the
-// consumers' registers have no room for it; those pools append separately).
-template <int D>
-constexpr bool kFusedAppend = fused_append_supported(D);
-
-// Bounded wait for a shared-memory count to reach `want` (the fused append's
-// progress); on timeout raises the error flag and returns.
-__device__ __forceinline__ void wait_count(volatile uint32_t* cnt, uint32_t want, volatile int* cta_abort, int* err) {
-  if (*cnt >= want) return;
-  const uint64_t limit = wait_limit_ns(err, cta_abort);
+// Bounded wait for a shared-memory word to reach `want`; on timeout raises the
+// error flag and returns.
+__device__ __forceinline__ void wait_count(volatile uint32_t* cnt, uint32_t want, volatile int* cta_abort,
+                                           int* err) {
+  const uint32_t limit = wait_limit_units(cta_abort);
   const uint64_t t0 = globaltimer();
   while (*cnt < want) {
-    if (globaltimer() - t0 > limit) {
+    if (((globaltimer() - t0) >> 10) > limit) {
       *cta_abort = 1;
       atomicOr(err, kErrTimeout);
       return;
     }
   }
-  __threadfence_block();
 }
 
 __device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
@@ -85,42 +78,20 @@ __device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
   return y;
 }
 
-// True when token t's K and V scales in the staged sub-block are all below
-// 64 in magnitude (finite), i.e. the one-fma dequantization is exact for it.
-// Warp-uniform (every lane reads the same words).
+// True when every K and V scale of the sub-block has |s| < 64 (and is finite),
+// i.e. the fast dequant is exact for the whole sub-block. Warp-uniform.
 template <int D, int NG>
-__device__ __forceinline__ bool token_scales_small(const uint8_t* __restrict__ sb, int t) {
+__device__ __forceinline__ bool scales_small(const uint8_t* __restrict__ sb, int lane) {
   using SG = SubGeom<D, NG>;
+  constexpr int BYTES = NG * SG::T * 2;  // one [NG][T] f16 array
   bool big = false;
-#pragma unroll
-  for (int gi = 0; gi < NG; ++gi) {
-    const uint16_t ks = *reinterpret_cast<const uint16_t*>(sb + SG::meta(0, gi, t));
-    const uint16_t vs = *reinterpret_cast<const uint16_t*>(sb + SG::meta(2, gi, t));
-    big |= (ks & 0x7fffu) >= 0x5400u || (vs & 0x7fffu) >= 0x5400u;
+  for (int off = lane * 16; off < 2 * BYTES; off += 512) {
+    const int a = off / BYTES;  // 0: K scales, 1: V scales (meta array 2)
+    const uint4 w = *reinterpret_cast<const uint4*>(sb + SG::META + a * 2 * BYTES + (off - a * BYTES));
+    big |= (__vcmpgeu2(w.x & 0x7fff7fffu, 0x54005400u) | __vcmpgeu2(w.y & 0x7fff7fffu, 0x54005400u) |
+            __vcmpgeu2(w.z & 0x7fff7fffu, 0x54005400u) | __vcmpgeu2(w.w & 0x7fff7fffu, 0x54005400u)) != 0;
   }
-  return !big;
-}
-
-// Copies one token's bytes (K row, V column, its scales and zeros) of head h
-// from the pool sub-block at gsb into the staged copy sb, through L2: the
-// token the fused append has just written.
-template <int D, int NG>
-__device__ __forceinline__ void patch_token(uint8_t* __restrict__ sb, const uint8_t* __restrict__ gsb,
-                                            int t, int lane) {
-  using SG = SubGeom<D, NG>;
-#pragma unroll
-  for (int w = lane; w < D / 4; w += 32)
-    *reinterpret_cast<uint32_t*>(sb + t * D + 4 * w) =
-        __ldcg(reinterpret_cast<const unsigned int*>(gsb + t * D) + w);
-#pragma unroll
-  for (int d = lane; d < D; d += 32) {
-    const int off = SG::VOFF + d * SG::T + t;
-    sb[off] = (uint8_t)__ldcg(reinterpret_cast<const unsigned char*>(gsb) + off);
-  }
-  if (lane < 4 * NG) {
-    const int off = SG::meta(lane / NG, lane % NG, t);
-    *reinterpret_cast<uint16_t*>(sb + off) = __ldcg(reinterpret_cast<const unsigned short*>(gsb + off));
-  }
+  return !__any_sync(0xffffffffu, big);
 }
 
 template <int D>
@@ -747,7 +718,6 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
   constexpr int SB = SM::SB;
   constexpr int HPR = NCW / R;
-  volatile uint32_t* app_done = reinterpret_cast<volatile uint32_t*>(smem + SM::MISC_OFF + 4);
   const int hr = warp / R, rr = warp % R;
   TCState<D> st;
   uint32_t J = 0;
@@ -801,30 +771,10 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
         const int pos0 = j * T;
         const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
         const uint8_t* sbp = stages + (size_t)stage * SB;
-        if constexpr (FMT == kFmtBf16) {
+        if constexpr (FMT == kFmtBf16)
           tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-        } else {
-          // The one-fma dequantization chosen at launch start is exact for
-          // scales below 64; a token appended by this very launch (fused
-          // append) may carry a larger one, so its sub-block is checked.
-          bool exact = false;
-          if (kFusedAppend<D> && p.app_dst != nullptr && un.t_hi - 1 >= pos0 && un.t_hi - 1 < pos0 + T) {
-            // the unit's new token, written by this launch's append warp
-            if (lane == 0) wait_count(app_done, (uint32_t)(it - it0 + 1), cta_abort, p.err);
-            __syncwarp();
-            const AppendDst ad = p.app_dst[un.qo_row];
-            const int slot = ad.pos & (kBlockTokens - 1);
-            const uint8_t* gsb = p.pool + (((int64_t)ad.block * p.L + un.layer) * p.Hkv + h) * p.page_bytes +
-                                 (int64_t)(slot / T) * p.sb_bytes;
-            patch_token<D, NG>(const_cast<uint8_t*>(sbp), gsb, slot % T, lane);
-            __syncwarp();
-            if constexpr (FAST) exact = !token_scales_small<D, NG>(sbp, slot % T);
-          }
-          if (exact)
-            tc_subblock<D, NG, false>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-          else
-            tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
-        }
+        else
+          tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
         if (pf < 2) prefetch_step();
@@ -884,57 +834,6 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   }
 }
 
-// Fused append of a decode step, run by one producer-group warp: for each of
-// the CTA's items, in order, that holds its unit's newest token, quantize that
-// token's K and V rows for the item's heads (the per-token core of the append
-// kernels, so the same bits) and write them into the pool, then publish the
-// count of items done in *done. The bulk copy of the sub-block holding the new
-// token may run before or after these writes; the consumer of that sub-block
-// waits for the count and copies the token's bytes from the pool into its
-// staged copy (patch_token), so it attends the new token either way.
-template <int D, int NG>
-__device__ __noinline__ void fused_append(const AttnParams& p, int it0, int it1, int lane,
-                                          volatile uint32_t* done) {
-  constexpr int T = SubGeom<D, NG>::T, EPL = D / 32, LPG = (D / NG) / EPL;
-  bool large = false;
-  for (int it = it0; it < it1; ++it) {
-    const AttnItem item = p.items[it];
-    const AttnUnit un = p.units[item.unit];
-    const int tail = (un.t_hi - 1) / T;
-    if (item.sb_begin <= tail && tail < item.sb_end) {
-      const AppendDst d = p.app_dst[un.qo_row];
-      const int slot = d.pos & (kBlockTokens - 1), t = slot % T;
-      for (int h = item.h0; h < item.h0 + p.hg; ++h) {
-        uint8_t* sb = const_cast<uint8_t*>(p.pool) +
-                      (((int64_t)d.block * p.L + un.layer) * p.Hkv + h) * p.page_bytes +
-                      (int64_t)(slot / T) * p.sb_bytes;
-        uint8_t ck[EPL], cv[EPL];
-        uint16_t sk, zk, sv, zv;
-        quant_token<EPL, LPG>(p.app_k, p.app_v, ((int64_t)un.qo_row * p.Hkv + h) * D, d.pos, D, lane,
-                              p.app_dtype, p.app_variant, RopeTable{nullptr, nullptr, 0}, ck, cv, sk,
-                              zk, sv, zv);
-        store_kcodes<EPL>(sb, D, t, lane, ck);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) sb[sb_vcode(D, t, lane * EPL + e)] = cv[e];
-        if ((lane % LPG) == 0) {
-          const int gi = lane / LPG;
-          *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 0, gi, t)) = sk;
-          *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 1, gi, t)) = zk;
-          *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 2, gi, t)) = sv;
-          *reinterpret_cast<uint16_t*>(sb + sb_meta(D, NG, 3, gi, t)) = zv;
-          large |= (sk & 0x7fffu) >= 0x5400u || (sv & 0x7fffu) >= 0x5400u;
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) {
-      __threadfence_block();
-      *done = (uint32_t)(it - it0 + 1);
-    }
-  }
-  if (large) atomicOr(p.app_large, 1);
-}
-
 template <int D, int NG, int NCW, int R, int NSTAGE, int FMT>
 __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
   static_assert(NCW == 8, "two consumer warpgroups");
@@ -946,7 +845,7 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
   const uint32_t bar_base = smem_u32(smem + SM::BAR_OFF);
   volatile int* cta_abort = reinterpret_cast<volatile int*>(smem + SM::MISC_OFF);
   volatile uint32_t* tags = reinterpret_cast<volatile uint32_t*>(smem + SM::TAG_OFF);
-  volatile uint32_t* app_done = reinterpret_cast<volatile uint32_t*>(smem + SM::MISC_OFF + 4);
+  volatile uint32_t* stall_word = reinterpret_cast<volatile uint32_t*>(smem + SM::MISC_OFF + 8);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -956,8 +855,8 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
       mbar_init(bar_base + 8 * (NSTAGE + s), 1);  // empty: the consuming warp
     }
     for (int s = 0; s < NSTAGE; ++s) tags[s] = 0xffffffffu;
-    *cta_abort = 0;
-    *app_done = 0;
+    init_wait_state(cta_abort, p.wait_us);
+    *stall_word = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -973,12 +872,12 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
 
   if (warp >= NCW) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
-    if constexpr (FMT == kFmtInt8 && kFusedAppend<D>) {
-      if (warp == NCW + 1 && p.app_dst != nullptr) {
-        fused_append<D, NG>(p, it0, it1, lane, app_done);
-        return;
-      }
-    }
+    // Testing only (the pool's kDevTestStall word): an otherwise idle warp of
+    // CTA 0 waits for a word that nothing raises, so that its bounded wait
+    // runs out (error flag set; the launch still ends, its outputs not valid).
+    if (warp == NCW + 1 && blockIdx.x == 0 && lane == 0 &&
+        reinterpret_cast<volatile const int*>(p.err)[kDevTestStall] != 0)
+      wait_count(stall_word, 1u, cta_abort, p.err);
     if (warp != NCW) return;
     // ---------------- producer ----------------
     // The lanes fetch an item's block ids together (one coalesced load per 32
@@ -1005,11 +904,6 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
       un_n = p.units[item_n.unit];
       blk_n = first_blocks(item_n, un_n);
     }
-    // Testing only (the pool's kDevTestStall word): CTA 0 leaves its last
-    // stage copy unissued, so that the consumer of that stage reaches its
-    // bounded wait with no copy in flight and the wait runs out.
-    const bool stall =
-        blockIdx.x == 0 && reinterpret_cast<volatile const int*>(p.err)[kDevTestStall] != 0;
     uint32_t J = 0;
     for (int it = it0; it < it1; ++it) {
       const AttnItem item = item_n;
@@ -1052,8 +946,6 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
                             p.err);
                 const uint32_t full = bar_base + 8 * stage;
                 tags[stage] = Jh;  // released by the arrive below
-                if (stall && !more && rd + 1 == rounds && j + 1 == item.sb_end && hr + 1 == HPR)
-                  continue;
                 mbar_expect_tx(full, SB);
                 bulk_g2s(smem_u32(stages + (size_t)stage * SB), sb_src + (int64_t)hr * p.page_bytes,
                          SB, full);

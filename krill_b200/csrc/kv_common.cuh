@@ -99,11 +99,9 @@ __host__ __device__ inline int64_t raw_voff(int D, int T, int t, int d) {
 constexpr int kErrTimeout = 1;
 constexpr int kErrBadArg = 2;
 // The pool's device words (int32): [0] error flag bits, [1] large-scale flag,
-// [2] scratch of the peer fetch, [4] bound of every device-side wait in
-// microseconds, [5] testing only: non-zero makes CTA 0 of the next decode
-// launch leave its last stage copy unissued (its consumer's wait runs out).
+// [2] scratch of the peer fetch, [5] testing only: non-zero makes a wait of
+// CTA 0 in the next decode launches run out.
 constexpr int kDevWords = 8;
-constexpr int kDevWaitUs = 4;
 constexpr int kDevTestStall = 5;
 constexpr int kDefaultWaitUs = 100000;  // 100 ms
 

@@ -33,13 +33,18 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Bound of a device-side wait in ns: the pool's configured limit (its device
-// word kDevWaitUs, next to the error flag `err`), or 20 us once the CTA has
-// already seen a timeout.
-__device__ __forceinline__ uint64_t wait_limit_ns(const int* err, volatile int* cta_abort) {
-  if (*cta_abort) return 20000ull;
-  const int us = reinterpret_cast<volatile const int*>(err)[kDevWaitUs];
-  return (uint64_t)(us > 0 ? us : kDefaultWaitUs) * 1000ull;
+// Every kernel with bounded waits keeps two shared-memory words: cta_abort[0]
+// (set once a wait of the CTA ran out) and cta_abort[1], the pool's wait
+// limit in microseconds (a launch parameter), set when the CTA starts.
+__device__ __forceinline__ void init_wait_state(volatile int* cta_abort, int wait_us) {
+  cta_abort[0] = 0;
+  cta_abort[1] = wait_us > 0 ? wait_us : kDefaultWaitUs;
+}
+// Bound of a device-side wait in units of 1,024 ns (elapsed globaltimer ns
+// >> 10): the pool's limit, or about 20 us once the CTA has already seen a
+// timeout.
+__device__ __forceinline__ uint32_t wait_limit_units(volatile int* cta_abort) {
+  return cta_abort[0] ? 20u : (uint32_t)cta_abort[1];
 }
 // Bounded wait: gives up after the pool's limit (100 ms by default), records
 // the error and returns false. The bound is far above any legitimate wait (a
@@ -47,13 +52,13 @@ __device__ __forceinline__ uint64_t wait_limit_ns(const int* err, volatile int* 
 // hanging the GPU.
 __device__ bool mbar_wait(uint32_t bar, uint32_t phase, volatile int* cta_abort, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t limit = wait_limit_ns(err, cta_abort);
+  const uint32_t limit = wait_limit_units(cta_abort);
   const uint64_t t0 = globaltimer();
   for (;;) {
     // the clock is read once per 16 polls: it is off the wake-up path
     for (int k = 0; k < 16; ++k)
       if (mbar_try_wait(bar, phase)) return true;
-    if (globaltimer() - t0 > limit) {
+    if (((globaltimer() - t0) >> 10) > limit) {
       *cta_abort = 1;
       atomicOr(err, kErrTimeout);
       return false;

@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(384, 1) attn_shared_kernel(AttnParams p) {
       mbar_init(bar_ff + 8 * s, kShDeqWarps);
       mbar_init(bar_fe + 8 * s, 8);            // each consumer warp
     }
-    *cta_abort = 0;
+    init_wait_state(cta_abort, p.wait_us);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();

@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       mbar_init(bar(SM::B_QF + h), 4);
     }
     mbar_init(bar(SM::B_FIN), 1);
-    *cta_abort = 0;
+    init_wait_state(cta_abort, p.wait_us);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 8) {
@@ -395,13 +395,21 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
       uint32_t cnt0 = 0, cnt1 = 0;  // tiles processed by each half
       uint32_t qn0 = 0, qn1 = 0;    // items processed by each half
       uint32_t J = 0;
+      // Shared-memory descriptors built once: per K/V stage and per half. An
+      // operand at a fixed byte offset o from a tile's start is its tile
+      // descriptor plus o / 16 (the start-address field; every address here
+      // is below 256 KB, so the addition never carries out of the field).
+      const uint64_t dK0 = sw128_desc(sbase + SM::KV_OFF);
+      const uint64_t dV0 = sw128_desc(sbase + SM::KV_OFF + SM::K_BYTES);
+      const uint64_t dQ0 = sw128_desc(sbase + SM::Q_OFF);
+      const uint64_t dP0 = sw128_desc(sbase + SM::P_OFF);
       // O_h += P_h · V of K/V stage st (P_h ready: PF observed by the caller)
       auto issue_pv = [&](int h, uint32_t st, bool first) {
-        const uint32_t vb = sbase + SM::KV_OFF + st * SM::KV_STAGE + SM::K_BYTES;
-        const uint32_t pb = sbase + SM::P_OFF + h * SM::P_BYTES;
+        const uint64_t pd = dP0 + (uint64_t)(h * (SM::P_BYTES >> 4));
+        const uint64_t vd = dV0 + (uint64_t)(st * (SM::KV_STAGE >> 4));
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_f16(tmem + 256u * h, sw128_desc(pb + 32 * ks), sw128_desc(vb + 32 * ks), idO,
+          umma_f16(tmem + 256u * h, pd + (uint64_t)(2 * ks), vd + (uint64_t)(2 * ks), idO,
                    (!first || ks > 0) ? 1u : 0u);
         umma_commit(bar(SM::B_PD + h));  // O_h updated, P_h free
       };
@@ -429,17 +437,17 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
             const uint32_t Jc = J + js, st = Jc % kUmNF;
             if (mbar_try_wait(bar(SM::B_KF + st), (Jc / kUmNF) & 1)) {
               tc_fence_after();
-              const uint32_t kb = sbase + SM::KV_OFF + st * SM::KV_STAGE;
+              const uint64_t kd = dK0 + (uint64_t)(st * (SM::KV_STAGE >> 4));
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 if (h >= nh) break;
                 const uint32_t c = (h == 0 ? cnt0 : cnt1) + js;
-                const uint32_t qb = sbase + SM::Q_OFF + h * SM::QH_BYTES;
+                const uint64_t qd = dQ0 + (uint64_t)(h * (SM::QH_BYTES >> 4));
                 const uint32_t sc = tmem + 256u * h + kUmS0 + 64u * (c & 1);
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks)
-                  umma_f16(sc, sw128_desc(qb + (ks >> 2) * (128 * 128) + 32 * (ks & 3)),
-                           sw128_desc(kb + (ks >> 2) * (64 * 128) + 32 * (ks & 3)), idS,
+                  umma_f16(sc, qd + (uint64_t)(((ks >> 2) * (128 * 128) + 32 * (ks & 3)) >> 4),
+                           kd + (uint64_t)(((ks >> 2) * (64 * 128) + 32 * (ks & 3)) >> 4), idS,
                            ks > 0 ? 1u : 0u);
                 umma_commit(bar(SM::B_SF + 2 * h + (c & 1)));
               }
@@ -463,7 +471,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) attn_shared_umma_kernel(AttnPar
           } else if ((++spins & 63u) == 0) {  // bounded: no progress within the pool's wait limit
             const uint64_t now = globaltimer();
             if (idle_since == 0) idle_since = now;
-            if (now - idle_since > wait_limit_ns(p.err, cta_abort)) {
+            if (((now - idle_since) >> 10) > wait_limit_units(cta_abort)) {
               *cta_abort = 1;
               atomicOr(p.err, kErrTimeout);
               break;
