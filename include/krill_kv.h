@@ -117,7 +117,8 @@ typedef struct {
   int64_t num_blocks;     /* pool capacity in 256-token blocks                  */
   int32_t wait_timeout_us; /* bound of every device-side wait in this pool's
                              kernels (a stage copy, a stage release), in
-                             microseconds; 0 -> 100000 (100 ms). A wait that
+                             microseconds (counted in 1.024 us units of the
+                             GPU timer); 0 -> 100000 (about 0.1 s). A wait that
                              runs out sets KRILL_DEVICE_ERR_TIMEOUT in the
                              device error flag and the kernel runs to its end
                              instead of hanging; that launch's outputs are
@@ -146,12 +147,12 @@ krill_status_t krill_pool_block_refcount(krill_pool_t pool, int32_t block, int32
  * with the pool's device. */
 #define KRILL_DEVICE_ERR_TIMEOUT 1
 krill_status_t krill_pool_device_error(krill_pool_t pool, int32_t* flag);
-/* Testing only (no reference counterpart): while enabled, CTA 0 of each
- * decode-attention launch on this pool leaves its last stage copy unissued,
- * so that the stage's consumer reaches its bounded wait with no copy in
- * flight and the wait runs out (KRILL_DEVICE_ERR_TIMEOUT; that launch's
- * outputs are not valid). Synchronises with the device. For tests of the
- * failure path; never enabled otherwise. */
+/* Testing only (no reference counterpart): while enabled, an otherwise idle
+ * warp of CTA 0 of each decode-attention launch on this pool waits for a
+ * shared-memory word that nothing sets, so that its bounded wait runs out
+ * (KRILL_DEVICE_ERR_TIMEOUT; that launch's outputs are not valid). Nothing
+ * faults or hangs. Synchronises with the device. For tests of the failure
+ * path; never enabled otherwise. */
 krill_status_t krill_pool_test_stall(krill_pool_t pool, int32_t enable);
 
 /* Measurement hook (no reference counterpart): while enabled, every attention

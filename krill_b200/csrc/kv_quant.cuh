@@ -1,7 +1,6 @@
-// kv_quant.cuh — the per-token quantizer core shared by the append kernels
-// (kv_ops.cu) and the decode kernel's fused append (kv_attn.cu): a warp
-// quantizes one token's K and V rows, lanes [k*LPG, (k+1)*LPG) holding one
-// group of EPL elements each. Reference: QuantizedKVCache.quantizePerHead
+// kv_quant.cuh — the per-token quantizer core of the warp-per-token append
+// kernels (kv_ops.cu): a warp quantizes one token's K and V rows, lanes
+// [k*LPG, (k+1)*LPG) holding one group of EPL elements each. Reference: QuantizedKVCache.quantizePerHead
 // (Sources/KrillCache/QuantizedKVCache.swift:181-197), applied per
 // `group_size` slice of head_dim, every rounding step the reference's.
 #pragma once

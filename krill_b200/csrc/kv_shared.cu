@@ -25,8 +25,8 @@
 //     stays below 256 and the final O / l is unchanged.
 // Each item's result is one fp32 partial record per member (record `slot` of
 // the member's unit); attn_combine_kernel merges it with the suffix pieces.
-// Every wait is bounded (10 s, then 20 us after the first timeout) and sets
-// the pool's error flag instead of hanging.
+// Every wait is bounded (the pool's wait_timeout_us, then 20 us after the
+// first timeout) and sets the pool's error flag instead of hanging.
 #include <atomic>
 
 #include "kv_device.cuh"

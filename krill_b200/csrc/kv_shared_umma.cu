@@ -24,8 +24,8 @@
 //     rare O rescale is a tcgen05.ld / st round trip after the previous P·V
 //     has completed. At the end of an item they read O and write the fp32
 //     partial records.
-// Every wait is bounded (10 s, then 20 us after the first timeout) and sets
-// the pool's error flag; the tensor memory is released on every path.
+// Every wait is bounded (the pool's wait_timeout_us, then 20 us after the
+// first timeout) and sets the pool's error flag; the tensor memory is released on every path.
 #include <atomic>
 
 #include "kv_device.cuh"

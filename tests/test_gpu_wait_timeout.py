@@ -2,10 +2,10 @@
 status instead of hanging the GPU.
 
 The pool is created with a 1 ms wait limit and its test switch
-(krill_pool_test_stall) makes CTA 0 of the next decode launch leave its last
-stage copy unissued: that stage's consumer waits, with no copy in flight, until
-the limit runs out, raises KRILL_DEVICE_ERR_TIMEOUT in the pool's device error
-flag and finishes the launch. Nothing faults or traps. The test checks that
+(krill_pool_test_stall) makes an otherwise idle warp of CTA 0 wait for a
+shared-memory word that nothing sets: the wait runs out after the limit,
+raises KRILL_DEVICE_ERR_TIMEOUT in the pool's device error flag, and the
+launch ends. Nothing faults or traps. The test checks that
 the launch ends well within a second, that the flag reports the timeout (and
 is cleared by reading it), and that the context stays usable: the same pool
 and a fresh one then give results within the attention tolerance of the
