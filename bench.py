@@ -641,7 +641,7 @@ def run_next_row(args, cfg, kb, torch, rank, world, local_rank):
                     config={"workload": args.config, "seqs": n, "chunk_tokens": C, "layers": layers,
                             "kv_heads": hkv, "head_dim": D, "group_size": G, "kv_in_dtype": "bf16",
                             "rope": "rotate-half, base 10000, caller-owned f32 cos/sin table"},
-                    roofline={"bound": "hbm", "kernel": "append_quantize_kernel (RoPE)",
+                    roofline={"bound": "hbm", "kernel": "append_rows_kernel (RoPE)",
                               "achieved": algo / (r["kernel_ms"] / 1e3) / 1e9, "peak": peak,
                               "unit": "GB/s", "peak_kind": peak_kind,
                               "frac": algo / (r["kernel_ms"] / 1e3) / 1e9 / peak,
@@ -1065,8 +1065,10 @@ def main():
     layers, hq, hkv, D, G = cfg["layers"], cfg["hq"], cfg["hkv"], cfg["D"], cfg["G"]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
     total_steps = args.warmup + args.steps + 4  # repetitions rewind to the same lengths
-    # at N > 1 the pool also holds one imported prefix entry (4096 tokens)
-    blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4 + (PEER_PREFIX // 256 if world > 1 else 0)
+    # at N > 1 the pool also holds the prefix entry: rank 0's original, or on
+    # the other ranks the two imports (the first, kept by the prefix cache,
+    # and the timed one) until the check ends
+    blocks = sum((L + total_steps + 255) // 256 for L in mine) + 4 + (2 * PEER_PREFIX // 256 + 2 if world > 1 else 0)
     raw = args.kv == "bf16"
     if raw and cfg["dtype"] != "bf16":
         raise SystemExit("--kv bf16 needs a workload with bf16 K/V")
