@@ -79,6 +79,13 @@ REPEATS = 5
 PEER_PREFIX = 4096
 
 
+
+def attn_impl_of(args):
+    """The pool's attention implementation for --attn-impl."""
+    import krill_b200 as kb
+    return {"tc": kb.ATTN_TENSOR_CORE, "tc1sm": kb.ATTN_TENSOR_CORE_1SM,
+            "cuda": kb.ATTN_CUDA_CORE}[args.attn_impl]
+
 def algo_bytes_attn(L, hkv, D, G):
     return L * hkv * (2 * D + 8 * D // G)
 
@@ -400,7 +407,8 @@ def run_prefix_workload(args, cfg, kb, torch, dist, rank, world, local_rank):
     e2e_steps = max(3, args.steps // 2)
     steps_total = args.warmup + REPEATS * args.steps + e2e_steps + 3
     blocks = P // 256 + n * ((P + S + steps_total + 255) // 256 - P // 256 + 1) + 4
-    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, device=local_rank)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G, device=local_rank,
+                     attn_impl=attn_impl_of(args))
     pc = kb.PrefixCache(pool)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
@@ -717,7 +725,7 @@ def run_next_row(args, cfg, kb, torch, rank, world, local_rank):
         n, P, C = cfg["seqs"], cfg["prefix"], cfg["chunk"]
         total = P + (args.warmup + args.steps) * C
         pool = kb.KVPool(layers, hkv, hq, D, num_blocks=n * ((total + 255) // 256 + 1) + 4, group_size=G,
-                         device=local_rank)
+                         device=local_rank, attn_impl=attn_impl_of(args))
         seqs = [pool.create_sequence() for _ in range(n)]
         for s_ in seqs:
             for l0 in range(0, layers, 8):
@@ -986,7 +994,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="krill", choices=["krill", "reference"])
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
-    ap.add_argument("--attn-impl", default="tc", choices=["tc", "cuda"])
+    ap.add_argument("--attn-impl", default="tc", choices=["tc", "tc1sm", "cuda"],
+                    help="tc: tensor cores (cascade on CTA pairs where items have > 128 rows); "
+                         "tc1sm: cascade on single CTAs; cuda: CUDA-core decode")
     ap.add_argument("--kv", default="int8", choices=["int8", "bf16"],
                     help="pool format; bf16 = the unquantized comparison variant (default workload)")
     ap.add_argument("--split-tokens", type=int, default=0)
@@ -1073,7 +1083,7 @@ def main():
     if raw and cfg["dtype"] != "bf16":
         raise SystemExit("--kv bf16 needs a workload with bf16 K/V")
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=blocks, group_size=G,
-                     attn_impl=kb.ATTN_TENSOR_CORE if args.attn_impl == "tc" else kb.ATTN_CUDA_CORE,
+                     attn_impl=attn_impl_of(args),
                      split_tokens=args.split_tokens, kv_format=kb.KV_BF16 if raw else kb.KV_INT8,
                      device=local_rank)
     seqs = [pool.create_sequence() for _ in mine]

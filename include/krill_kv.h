@@ -72,10 +72,19 @@ enum { KRILL_QUANT_F32 = 0, KRILL_QUANT_INPUT_DTYPE = 1 };
  * results within the attention tolerance):
  *   TENSOR_CORE       per-sequence decode on mma.sync m16n8k16 over the
  *                     dequantized tiles; the shared-prefix (cascade) part on
- *                     tcgen05 with tensor-memory accumulators (head_dim <= 128)
+ *                     tcgen05 with tensor-memory accumulators (head_dim <= 128),
+ *                     as pairs of CTAs (cta_group::2, M = 256) when its items
+ *                     have more than 128 query rows
  *   CUDA_CORE         per-sequence decode on FMA, no cascade
- *   TENSOR_CORE_SYNC  as TENSOR_CORE with the cascade part on mma.sync */
-enum { KRILL_ATTN_TENSOR_CORE = 0, KRILL_ATTN_CUDA_CORE = 1, KRILL_ATTN_TENSOR_CORE_SYNC = 2 };
+ *   TENSOR_CORE_SYNC  as TENSOR_CORE with the cascade part on mma.sync
+ *   TENSOR_CORE_1SM   as TENSOR_CORE with the tcgen05 cascade on single CTAs
+ *                     (M = 128 per instruction) whatever the row count */
+enum {
+  KRILL_ATTN_TENSOR_CORE = 0,
+  KRILL_ATTN_CUDA_CORE = 1,
+  KRILL_ATTN_TENSOR_CORE_SYNC = 2,
+  KRILL_ATTN_TENSOR_CORE_1SM = 3
+};
 
 /* Storage format of a pool: int8 codes with fp16 scale/zero per group (the
  * reference's QuantizedKVCache), or raw bf16 K/V (the unquantized KVCache of

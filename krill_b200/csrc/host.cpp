@@ -150,6 +150,7 @@ struct krill_pool_s {
   std::vector<Seq> seqs;
   std::vector<uint32_t> free_slots;
   int num_sms = 148;
+  int pair_slots = 74;  // CTA pairs of the cascade kernel resident at once (0: none)
   float* d_partials = nullptr;
   int64_t partials_cap = 0;
   unsigned long long* d_split_ctr = nullptr;  // arrival counters, one per partial record
@@ -765,12 +766,20 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
           }
         }
   }
+  // Items of more than 128 rows run on CTA pairs (one M = 256 instruction for
+  // both halves, each CTA dequantizing half of every sub-block); a pair then
+  // takes the place of one CTA in the split below.
+  bool sh_pair = false;
+  if (!pl.pairs.empty() && p->cfg.attn_impl == KRILL_ATTN_TENSOR_CORE && p->pair_slots > 0 &&
+      shared_uses_umma(g, p->cfg.attn_impl))
+    for (const Plan::Pair& pr : pl.pairs) sh_pair = sh_pair || pr.n_rows > 128;
   if (!pl.pairs.empty()) {
     int64_t W = 0;
     for (const Plan::Pair& pr : pl.pairs) W += pr.n_sb;
     constexpr int64_t kMinFragment = 8;  // sub-blocks
+    const int64_t workers = sh_pair ? p->pair_slots : p->num_sms;
     const int64_t grid_sh =
-        std::max<int64_t>(1, std::min<int64_t>(p->num_sms, (W + kMinFragment - 1) / kMinFragment));
+        std::max<int64_t>(1, std::min<int64_t>(workers, (W + kMinFragment - 1) / kMinFragment));
     const int64_t per = (W + grid_sh - 1) / grid_sh;
     sh_grid = (int)((W + per - 1) / per);
     pl.sh_cta.assign((size_t)sh_grid + 1, 0);
@@ -948,7 +957,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   if (pre_bytes) std::memcpy(h + pre_off, pre->dst.data(), pre->dst.size() * sizeof(AppendDst));
   pl.last_groups = n_groups;
   pl.last_pslots = n_pslots;
-  pl.last_sh_grid = sh_grid;
+  pl.last_sh_grid = sh_pair ? 2 * sh_grid : sh_grid;
   pl.last_sh_items = (int64_t)pl.sh_items.size();
   pl.last_C = C;
   pl.last_HG = HG;
@@ -964,6 +973,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     dp.n_split_units = (int)pl.split_units.size();
     dp.split_ctr = merge_in_kernel ? &ctr_tag : nullptr;
     dp.sh_grid = sh_grid;
+    dp.sh_pair = sh_pair ? 1 : 0;
     describe_attention(g, dp, grid, p->cfg.attn_impl, pl.last_kernels, sizeof(pl.last_kernels));
   }
   if (p->host_only) return KRILL_OK;  // dry run: planned, nothing launched
@@ -1002,6 +1012,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     ap.sh_cta_off = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes);
     ap.sh_members = reinterpret_cast<const int32_t*>(slot->d + sh_off + shi_bytes + shc_bytes);
     ap.sh_grid = sh_grid;
+    ap.sh_pair = sh_pair ? 1 : 0;
     ap.n_pslots = n_pslots;
   }
   if (pre_bytes) {
@@ -1112,7 +1123,7 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   if (cfg.quant_variant != KRILL_QUANT_F32 && cfg.quant_variant != KRILL_QUANT_INPUT_DTYPE)
     return fail(KRILL_ERR_INVALID, "bad quant_variant");
   if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE &&
-      cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_SYNC)
+      cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_SYNC && cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_1SM)
     return fail(KRILL_ERR_INVALID, "bad attn_impl");
   if (cfg.split_tokens < 0 || cfg.split_tokens % 64 != 0)
     return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");
@@ -1164,6 +1175,10 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     // pool's device current, so that the driver reserves it (a module load
     // under lazy loading) at pool creation rather than inside a decode call.
     if (e == cudaSuccess) e = krill::noalloc_prepare(device);
+    // CTA pairs of the cascade kernel that fit at once (0: single-CTA cascade)
+    if (e == cudaSuccess && cfg.attn_impl == KRILL_ATTN_TENSOR_CORE &&
+        shared_uses_umma(p->geom, cfg.attn_impl))
+      p->pair_slots = std::min(krill::shared_pair_capacity(p->geom), p->num_sms / 2);
     if (e != cudaSuccess) {
       krill_status_t code = (e == cudaErrorMemoryAllocation) ? KRILL_ERR_OOM : KRILL_ERR_CUDA;
       if (p->d_pool) cudaFree(p->d_pool);

@@ -124,7 +124,8 @@ struct AttnParams {
   const ShItem* sh_items;
   const int32_t* sh_cta_off;  // [sh_grid + 1]
   const int32_t* sh_members;  // unit ids
-  int sh_grid;
+  int sh_grid;                // CTAs, or CTA pairs when sh_pair (sh_cta_off per pair)
+  int sh_pair;                // 1: the tcgen05 cascade runs as CTA pairs (cta_group::2)
   int n_pslots;               // prefix record slots per cascaded unit
   // host side only: launch the decode kernel as the programmatic dependent of
   // the append kernel launched just before it on the stream
@@ -177,6 +178,9 @@ inline bool attn_needs_combine(const AttnParams& p, int grid, int impl) {
 // per item as two 128-row halves) for head_dim <= 128 under
 // KRILL_ATTN_TENSOR_CORE; otherwise on mma.sync (sh_rows(D) rows per item).
 bool shared_uses_umma(const Geom& g, int impl);
+// Clusters of two CTAs of the pair cascade kernel that fit on the current
+// device at once (0: no pair kernel for this geometry, or no device).
+int shared_pair_capacity(const Geom& g);
 cudaError_t launch_shared_umma(const Geom& g, const AttnParams& p, cudaStream_t stream);
 inline int shared_rows(const Geom& g, int impl) { return shared_uses_umma(g, impl) ? 256 : sh_rows(g.D); }
 // Launch description produced for the allocation-free decode attention:

@@ -1240,8 +1240,10 @@ void describe_attention(const Geom& g, const AttnParams& p, int grid, int impl, 
   if (cap == 0) return;
   buf[0] = 0;
   if (p.sh_grid > 0)
-    put(snprintf(buf + n, cap - n, "%s<%d,%d>+", shared_uses_umma(g, impl) ? "attn_shared_umma_kernel"
-                                                                          : "attn_shared_kernel",
+    put(snprintf(buf + n, cap - n, "%s<%d,%d>+",
+                 !shared_uses_umma(g, impl) ? "attn_shared_kernel"
+                 : p.sh_pair                ? "attn_shared_pair_kernel"
+                                            : "attn_shared_umma_kernel",
                  g.D, g.NG));
   if (grid > 0) {
     if (impl == 1) put(snprintf(buf + n, cap - n, "attn_cc_kernel<%d,%d,%d>", g.D, g.NG, p.g));

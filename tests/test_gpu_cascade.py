@@ -30,9 +30,10 @@ from tests.test_gpu_attention import ATOL, half_ulp  # noqa: E402
 
 def run_cascade(D, G, hq, hkv, dtype, prefixes, scale, layers=2, extra=(), outliers=False,
                 out_dtype=torch.float32, steps=2, seed=0, min_groups=1, min_slots=1,
-                impl=kb.ATTN_TENSOR_CORE):
+                impl=kb.ATTN_TENSOR_CORE, expect_kernel=None):
     """prefixes: list of (prefix length, [suffix length per fork]). extra:
-    lengths of independent sequences batched alongside."""
+    lengths of independent sequences batched alongside. expect_kernel: a
+    kernel name that the step's launch description must contain."""
     rng = np.random.default_rng(seed)
     total = sum(p + sum(s) + len(s) * 256 for p, s in prefixes) + sum(extra) + 1024
     pool = kb.KVPool(layers, hkv, hq, D, num_blocks=total // 256 + 16 * (len(extra) + 4),
@@ -81,6 +82,8 @@ def run_cascade(D, G, hq, hkv, dtype, prefixes, scale, layers=2, extra=(), outli
         torch.cuda.synchronize()
         groups, items, slots, ctas = pool.last_cascade()
         assert groups >= min_groups and items > 0 and slots >= min_slots and ctas > 0
+        if expect_kernel is not None:
+            assert expect_kernel in pool.last_kernels(), pool.last_kernels()
         assert pool.device_error() == 0
         got = out.float().cpu().numpy().astype(np.float64)
         for i in range(n):
@@ -155,3 +158,35 @@ def test_cascade_mma_sync_variant(D, G, hq, hkv, dtype, scale):
     # the cascade part on mma.sync (KRILL_ATTN_TENSOR_CORE_SYNC), kept for comparison
     run_cascade(D, G, hq, hkv, dtype, [(1024, [1, 17, 64, 300])], scale,
                 impl=kb.ATTN_TENSOR_CORE_SYNC)
+
+
+PAIR = "attn_shared_pair_kernel"
+
+
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,scale,forks", [
+    (128, 64, 32, 8, BF16, 1 / math.sqrt(128), 64),    # configs[2] shape: 256 rows per item
+    (64, 64, 32, 8, F16, 1 / 8, 40),                   # D = 64: 160 rows
+    (128, 64, 32, 4, BF16, 1 / math.sqrt(128), 20),    # GQA 8: 160 rows
+    (128, 128, 16, 16, F16, 1 / math.sqrt(128), 150),  # G = D, MHA: items of 150 rows
+])
+def test_cascade_cta_pairs(D, G, hq, hkv, dtype, scale, forks):
+    # items of more than 128 query rows run on CTA pairs (tcgen05 cta_group::2,
+    # M = 256 per instruction, each CTA dequantizing half of every sub-block)
+    run_cascade(D, G, hq, hkv, dtype, [(1024, [1 + (i * 37) % 300 for i in range(forks)])], scale,
+                expect_kernel=PAIR)
+
+
+def test_cascade_cta_pairs_outliers_and_fragments():
+    # scales above 64 (exact two-rounding dequant) on the pair kernel; a
+    # 4096-token prefix over 4 layers cut into several fragments per (layer, head)
+    run_cascade(128, 64, 32, 4, BF16, [(1024, [10 + 3 * i for i in range(40)])], 1 / math.sqrt(128),
+                outliers=True, layers=1, expect_kernel=PAIR)
+    run_cascade(128, 64, 32, 8, BF16, [(4096, [1 + 5 * i for i in range(48)])], 1 / math.sqrt(128),
+                layers=4, steps=1, min_slots=2, expect_kernel=PAIR)
+
+
+def test_cascade_single_cta_variant():
+    # the same many-row items on one CTA per item (KRILL_ATTN_TENSOR_CORE_1SM)
+    run_cascade(128, 64, 32, 8, BF16, [(1024, [1 + (i * 37) % 300 for i in range(64)])],
+                1 / math.sqrt(128), impl=kb.ATTN_TENSOR_CORE_1SM,
+                expect_kernel="attn_shared_umma_kernel")

@@ -97,6 +97,9 @@ def test_prefill_attention_matches_oracle(D, G, hq, hkv, dtype, prefix, chunk):
     kb.prefill_attention(pool, seqs, 0, dev_bits(qb, dtype), out, scale)
     torch.cuda.synchronize()
     assert pool.device_error() == 0
+    # query blocks of more than 128 rows run on the CTA-pair cascade kernel
+    if chunk * (hq // hkv) > 128:
+        assert "attn_shared_pair_kernel" in pool.last_kernels(), pool.last_kernels()
     got = out.cpu().numpy().astype(np.float64)
     check_q = sorted(set(list(range(0, chunk, 13)) + [chunk - 1]))
     for i in range(n):
