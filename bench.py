@@ -285,10 +285,7 @@ def headline_config(args, cfg, world, lengths_all, mine, raw):
             "mean_len": float(np.mean(lengths_all)),
             "l2": (f"inputs larger than L2 ({step_b / 1e9:.2f} GB/step)" if step_b >= L2_FLUSH_BYTES
                    else f"L2 flushed between steps ({step_b / 1e9:.3f} GB/step < "
-                        f"{L2_FLUSH_BYTES / 1e9:.2f} GB; each step timed alone; flush: "
-                        + ("a 256 MB buffer written, then another 256 MB read, so no dirty line of "
-                           "the flush is left for the step to write back" if args.l2_flush == "write-read"
-                           else "a 256 MB buffer written") + ")"),
+                        f"{L2_FLUSH_BYTES / 1e9:.2f} GB; each step timed alone)"),
             "attn_impl": args.attn_impl, "parallelism": f"seq-partition x{world}"}
 
 
@@ -1006,8 +1003,6 @@ def main():
     ap.add_argument("--e2e-chunk", type=int, default=0,
                     help="layers per chunk of the host-buffer step (0 = one chunk)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--l2-flush", default="write-read", choices=["write", "write-read"],
-                    help="L2 flush between steps of a workload smaller than L2")
     ap.add_argument("--cpu-layer-sample", type=int, default=12)
     ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (profiling)")
     ap.add_argument("--diag", action="store_true",
@@ -1150,19 +1145,9 @@ def main():
     # then each step is timed alone, with an L2 flush (a write of 2 x L2)
     # between steps, outside the timed pairs. Otherwise the inputs are larger
     # than L2 and the steps run back to back.
-    flush = flush_r = None
+    flush = None
     if step_bytes([L + 1 for L in len_before], cfg, raw)[1] < L2_FLUSH_BYTES:
         flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-        if args.l2_flush == "write-read":
-            flush_r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-
-    def flush_l2():
-        """Evicts the step's data from L2: a write of 2 x L2; with
-        --l2-flush write-read also a read of another 2 x L2, which writes the
-        flush's own dirty lines back before the timed step instead of during it."""
-        flush.add_(1)
-        if flush_r is not None:
-            flush_r.sum()
     n_pairs = 1 if flush is None else args.steps
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_pairs)]
@@ -1176,7 +1161,7 @@ def main():
         torch.cuda.synchronize()
         for i in range(args.steps):
             if flush is not None:
-                flush_l2()
+                flush.add_(1)
             if flush is not None or i == 0:
                 evs[min(i, n_pairs - 1)][0].record(stream)
             kb.decode_step(pool, seqs, 0, k_new, v_new, q, out, cfg["scale"], stream=stream)
@@ -1259,7 +1244,7 @@ def main():
     e2e_ms = []
     for _ in range(e2e_steps):
         if flush is not None:
-            flush_l2()
+            flush.add_(1)
             torch.cuda.synchronize()
         t0 = time.perf_counter()
         kb.decode_step_host(pool, seqs, 0, h_k, h_v, h_q, h_out, cfg["scale"],

@@ -961,17 +961,6 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   pl.last_sh_items = (int64_t)pl.sh_items.size();
   pl.last_C = C;
   pl.last_HG = HG;
-  // Latency-bound single-head items at head_dim 64 (configs[0]-like steps:
-  // one item per CTA, each a whole sequence for one kv head) run with 12
-  // consumer warps instead of 8, so each warp's chain of sub-blocks is a
-  // third shorter; they merge in shared memory as before.
-  int ncw = 8;
-  if (latency_bound && HG == 1 && g.fmt == kFmtInt8 && g.D == 64 && g.NG == 1 &&
-      p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE && n_items <= grid) {
-    int64_t min_sb = INT64_MAX;
-    for (const AttnItem& it : pl.items) min_sb = std::min<int64_t>(min_sb, it.sb_end - it.sb_begin);
-    if (min_sb >= 12) ncw = 12;
-  }
   pl.last_items = n_items;
   pl.last_grid = grid;
   {
@@ -980,7 +969,6 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     static unsigned long long ctr_tag;
     AttnParams dp{};
     dp.hg = HG;
-    dp.ncw = ncw;
     dp.g = g.g;
     dp.n_split_units = (int)pl.split_units.size();
     dp.split_ctr = merge_in_kernel ? &ctr_tag : nullptr;
@@ -1005,7 +993,6 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.bt = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes);
   ap.bt_stride = (int)bt_stride;
   ap.hg = HG;
-  ap.ncw = ncw;
   ap.split_units = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes + bt_bytes);
   ap.n_split_units = (int)pl.split_units.size();
   ap.q = q;

@@ -97,8 +97,6 @@ struct AttnParams {
   int64_t page_bytes, sb_bytes;
   int L, Hkv, Hq, g, ring;
   int hg;                  // kv heads per item (divides Hkv)
-  int ncw;                 // consumer warps of the decode kernel: 8, or 12 for
-                           // latency-bound single-head items at head_dim 64
   const AttnUnit* units;
   const AttnItem* items;
   const int32_t* cta_off;  // [grid + 1] item ranges per CTA

@@ -697,17 +697,14 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 // rounds. For an item of n_sb sub-blocks the
 // producer issues, per round, sub-block k of head hr as stage J0 + k*HPR + hr;
 // warp (hr, r) takes the sub-blocks k = r, r + R, ...
-// Threads: NCW consumer warps (two or four warpgroups) + one producer
-// warpgroup, of which one warp issues the copies. At start the producer
-// warpgroup gives its registers back (setmaxnreg.dec to 56) and the consumers
-// take them: with 8 consumer warps setmaxnreg.inc to 224, 128*56 + 256*224 =
-// 384*168, the launch budget; with 12 (latency-bound single-head plans at
-// head_dim 64) to 152, 128*56 + 384*152 = 512*128.
+// Threads: NCW consumer warps (two warpgroups) + one producer warpgroup, of
+// which one warp issues the copies. At start the producer warpgroup gives its
+// registers back (setmaxnreg.dec to 56) and the consumers take them
+// (setmaxnreg.inc to 224): 128*56 + 256*224 = 384*168, the launch budget.
 // (With 40 the producer's metadata prefetch spilled; 224 still holds every
 // consumer without spills.)
 constexpr int kProducerRegs = 56;
-template <int NCW>
-constexpr int consumer_regs() { return NCW == 8 ? 224 : 152; }
+constexpr int kConsumerRegs = 224;
 
 // Consumer warps of attn_tc_kernel. FAST selects the one-fma dequantization,
 // exact only while every scale in the pool is below 64 in magnitude; the
@@ -839,7 +836,7 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
 
 template <int D, int NG, int NCW, int R, int NSTAGE, int FMT>
 __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
-  static_assert(NCW == 8 || NCW == 12, "two or three consumer warpgroups");
+  static_assert(NCW == 8, "two consumer warpgroups");
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
   constexpr int SB = SM::SB;
   constexpr int HPR = NCW / R;
@@ -965,7 +962,7 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
   }
 
   // ---------------- consumers ----------------
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(consumer_regs<NCW>()));
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   if (FMT == kFmtInt8 && *reinterpret_cast<volatile const int*>(p.large_scale) != 0)
     attn_consume<D, NG, NCW, R, NSTAGE, FMT, false>(p, smem, stages, bar_base, cta_abort, tags, warp,
                                                     lane, it0, it1, rounds);
@@ -992,7 +989,7 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
     cudaFuncAttributes fa;
     e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>);
     if (e != cudaSuccess) return e;
-    if (fa.numRegs * (NCW + 4) * 32 < 128 * kProducerRegs + NCW * 32 * consumer_regs<NCW>())
+    if (fa.numRegs * (NCW + 4) * 32 < 128 * kProducerRegs + NCW * 32 * kConsumerRegs)
       return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
@@ -1022,16 +1019,14 @@ cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
   const int hpr = p.hg < NCW ? p.hg : NCW;
   if (NCW % hpr != 0 || p.hg % hpr != 0) return cudaErrorInvalidValue;
   cudaError_t e = cudaErrorInvalidValue;
-  if constexpr (NCW == 12) {  // single-head items only: all 12 warps share one head
-    if (hpr == 1) e = launch_tc<D, NG, NCW, 12, FMT>(p, grid, stream);
-  } else {
-    switch (NCW / hpr) {
-      case 1: e = launch_tc<D, NG, NCW, 1, FMT>(p, grid, stream); break;
-      case 2: e = launch_tc<D, NG, NCW, 2, FMT>(p, grid, stream); break;
-      case 4: e = launch_tc<D, NG, NCW, 4, FMT>(p, grid, stream); break;
-      case 8: e = launch_tc<D, NG, NCW, 8, FMT>(p, grid, stream); break;
-      default: break;
-    }
+  switch (NCW / hpr) {
+    case 1: e = launch_tc<D, NG, NCW, 1, FMT>(p, grid, stream); break;
+    case 2: e = launch_tc<D, NG, NCW, 2, FMT>(p, grid, stream); break;
+    case 4: e = launch_tc<D, NG, NCW, 4, FMT>(p, grid, stream); break;
+    case 8:
+      if constexpr (NCW == 8) e = launch_tc<D, NG, NCW, 8, FMT>(p, grid, stream);
+      break;
+    default: break;
   }
   if (e != cudaSuccess || p.n_split_units == 0 || p.split_ctr != nullptr) return e;
   attn_combine_kernel<D><<<p.n_split_units * p.Hkv, 128, 0, stream>>>(p);
@@ -1225,8 +1220,6 @@ int tc_desc(char* buf, size_t cap) {
 }
 template <int D, int NG, int FMT = kFmtInt8>
 int tc_desc_r(const AttnParams& p, char* buf, size_t cap) {
-  if constexpr (D == 64 && NG == 1 && FMT == kFmtInt8)
-    if (p.ncw == 12 && p.hg == 1) return tc_desc<64, 1, 12, 12, kFmtInt8>(buf, cap);
   const int hpr = p.hg < 8 ? p.hg : 8;
   if (hpr <= 0 || 8 % hpr != 0) return snprintf(buf, cap, "none");
   switch (8 / hpr) {
@@ -1289,8 +1282,7 @@ cudaError_t launch_attention(const Geom& g, const AttnParams& p, int grid, int i
     if (g.D == 128) return launch_tc_r<128, 1, 8, kFmtBf16>(p, grid, stream);
     return cudaErrorInvalidValue;
   }
-  if (g.D == 64 && g.NG == 1)
-    return p.ncw == 12 ? launch_tc_r<64, 1, 12>(p, grid, stream) : launch_tc_r<64, 1, 8>(p, grid, stream);
+  if (g.D == 64 && g.NG == 1) return launch_tc_r<64, 1, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 2) return launch_tc_r<128, 2, 8>(p, grid, stream);
   if (g.D == 128 && g.NG == 1) return launch_tc_r<128, 1, 8>(p, grid, stream);
   if (g.D == 256 && g.NG == 4) return launch_tc_r<256, 4, 8>(p, grid, stream);

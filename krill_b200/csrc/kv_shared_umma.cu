@@ -721,8 +721,7 @@ cudaError_t launch_um(const AttnParams& p, cudaStream_t stream) {
 // memory is released. Waits are bounded as in the one-CTA kernel.
 constexpr int kPrNF = 5;           // K/V half-tile stages
 constexpr int kPrNR = 4;           // raw half-sub-block stages
-constexpr int kPrNS = 4;           // S buffers in tensor memory (64 columns each)
-constexpr uint32_t kPrCols = 512;  // O at [0, D); S buffer b at D + 64 b
+constexpr uint32_t kPrCols = 256;  // O at [0, D); S double buffer at D and D + 64
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -808,7 +807,7 @@ struct PrSmem {
   using SG = SubGeom<D, NG>;
   static_assert(SG::T == 64, "one 64-token sub-block per tile");
   static constexpr int Q_BYTES = 128 * D * 2;         // this CTA's 128 rows
-  static constexpr int P_BYTES = 128 * 64 * 2;        // one of two P buffers
+  static constexpr int P_BYTES = 128 * 64 * 2;
   static constexpr int KH_BYTES = 32 * D * 2;         // K half tile: 32 tokens x D
   static constexpr int VH_BYTES = (D / 2) * 64 * 2;   // V half tile: D/2 rows x 64 tokens
   static constexpr int KV_STAGE = KH_BYTES + VH_BYTES;
@@ -818,17 +817,16 @@ struct PrSmem {
   static constexpr int RAW_STAGE = RK_BYTES + RV_BYTES + RM_BYTES;
   static constexpr int Q_OFF = 0;
   static constexpr int P_OFF = Q_OFF + Q_BYTES;
-  static constexpr int KV_OFF = P_OFF + 2 * P_BYTES;
+  static constexpr int KV_OFF = P_OFF + P_BYTES;
   static constexpr int RAW_OFF = KV_OFF + kPrNF * KV_STAGE;
   static constexpr int XM_OFF = RAW_OFF + kPrNR * RAW_STAGE;  // row max exchange [2][2][128] f32
   static constexpr int XL_OFF = XM_OFF + 2 * 2 * 128 * 4;      // row sum exchange [2][128] f32
   static constexpr int BAR_OFF = XL_OFF + 2 * 128 * 4;
-  // raw full / empty [NR], K/V full / free [NF], S full [NS], P full [2],
-  // P·V done [2] (per P buffer), Q full, final. K/V full, P full and Q full
-  // are used in rank 0 only.
+  // raw full / empty [NR], K/V full / free [NF], S full [2], P full, P·V
+  // done, Q full, final. K/V full, P full and Q full are used in rank 0 only.
   static constexpr int B_RF = 0, B_RE = kPrNR, B_KF = 2 * kPrNR, B_KE = 2 * kPrNR + kPrNF,
-                       B_SF = 2 * kPrNR + 2 * kPrNF, B_PF = B_SF + kPrNS, B_PD = B_PF + 2,
-                       B_QF = B_PD + 2, B_FIN = B_QF + 1, NBAR = B_FIN + 1;
+                       B_SF = 2 * kPrNR + 2 * kPrNF, B_PF = B_SF + 2, B_PD = B_PF + 1,
+                       B_QF = B_PD + 1, B_FIN = B_QF + 1, NBAR = B_FIN + 1;
   static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem address, abort flag, wait limit
   static constexpr int TOTAL = MISC_OFF + 16;
   static_assert(Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0 && KH_BYTES % 1024 == 0 &&
@@ -943,11 +941,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
       mbar_init(bar(SM::B_KF + s), 2 * kUmDeqWarps);  // both CTAs' dequantizers (rank 0)
       mbar_init(bar(SM::B_KE + s), 1);                // MMA commit
     }
-    for (int b = 0; b < kPrNS; ++b) mbar_init(bar(SM::B_SF + b), 1);  // MMA commit
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(SM::B_PF + b), 16);  // both CTAs' 8 softmax warps (rank 0)
-      mbar_init(bar(SM::B_PD + b), 1);   // MMA commit
-    }
+    mbar_init(bar(SM::B_SF), 1);
+    mbar_init(bar(SM::B_SF + 1), 1);
+    mbar_init(bar(SM::B_PF), 16);  // both CTAs' 8 softmax warps (rank 0)
+    mbar_init(bar(SM::B_PD), 1);
     mbar_init(bar(SM::B_QF), 16);
     mbar_init(bar(SM::B_FIN), 1);
     init_wait_state(cta_abort, p.wait_us);
@@ -1038,37 +1035,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
         uint64_t idle_since = 0;
         while (jp < n) {
           bool progressed = false;
-          // S of tile js reuses the buffer of tile js - kPrNS: issued once the
-          // softmax of that tile signalled P (so its S was read), i.e. once
-          // P·V of js - kPrNS was issued
-          if (js < n && js <= jp + kPrNS - 1) {
+          if (js < n && js <= jp + 1) {
             const uint32_t Jc = J + js, st = Jc % kPrNF;
             if (mbar_try_wait_cl(bar(SM::B_KF + st), (Jc / kPrNF) & 1)) {
               tc_fence_after();
               const uint32_t c = cnt + js;
               const uint64_t kd = dK0 + (uint64_t)(st * (SM::KV_STAGE >> 4));
-              const uint32_t sc = tmem + (uint32_t)D + 64u * (c % kPrNS);
+              const uint32_t sc = tmem + (uint32_t)D + 64u * (c & 1);
 #pragma unroll
               for (int ks = 0; ks < D / 16; ++ks)
                 umma2_f16(sc, dQ0 + (uint64_t)(((ks >> 2) * (128 * 128) + 32 * (ks & 3)) >> 4),
                           kd + (uint64_t)(((ks >> 2) * (32 * 128) + 32 * (ks & 3)) >> 4), idS,
                           ks > 0 ? 1u : 0u);
-              umma2_commit_both(bar(SM::B_SF + (c % kPrNS)));
+              umma2_commit_both(bar(SM::B_SF + (c & 1)));
               ++js;
               progressed = true;
             }
           }
-          const uint32_t cp = cnt + jp;  // P buffer cp & 1, its (cp >> 1)-th use
-          if (jp < js && mbar_try_wait_cl(bar(SM::B_PF + (cp & 1)), (cp >> 1) & 1)) {
+          if (jp < js && mbar_try_wait_cl(bar(SM::B_PF), (cnt + jp) & 1)) {
             tc_fence_after();
             const uint32_t st = (J + jp) % kPrNF;
             const uint64_t vd = dV0 + (uint64_t)(st * (SM::KV_STAGE >> 4));
-            const uint64_t pd = dP0 + (uint64_t)((cp & 1) * (SM::P_BYTES >> 4));
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma2_f16(tmem, pd + (uint64_t)(2 * ks), vd + (uint64_t)(2 * ks), idO,
+              umma2_f16(tmem, dP0 + (uint64_t)(2 * ks), vd + (uint64_t)(2 * ks), idO,
                         (jp > 0 || ks > 0) ? 1u : 0u);
-            umma2_commit_both(bar(SM::B_PD + (cp & 1)));  // O updated, P buffer free
+            umma2_commit_both(bar(SM::B_PD));       // O updated, P free
             umma2_commit_both(bar(SM::B_KE + st));  // K/V stage free in both CTAs
             ++jp;
             progressed = true;
@@ -1109,6 +1101,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
     float* xm = reinterpret_cast<float*>(smem + SM::XM_OFF);
     float* xl = reinterpret_cast<float*>(smem + SM::XL_OFF);
     const int gq = p.g;
+    uint8_t* pb = smem + SM::P_OFF;
     uint32_t cnt = 0;
     for (int it = it0; it < it1; ++it) {
       const ShItem item = p.sh_items[it];
@@ -1146,10 +1139,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n; ++j) {
         const uint32_t c = cnt + j;
-        mbar_wait_cl(bar(SM::B_SF + (c % kPrNS)), (c / kPrNS) & 1, cta_abort, p.err);
+        mbar_wait_cl(bar(SM::B_SF + (c & 1)), (c >> 1) & 1, cta_abort, p.err);
         tc_fence_after();
         float s[32];
-        tmem_ld32(lane_addr + (uint32_t)D + 64u * (c % kPrNS) + 32u * (uint32_t)ch, s);
+        tmem_ld32(lane_addr + (uint32_t)D + 64u * (c & 1) + 32u * (uint32_t)ch, s);
         float sc = p.scale_log2;
         if (!(sc > 0.f)) {
 #pragma unroll
@@ -1174,14 +1167,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
         mx = fmaxf(mx, xp[(ch ^ 1) * 128 + t]);
         // both threads of a row hold the same m and mx, so they take the
         // same branch (and __any_sync agrees between the row's two warps)
+        bool pv_done = j == 0;
         if (j == 0) {
           m = mx;
         } else {
           const bool grow = mx > m + 8.f || (m == -INFINITY && mx > -INFINITY);
           if (__any_sync(0xffffffffu, grow)) {
-            // O is touched only after P·V of tile c - 1 (the last one issued) completed
-            mbar_wait_cl(bar(SM::B_PD + ((c - 1) & 1)), ((c - 1) >> 1) & 1, cta_abort, p.err);
+            mbar_wait_cl(bar(SM::B_PD), (c - 1) & 1, cta_abort, p.err);
             tc_fence_after();
+            pv_done = true;
             const float mn = grow ? mx : m;
             const float al = m == -INFINITY ? 0.f : exp2f(m - mn);
             m = mn;
@@ -1207,9 +1201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
           ps[i & 7] += s[i];
         }
         l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        // P buffer c & 1 was last read by P·V of tile c - 2
-        if (c >= 2) mbar_wait_cl(bar(SM::B_PD + (c & 1)), ((c >> 1) - 1) & 1, cta_abort, p.err);
-        uint8_t* pb = smem + SM::P_OFF + (c & 1) * SM::P_BYTES;
+        if (!pv_done) mbar_wait_cl(bar(SM::B_PD), (c - 1) & 1, cta_abort, p.err);
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint4 w;
@@ -1222,12 +1214,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUmThreads, 1)
         fence_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_at(bar(SM::B_PF + (c & 1)), 0);
+        if (lane == 0) mbar_arrive_at(bar(SM::B_PF), 0);
       }
       if (n > 0) {
         // ---- epilogue: O row (this thread's D/2 columns) -> partial record ----
-        const uint32_t cl = cnt + n - 1;  // the item's last tile: its P·V is the last MMA
-        mbar_wait_cl(bar(SM::B_PD + (cl & 1)), (cl >> 1) & 1, cta_abort, p.err);
+        mbar_wait_cl(bar(SM::B_PD), (cnt + n - 1) & 1, cta_abort, p.err);
         tc_fence_after();
         xl[ch * 128 + t] = l;
         named_sync(nbar, 64);
