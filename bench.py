@@ -83,7 +83,7 @@ PEER_PREFIX = 4096
 def attn_impl_of(args):
     """The pool's attention implementation for --attn-impl."""
     import krill_b200 as kb
-    return {"tc": kb.ATTN_TENSOR_CORE, "tc1sm": kb.ATTN_TENSOR_CORE_1SM,
+    return {"tc": kb.ATTN_TENSOR_CORE, "tcpair": kb.ATTN_TENSOR_CORE_PAIR,
             "cuda": kb.ATTN_CUDA_CORE}[args.attn_impl]
 
 def algo_bytes_attn(L, hkv, D, G):
@@ -994,9 +994,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="krill", choices=["krill", "reference"])
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
-    ap.add_argument("--attn-impl", default="tc", choices=["tc", "tc1sm", "cuda"],
-                    help="tc: tensor cores (cascade on CTA pairs where items have > 128 rows); "
-                         "tc1sm: cascade on single CTAs; cuda: CUDA-core decode")
+    ap.add_argument("--attn-impl", default="tc", choices=["tc", "tcpair", "cuda"],
+                    help="tc: tensor cores (tcgen05 cascade, one CTA per item); tcpair: the "
+                         "cascade on CTA pairs where items have > 128 rows; cuda: CUDA-core decode")
     ap.add_argument("--kv", default="int8", choices=["int8", "bf16"],
                     help="pool format; bf16 = the unquantized comparison variant (default workload)")
     ap.add_argument("--split-tokens", type=int, default=0)

@@ -73,17 +73,17 @@ enum { KRILL_QUANT_F32 = 0, KRILL_QUANT_INPUT_DTYPE = 1 };
  *   TENSOR_CORE       per-sequence decode on mma.sync m16n8k16 over the
  *                     dequantized tiles; the shared-prefix (cascade) part on
  *                     tcgen05 with tensor-memory accumulators (head_dim <= 128),
- *                     as pairs of CTAs (cta_group::2, M = 256) when its items
- *                     have more than 128 query rows
+ *                     one CTA per item (M = 128 per instruction)
  *   CUDA_CORE         per-sequence decode on FMA, no cascade
  *   TENSOR_CORE_SYNC  as TENSOR_CORE with the cascade part on mma.sync
- *   TENSOR_CORE_1SM   as TENSOR_CORE with the tcgen05 cascade on single CTAs
- *                     (M = 128 per instruction) whatever the row count */
+ *   TENSOR_CORE_PAIR  as TENSOR_CORE with the tcgen05 cascade on pairs of
+ *                     CTAs (cta_group::2, M = 256 per instruction) where its
+ *                     items have more than 128 query rows */
 enum {
   KRILL_ATTN_TENSOR_CORE = 0,
   KRILL_ATTN_CUDA_CORE = 1,
   KRILL_ATTN_TENSOR_CORE_SYNC = 2,
-  KRILL_ATTN_TENSOR_CORE_1SM = 3
+  KRILL_ATTN_TENSOR_CORE_PAIR = 3
 };
 
 /* Storage format of a pool: int8 codes with fp16 scale/zero per group (the

@@ -23,7 +23,7 @@ KRILL_ERR_NO_DEVICE = 7
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32, DTYPE_U8 = 0, 1, 2, 3
 QUANT_F32, QUANT_INPUT_DTYPE = 0, 1
-ATTN_TENSOR_CORE, ATTN_CUDA_CORE, ATTN_TENSOR_CORE_SYNC, ATTN_TENSOR_CORE_1SM = 0, 1, 2, 3
+ATTN_TENSOR_CORE, ATTN_CUDA_CORE, ATTN_TENSOR_CORE_SYNC, ATTN_TENSOR_CORE_PAIR = 0, 1, 2, 3
 KV_INT8, KV_BF16 = 0, 1
 DEVICE_ERR_TIMEOUT = 1
 

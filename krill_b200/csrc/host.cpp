@@ -766,11 +766,12 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
           }
         }
   }
-  // Items of more than 128 rows run on CTA pairs (one M = 256 instruction for
-  // both halves, each CTA dequantizing half of every sub-block); a pair then
-  // takes the place of one CTA in the split below.
+  // Under KRILL_ATTN_TENSOR_CORE_PAIR, items of more than 128 rows run on CTA
+  // pairs (one M = 256 instruction for both halves, each CTA dequantizing
+  // half of every sub-block); a pair then takes the place of one CTA in the
+  // split below.
   bool sh_pair = false;
-  if (!pl.pairs.empty() && p->cfg.attn_impl == KRILL_ATTN_TENSOR_CORE && p->pair_slots > 0 &&
+  if (!pl.pairs.empty() && p->cfg.attn_impl == KRILL_ATTN_TENSOR_CORE_PAIR && p->pair_slots > 0 &&
       shared_uses_umma(g, p->cfg.attn_impl))
     for (const Plan::Pair& pr : pl.pairs) sh_pair = sh_pair || pr.n_rows > 128;
   if (!pl.pairs.empty()) {
@@ -1123,7 +1124,7 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
   if (cfg.quant_variant != KRILL_QUANT_F32 && cfg.quant_variant != KRILL_QUANT_INPUT_DTYPE)
     return fail(KRILL_ERR_INVALID, "bad quant_variant");
   if (cfg.attn_impl != KRILL_ATTN_TENSOR_CORE && cfg.attn_impl != KRILL_ATTN_CUDA_CORE &&
-      cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_SYNC && cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_1SM)
+      cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_SYNC && cfg.attn_impl != KRILL_ATTN_TENSOR_CORE_PAIR)
     return fail(KRILL_ERR_INVALID, "bad attn_impl");
   if (cfg.split_tokens < 0 || cfg.split_tokens % 64 != 0)
     return fail(KRILL_ERR_INVALID, "split_tokens must be 0 (adaptive) or a multiple of 64");
@@ -1176,7 +1177,7 @@ krill_status_t krill_pool_create(const krill_pool_cfg* cfg_in, int32_t device, k
     // under lazy loading) at pool creation rather than inside a decode call.
     if (e == cudaSuccess) e = krill::noalloc_prepare(device);
     // CTA pairs of the cascade kernel that fit at once (0: single-CTA cascade)
-    if (e == cudaSuccess && cfg.attn_impl == KRILL_ATTN_TENSOR_CORE &&
+    if (e == cudaSuccess && cfg.attn_impl == KRILL_ATTN_TENSOR_CORE_PAIR &&
         shared_uses_umma(p->geom, cfg.attn_impl))
       p->pair_slots = std::min(krill::shared_pair_capacity(p->geom), p->num_sms / 2);
     if (e != cudaSuccess) {

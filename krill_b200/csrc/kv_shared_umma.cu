@@ -1333,7 +1333,7 @@ int pair_capacity() {
 }  // namespace
 
 bool shared_uses_umma(const Geom& g, int impl) {
-  return (impl == KRILL_ATTN_TENSOR_CORE || impl == KRILL_ATTN_TENSOR_CORE_1SM) && g.D <= 128;
+  return (impl == KRILL_ATTN_TENSOR_CORE || impl == KRILL_ATTN_TENSOR_CORE_PAIR) && g.D <= 128;
 }
 
 int shared_pair_capacity(const Geom& g) {

@@ -170,23 +170,28 @@ PAIR = "attn_shared_pair_kernel"
     (128, 128, 16, 16, F16, 1 / math.sqrt(128), 150),  # G = D, MHA: items of 150 rows
 ])
 def test_cascade_cta_pairs(D, G, hq, hkv, dtype, scale, forks):
-    # items of more than 128 query rows run on CTA pairs (tcgen05 cta_group::2,
-    # M = 256 per instruction, each CTA dequantizing half of every sub-block)
+    # KRILL_ATTN_TENSOR_CORE_PAIR: items of more than 128 query rows run on CTA
+    # pairs (tcgen05 cta_group::2, M = 256 per instruction, each CTA
+    # dequantizing half of every sub-block)
     run_cascade(D, G, hq, hkv, dtype, [(1024, [1 + (i * 37) % 300 for i in range(forks)])], scale,
-                expect_kernel=PAIR)
+                impl=kb.ATTN_TENSOR_CORE_PAIR, expect_kernel=PAIR)
 
 
-def test_cascade_cta_pairs_outliers_and_fragments():
+def test_cascade_cta_pairs_outliers_fragments_and_rows():
     # scales above 64 (exact two-rounding dequant) on the pair kernel; a
-    # 4096-token prefix over 4 layers cut into several fragments per (layer, head)
+    # 4096-token prefix over 4 layers cut into several fragments per (layer,
+    # head); 70 forks x GQA 4 = 280 rows: one item of 256 rows and one of 24
+    # (the second CTA of that pair has no rows of its own)
+    pair = kb.ATTN_TENSOR_CORE_PAIR
     run_cascade(128, 64, 32, 4, BF16, [(1024, [10 + 3 * i for i in range(40)])], 1 / math.sqrt(128),
-                outliers=True, layers=1, expect_kernel=PAIR)
+                outliers=True, layers=1, impl=pair, expect_kernel=PAIR)
     run_cascade(128, 64, 32, 8, BF16, [(4096, [1 + 5 * i for i in range(48)])], 1 / math.sqrt(128),
-                layers=4, steps=1, min_slots=2, expect_kernel=PAIR)
+                layers=4, steps=1, min_slots=2, impl=pair, expect_kernel=PAIR)
+    run_cascade(128, 64, 32, 8, BF16, [(512, [3 + (i % 7) for i in range(70)])], 1 / math.sqrt(128),
+                layers=1, steps=1, impl=pair, expect_kernel=PAIR)
 
 
-def test_cascade_single_cta_variant():
-    # the same many-row items on one CTA per item (KRILL_ATTN_TENSOR_CORE_1SM)
+def test_cascade_single_cta_by_default():
+    # the default tensor-core path keeps one CTA per item at any row count
     run_cascade(128, 64, 32, 8, BF16, [(1024, [1 + (i * 37) % 300 for i in range(64)])],
-                1 / math.sqrt(128), impl=kb.ATTN_TENSOR_CORE_1SM,
-                expect_kernel="attn_shared_umma_kernel")
+                1 / math.sqrt(128), layers=1, steps=1, expect_kernel="attn_shared_umma_kernel")

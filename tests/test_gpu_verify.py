@@ -69,19 +69,21 @@ def test_verify_matches_sequential_oracle(D, G, hq, hkv, dtype, nq):
     pool.close()
 
 
-@pytest.mark.parametrize("D,G,hq,hkv,dtype,prefix,chunk", [
-    (128, 64, 32, 8, BF16, 1000, 300),   # 1200 query rows: causal tcgen05 items
-    (64, 64, 32, 8, F16, 77, 130),
-    (128, 128, 16, 16, F16, 500, 64),    # MHA, G = D
+@pytest.mark.parametrize("D,G,hq,hkv,dtype,prefix,chunk,impl", [
+    (128, 64, 32, 8, BF16, 1000, 300, kb.ATTN_TENSOR_CORE),   # 1200 query rows: causal tcgen05 items
+    (64, 64, 32, 8, F16, 77, 130, kb.ATTN_TENSOR_CORE),
+    (128, 128, 16, 16, F16, 500, 64, kb.ATTN_TENSOR_CORE),    # MHA, G = D
+    (128, 64, 32, 8, BF16, 1000, 300, kb.ATTN_TENSOR_CORE_PAIR),  # the same on CTA pairs
+    (64, 64, 32, 8, F16, 77, 130, kb.ATTN_TENSOR_CORE_PAIR),
 ])
-def test_prefill_attention_matches_oracle(D, G, hq, hkv, dtype, prefix, chunk):
+def test_prefill_attention_matches_oracle(D, G, hq, hkv, dtype, prefix, chunk, impl):
     """Chunked prefill (InferenceEngine.swift:3122-3147): append the chunk's
     K/V, then every chunk query attends the cache causally. Checked against
     the oracle at a spread of queries (first, last and every 13th)."""
     rng = np.random.default_rng(13)
     layers = 2
     scale = 1 / math.sqrt(D)
-    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=48, group_size=G)
+    pool = kb.KVPool(layers, hkv, hq, D, num_blocks=48, group_size=G, attn_impl=impl)
     seqs, K, V = [], [], []
     for L in (prefix, prefix // 3 + 1):
         s = pool.create_sequence()
@@ -97,9 +99,8 @@ def test_prefill_attention_matches_oracle(D, G, hq, hkv, dtype, prefix, chunk):
     kb.prefill_attention(pool, seqs, 0, dev_bits(qb, dtype), out, scale)
     torch.cuda.synchronize()
     assert pool.device_error() == 0
-    # query blocks of more than 128 rows run on the CTA-pair cascade kernel
-    if chunk * (hq // hkv) > 128:
-        assert "attn_shared_pair_kernel" in pool.last_kernels(), pool.last_kernels()
+    assert ("attn_shared_pair_kernel" in pool.last_kernels()) == (
+        impl == kb.ATTN_TENSOR_CORE_PAIR and chunk * (hq // hkv) > 128), pool.last_kernels()
     got = out.cpu().numpy().astype(np.float64)
     check_q = sorted(set(list(range(0, chunk, 13)) + [chunk - 1]))
     for i in range(n):
