@@ -1005,6 +1005,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layer-sample", type=int, default=12)
     ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (profiling)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (profiling captures on a smaller pool)")
     ap.add_argument("--diag", action="store_true",
                     help="per-rank, per-step kernel times and device error flags on stderr")
     args = ap.parse_args()
@@ -1014,6 +1016,8 @@ def main():
     cfg = dict(CONFIGS[args.config])
     if args.seqs:
         cfg["seqs"] = args.seqs
+    if args.layers:
+        cfg["layers"] = args.layers
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
