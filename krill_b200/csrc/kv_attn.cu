@@ -1257,7 +1257,8 @@ void describe_attention(const Geom& g, const AttnParams& p, int grid, int impl, 
     if (p.split_ctr != nullptr && p.n_split_units > 0 && impl != 1)
       put(snprintf(buf + n, cap - n, "[merge in kernel]"));
   }
-  if (attn_needs_combine(p, grid, impl)) put(snprintf(buf + n, cap - n, "+attn_combine_kernel<%d>", g.D));
+  if (attn_needs_combine(p, grid, impl))
+    put(snprintf(buf + n, cap - n, "%sattn_combine_kernel<%d>", n > 0 && buf[n - 1] != '+' ? "+" : "", g.D));
   if (n > 0 && buf[n - 1] == '+') buf[--n] = 0;
 }
 
