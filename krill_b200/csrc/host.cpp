@@ -634,8 +634,17 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   // With n_query > 1 (speculative verify) the last n_query tokens of each
   // sequence are the queries: query j sees the cache up to and including its
   // own token and none of the later drafts (buildBatchedVerifyMask,
-  // BatchedDecode.swift:299-312), i.e. one unit per query with its own bound.
-  const int64_t n_units = (int64_t)lc * n_seqs * n_query;
+  // BatchedDecode.swift:299-312). On the int8 tensor-core decode kernel up to
+  // 8 / g consecutive queries share one unit as further columns of its query
+  // tile, each column masked at its own query's bound (AttnUnit::nq), so the
+  // cache is read once per unit instead of once per query; otherwise (and on
+  // the causal cascade path) one unit per query.
+  const int fold = (n_query > 1 && !causal_path && g.fmt == kFmtInt8 &&
+                    p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE)
+                       ? std::max(1, std::min(n_query, 8 / g.g))
+                       : 1;
+  const int q_units = (n_query + fold - 1) / fold;  // units per (layer, sequence)
+  const int64_t n_units = (int64_t)lc * n_seqs * q_units;
   pl.units.resize((size_t)n_units);
   pl.nsb.resize((size_t)n_units);
   int64_t total_sb = 0;
@@ -648,17 +657,19 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
       if (len < n_query)
         return fail(KRILL_ERR_INVALID, "%d queries need their tokens in the cache (layer %d holds %lld)",
                     n_query, L, (long long)len);
-      for (int j = 0; j < n_query; ++j) {
-        const int64_t t_hi = len - n_query + 1 + j;
+      for (int k = 0; k < q_units; ++k) {
+        const int j0 = k * fold, nq = std::min(fold, n_query - j0);  // queries j0 .. j0 + nq - 1
+        const int64_t t_hi = len - n_query + j0 + nq;                // the last one's bound
         const int64_t t_lo = p->windowed() ? len - std::min<int64_t>(s.ret[L], p->cfg.window) : 0;
-        const int64_t ui = ((int64_t)li * n_seqs + si) * n_query + j;
+        const int64_t ui = ((int64_t)li * n_seqs + si) * q_units + k;
         AttnUnit& u = pl.units[ui];
-        u.qo_row = (int32_t)ui;
+        u.qo_row = (int32_t)(((int64_t)li * n_seqs + si) * n_query + j0);
         u.si = si;
         u.layer = L;
         u.t_lo = (int32_t)t_lo;
         u.t_hi = (int32_t)t_hi;
         u.n_pre = 0;
+        u.nq = nq;
         pl.nsb[ui] = causal_path ? 0
                                  : (t_hi + g.subt - 1) / g.subt -
                                        std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);

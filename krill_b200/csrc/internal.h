@@ -55,7 +55,18 @@ struct AttnUnit {
                         // kernel: with n_split == 1 merged by the decode item that
                         // finishes; with n_split > 1 the first n_pre of the n_split
                         // records (the decode pieces arrive as the other n_split - n_pre)
+  int32_t nq;           // consecutive queries of one sequence held as columns of the
+                        // query tile (multi-query verify; 0 or 1: one query). Column
+                        // c is query c / g (row qo_row + c / g), kv-group head c % g,
+                        // and sees positions below t_hi - (nq - 1 - c / g)
 };
+
+// Columns of a unit's query tile (at most 8) and the element offset of column
+// c in q / out relative to the unit's first row and head group.
+__host__ __device__ inline int unit_cols(const AttnUnit& u, int g) { return g * (u.nq > 1 ? u.nq : 1); }
+__host__ __device__ inline int64_t col_off(int c, int g, int64_t row_elems, int D) {
+  return (int64_t)(c / g) * row_elems + (int64_t)(c % g) * D;
+}
 
 struct AttnItem {
   int32_t unit;

@@ -110,13 +110,16 @@ struct QRaw {
   uint4 w[D / 64][2];
 };
 
+// Column r = lane / 4 of the tile (see AttnUnit::nq): query r / g, head r % g.
 template <int D>
-__device__ __forceinline__ void fetch_q(QRaw<D>& qr, const void* q, int64_t row_elem, int g, int lane) {
+__device__ __forceinline__ void fetch_q(QRaw<D>& qr, const void* q, int64_t row_elem, int g, int cols,
+                                        int64_t row_elems, int lane) {
   const int r = lane >> 2, tig = lane & 3;
+  const int64_t cbase = row_elem + col_off(r, g, row_elems, D);
 #pragma unroll
   for (int hh = 0; hh < D / 64; ++hh) {
-    if (r < g) {
-      const int64_t e = row_elem + (int64_t)r * D + 16 * (tig + 4 * hh);
+    if (r < cols) {
+      const int64_t e = cbase + 16 * (tig + 4 * hh);
       const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q) + e);
       qr.w[hh][0] = __ldg(p);
       qr.w[hh][1] = __ldg(p + 1);
@@ -158,11 +161,12 @@ __device__ __forceinline__ void reset_state(TCState<D>& st) {
 
 // Process one 64-token sub-block resident in shared memory at `sb`.
 // pos0 = absolute position of its token 0; tokens outside [t_lo, t_hi) are
-// masked (only checked when `boundary`).
+// masked (only checked when `boundary`), and for this lane's two query
+// columns 2*tig and 2*tig + 1 also those at or past th0 / th1 (<= t_hi).
 template <int D, int NG, bool FAST>
 __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCState<D>& st,
                                             int lane, float scale_log2, bool boundary, int pos0,
-                                            int t_lo, int t_hi) {
+                                            int t_lo, int t_hi, int th0, int th1) {
   using SG = SubGeom<D, NG>;
   constexpr bool SWZ = D >= 128;
   const int r = lane >> 2, tig = lane & 3;
@@ -213,10 +217,12 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) s[u][c] = acc[c] * scale_log2;
-    if (boundary) {
+    if (boundary) {  // fragment: [0] (ta, col 2tig), [1] (ta, 2tig+1), [2] (tb, 2tig), [3] (tb, 2tig+1)
       const int pa = pos0 + ta, pb = pos0 + tb;
-      if (pa < t_lo || pa >= t_hi) s[u][0] = s[u][1] = -INFINITY;
-      if (pb < t_lo || pb >= t_hi) s[u][2] = s[u][3] = -INFINITY;
+      if (pa < t_lo || pa >= th0) s[u][0] = -INFINITY;
+      if (pa < t_lo || pa >= th1) s[u][1] = -INFINITY;
+      if (pb < t_lo || pb >= th0) s[u][2] = -INFINITY;
+      if (pb < t_lo || pb >= th1) s[u][3] = -INFINITY;
     }
   }
 
@@ -469,12 +475,13 @@ constexpr int stages_for() {
 // Records written by other CTAs are read through L2 (ld.global.cg).
 template <int D>
 __device__ __forceinline__ void merge_split(const AttnParams& p, const AttnUnit& un, int h, int lane) {
-  const int g = p.g, n = un.n_split;
+  const int g = p.g, n = un.n_split, cols = unit_cols(un, g);
+  const int64_t row_elems = (int64_t)p.Hq * D;
   const int64_t stride = (int64_t)p.Hkv * partial_floats(D);
   const float* base = p.partials + ((int64_t)un.first_split * p.Hkv + h) * partial_floats(D);
   // lane j < g: max and normalizer of query head j
   float M = -INFINITY, Ls = 0.f;
-  if (lane < g) {
+  if (lane < cols) {
 #pragma unroll 8
     for (int i = 0; i < n; ++i) M = fmaxf(M, __ldcg(base + i * stride + lane));
 #pragma unroll 8
@@ -493,11 +500,11 @@ __device__ __forceinline__ void merge_split(const AttnParams& p, const AttnUnit&
 #pragma unroll 2
   for (int i = 0; i < n; ++i) {
     const float* ri = base + i * stride;
-    const float mj = lane < g ? __ldcg(ri + lane) : -INFINITY;
+    const float mj = lane < cols ? __ldcg(ri + lane) : -INFINITY;
     const float wj = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
 #pragma unroll
     for (int hq = 0; hq < 8; ++hq) {
-      if (hq < g) {
+      if (hq < cols) {
         const float mh = __shfl_sync(0xffffffffu, mj, hq);
         const float wh = __shfl_sync(0xffffffffu, wj, hq);
 #pragma unroll
@@ -511,10 +518,11 @@ __device__ __forceinline__ void merge_split(const AttnParams& p, const AttnUnit&
   const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
 #pragma unroll
   for (int hq = 0; hq < 8; ++hq) {
-    if (hq < g) {
+    if (hq < cols) {
       const float ih = __shfl_sync(0xffffffffu, inv, hq);
 #pragma unroll
-      for (int c = 0; c < NC; ++c) store_out(p.out, p.out_dtype, orow + hq * D + lane + 32 * c, acc[hq][c] * ih);
+      for (int c = 0; c < NC; ++c)
+        store_out(p.out, p.out_dtype, orow + col_off(hq, g, row_elems, D) + lane + 32 * c, acc[hq][c] * ih);
     }
   }
 }
@@ -559,6 +567,7 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
   const int Hkv = p.Hkv;
   const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
   const int h0 = 2 * tig, h1 = 2 * tig + 1;
+  const int cols = unit_cols(un, g);
   if (un.n_split == 1) {
     if (un.n_pre > 0) {
       // merge the shared-prefix records the cascade kernel completed earlier
@@ -603,7 +612,7 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
         }
         const float b0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
         const float b1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
-        const bool t0 = b0 != 0.f && h0 < g, t1 = b1 != 0.f && h1 < g;
+        const bool t0 = b0 != 0.f && h0 < cols, t1 = b1 != 0.f && h1 < cols;
         l0 = t0 ? l0 + lv0 * b0 : l0;
         l1 = t1 ? l1 + lv1 * b1 : l1;
 #pragma unroll
@@ -616,16 +625,18 @@ __device__ __forceinline__ void finish_head(const AttnParams& p, TCState<D>& st,
       }
     }
     const float i0 = 1.f / l0, i1 = 1.f / l1;
+    const int64_t row_elems = (int64_t)p.Hq * D;
+    const int64_t o0 = orow + col_off(h0, g, row_elems, D), o1 = orow + col_off(h1, g, row_elems, D);
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
       const int d = 16 * mt + r;
-      if (h0 < g) {
-        store_out(p.out, p.out_dtype, orow + h0 * D + d, st.o[mt][0] * i0);
-        store_out(p.out, p.out_dtype, orow + h0 * D + d + 8, st.o[mt][2] * i0);
+      if (h0 < cols) {
+        store_out(p.out, p.out_dtype, o0 + d, st.o[mt][0] * i0);
+        store_out(p.out, p.out_dtype, o0 + d + 8, st.o[mt][2] * i0);
       }
-      if (h1 < g) {
-        store_out(p.out, p.out_dtype, orow + h1 * D + d, st.o[mt][1] * i1);
-        store_out(p.out, p.out_dtype, orow + h1 * D + d + 8, st.o[mt][3] * i1);
+      if (h1 < cols) {
+        store_out(p.out, p.out_dtype, o1 + d, st.o[mt][1] * i1);
+        store_out(p.out, p.out_dtype, o1 + d + 8, st.o[mt][3] * i1);
       }
     }
     return;
@@ -660,8 +671,10 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
   const int64_t stride = (int64_t)Hkv * partial_floats(D);
   // (loops unrolled so that several records' loads are in flight; the sums
   // keep record order)
+  const int cols = unit_cols(un, g);
+  const int64_t row_elems = (int64_t)p.Hq * D;
   __shared__ float sm[8], sinv[8];
-  if (threadIdx.x < g) {
+  if (threadIdx.x < cols) {
     const int hq = threadIdx.x;
     float M = -INFINITY;
 #pragma unroll 8
@@ -678,7 +691,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
   }
   __syncthreads();
   const int64_t orow = ((int64_t)un.qo_row * p.Hq + (int64_t)h * g) * D;
-  for (int idx = threadIdx.x; idx < g * D; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < cols * D; idx += blockDim.x) {
     const int hq = idx / D, d = idx - hq * D;
     const float M = sm[hq];
     float Os = 0.f;
@@ -688,7 +701,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
       const float oi = base[i * stride + 16 + hq * D + d];
       Os = (mi != -INFINITY) ? Os + oi * exp2f(mi - M) : Os;
     }
-    store_out(p.out, p.out_dtype, orow + idx, Os * sinv[hq]);
+    store_out(p.out, p.out_dtype, orow + col_off(hq, g, row_elems, D) + d, Os * sinv[hq]);
   }
 }
 
@@ -731,10 +744,12 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   auto q_row = [&](const AttnUnit& u, int hh) {
     return ((int64_t)u.qo_row * p.Hq + (int64_t)hh * p.g) * D;
   };
+  const int64_t q_row_elems = (int64_t)p.Hq * D;
   if (it0 < it1) {
     item_next = p.items[it0];
     un_next = p.units[item_next.unit];
-    fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, lane);
+    fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
+                   q_row_elems, lane);
   }
   for (int it = it0; it < it1; ++it) {
     const AttnItem item = item_next;
@@ -749,7 +764,7 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
       int pf = 0;
       auto prefetch_step = [&]() {
         if (rd + 1 < rounds) {  // next round: same unit, the next head group
-          fetch_q<D>(qr, p.q, q_row(un, h + HPR), p.g, lane);
+          fetch_q<D>(qr, p.q, q_row(un, h + HPR), p.g, unit_cols(un, p.g), q_row_elems, lane);
           pf = 2;
         } else if (it + 1 >= it1) {
           pf = 2;
@@ -757,10 +772,15 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
           un_next = p.units[item_next.unit];
           pf = 1;
         } else {
-          fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, lane);
+          fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
+                   q_row_elems, lane);
           pf = 2;
         }
       };
+      // per-column bounds of a multi-query unit (AttnUnit::nq)
+      const int nq = un.nq > 1 ? un.nq : 1;
+      const int th0 = un.t_hi - (nq - 1 - (2 * (lane & 3)) / p.g);
+      const int th1 = un.t_hi - (nq - 1 - (2 * (lane & 3) + 1) / p.g);
       for (int k = rr; k < n_sb; k += R) {
         const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
@@ -769,12 +789,13 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
         const int j = item.sb_begin + k;
         constexpr int T = SubGeom<D, NG, FMT>::T;
         const int pos0 = j * T;
-        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi;
+        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi - (nq - 1);
         const uint8_t* sbp = stages + (size_t)stage * SB;
         if constexpr (FMT == kFmtBf16)
           tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
         else
-          tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
+          tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi, th0,
+                                   th1);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
         if (pf < 2) prefetch_step();
