@@ -112,7 +112,8 @@ __global__ void or_flag_kernel(int* dst, const int* src) { *dst |= *src; }
 struct Plan {
   std::vector<Seq*> sv;
   std::vector<AttnUnit> units;
-  std::vector<AttnItem> items;
+  std::vector<AttnItem> items, items_tmp;
+  std::vector<size_t> run_start, run_cur;
   std::vector<int64_t> bucket;
   std::vector<int32_t> order, owner, count, fill;
   std::vector<uint64_t> heap;
@@ -870,6 +871,35 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
                                     (int16_t)(u.n_split == 1 ? 0 : off + i), (int16_t)h0});
       b += sz;
     }
+  }
+  if (q_units > 1 && !causal_path) {
+    // The units of one (layer, sequence) in a multi-query call read the same
+    // blocks: interleave their items (piece by piece) so that the assignment
+    // below, stable for equal sizes, hands matching pieces to CTAs side by
+    // side, and the second read of each sub-block is served from L2.
+    pl.items_tmp.clear();
+    pl.items_tmp.reserve(pl.items.size());
+    size_t a = 0;
+    while (a < pl.items.size()) {
+      const int32_t grp = pl.items[a].unit / q_units;
+      size_t b = a;
+      while (b < pl.items.size() && pl.items[b].unit / q_units == grp) ++b;
+      // [a, b) holds the group's units, each a contiguous run, in unit order
+      pl.run_start.clear();
+      for (size_t i = a; i < b; ++i)
+        if (i == a || pl.items[i].unit != pl.items[i - 1].unit) pl.run_start.push_back(i);
+      const size_t nr = pl.run_start.size();
+      pl.run_start.push_back(b);
+      pl.run_cur.assign(pl.run_start.begin(), pl.run_start.end() - 1);
+      for (size_t left = b - a; left > 0;)
+        for (size_t r = 0; r < nr; ++r)
+          if (pl.run_cur[r] < pl.run_start[r + 1]) {
+            pl.items_tmp.push_back(pl.items[pl.run_cur[r]++]);
+            --left;
+          }
+      a = b;
+    }
+    pl.items.swap(pl.items_tmp);
   }
   if (!p->host_only) TRY(ensure_scratch(p, split_count * g.Hkv, 0));
   // ---- longest-processing-time assignment of items to persistent CTAs ----
