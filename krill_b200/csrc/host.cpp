@@ -645,6 +645,13 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
                        ? std::max(1, std::min(n_query, 8 / g.g))
                        : 1;
   const int q_units = (n_query + fold - 1) / fold;  // units per (layer, sequence)
+  // Two units per sequence on a decode kernel with one warp per kv head:
+  // the second unit (the shadow) becomes the second 8-column query tile of
+  // the first one's items, so each sub-block is staged once for both; the
+  // shadow keeps its own queries, bounds and partial records, and has no
+  // items of its own.
+  const bool qt2 = q_units == 2 && !causal_path && g.fmt == kFmtInt8 && g.D <= 128 &&
+                   g.Hkv >= 8 && p->cfg.attn_impl != KRILL_ATTN_CUDA_CORE;
   const int64_t n_units = (int64_t)lc * n_seqs * q_units;
   pl.units.resize((size_t)n_units);
   pl.nsb.resize((size_t)n_units);
@@ -675,6 +682,10 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
                                  : (t_hi + g.subt - 1) / g.subt -
                                        std::max<int64_t>(t_lo / g.subt, pl.seq_sh[si]);
         total_sb += pl.nsb[ui];
+        if (qt2 && k == 1) {  // the shadow's range is the pair's: its items cover both
+          total_sb -= pl.nsb[ui - 1];
+          pl.nsb[ui - 1] = pl.nsb[ui];
+        }
       }
     }
   }
@@ -688,8 +699,8 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   bool latency_bound = false;
   if (p->cfg.split_tokens > 0) {
     C = std::max(1, p->cfg.split_tokens / g.subt);
-  } else if ((latency_bound = (int64_t)8 * g.Hkv >
-                               std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4))) {
+  } else if ((latency_bound = !qt2 && (int64_t)8 * g.Hkv >
+                                          std::max<int64_t>(1, total_sb * g.Hkv / p->num_sms / 4))) {
     // Small batch (8-sub-block items of all kv heads would exceed a quarter of
     // a CTA's share): the step is latency-bound, and its time is about the
     // largest item plus, where a sequence is split over CTAs, the merge of
@@ -863,6 +874,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
         pl.split_units.push_back((int32_t)ui);
       }
     }
+    if (qt2 && (ui % 2) == 1) continue;  // a shadow: tile 2 of the previous unit's items
     int64_t b = std::max<int64_t>(u.t_lo / g.subt, sh_sb);
     for (int64_t i = 0; i < n_it; ++i) {
       const int64_t sz = base + (i < extra ? 1 : 0);
@@ -1011,6 +1023,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
     static unsigned long long ctr_tag;
     AttnParams dp{};
     dp.hg = HG;
+    dp.qt = qt2 ? 2 : 1;
     dp.g = g.g;
     dp.n_split_units = (int)pl.split_units.size();
     dp.split_ctr = merge_in_kernel ? &ctr_tag : nullptr;
@@ -1035,6 +1048,7 @@ krill_status_t do_attention(krill_pool_t p, int32_t n_seqs, const krill_seq_t* s
   ap.bt = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes);
   ap.bt_stride = (int)bt_stride;
   ap.hg = HG;
+  ap.qt = qt2 ? 2 : 1;
   ap.split_units = reinterpret_cast<const int32_t*>(slot->d + units_bytes + items_bytes + off_bytes + bt_bytes);
   ap.n_split_units = (int)pl.split_units.size();
   ap.q = q;

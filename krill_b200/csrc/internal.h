@@ -108,6 +108,8 @@ struct AttnParams {
   int64_t page_bytes, sb_bytes;
   int L, Hkv, Hq, g, ring;
   int hg;                  // kv heads per item (divides Hkv)
+  int qt;                  // query tiles per unit: 1, or 2 (each unit followed by its
+                           // shadow unit, AttnUnit::nq; int8, head_dim <= 128, hg = 8)
   const AttnUnit* units;
   const AttnItem* items;
   const int32_t* cta_off;  // [grid + 1] item ranges per CTA

@@ -159,14 +159,17 @@ __device__ __forceinline__ void reset_state(TCState<D>& st) {
   st.l[0] = st.l[1] = 0.f;
 }
 
-// Process one 64-token sub-block resident in shared memory at `sb`.
-// pos0 = absolute position of its token 0; tokens outside [t_lo, t_hi) are
-// masked (only checked when `boundary`), and for this lane's two query
-// columns 2*tig and 2*tig + 1 also those at or past th0 / th1 (<= t_hi).
-template <int D, int NG, bool FAST>
-__device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCState<D>& st,
+// Process one 64-token sub-block resident in shared memory at `sb` for QT
+// query tiles of 8 columns (st[q]; QT = 2 for multi-query units of more than
+// 8 columns): each K and V fragment is dequantized once and feeds the MMAs of
+// every tile. pos0 = absolute position of its token 0; tokens outside
+// [t_lo, t_hi) are masked (only checked when `boundary`), and for this lane's
+// two columns 2*tig and 2*tig + 1 of tile q also those at or past th[q][0] /
+// th[q][1] (<= t_hi).
+template <int D, int NG, bool FAST, int QT>
+__device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCState<D> (&st)[QT],
                                             int lane, float scale_log2, bool boundary, int pos0,
-                                            int t_lo, int t_hi, int th0, int th1) {
+                                            int t_lo, int t_hi, const int (&th)[QT][2]) {
   using SG = SubGeom<D, NG>;
   constexpr bool SWZ = D >= 128;
   const int r = lane >> 2, tig = lane & 3;
@@ -177,13 +180,15 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
   // plus 2: after movmatrix.trans this is exactly the token order of the V
   // fragments, where lane tig holds tokens TPT*tig + 4u + 0..3.
   constexpr int NU = SG::NU, TPT = SG::TPT;
-  float s[NU][4];
+  float s[QT][NU][4];
 #pragma unroll
   for (int u = 0; u < NU; ++u) {
     const int tbase = TPT * (r >> 1) + 4 * u;
     const int ta = tbase + (r & 1);
     const int tb = ta + 2;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[QT][4];
+#pragma unroll
+    for (int q = 0; q < QT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
 #pragma unroll
     for (int hh = 0; hh < D / 64; ++hh) {
       const int grp = (64 * hh) / SG::G;
@@ -212,57 +217,65 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
           a2 = deq2(wav[k], 0x4342u, sA, zA);
           a3 = deq2(wbv[k], 0x4342u, sB, zB);
         }
-        mma16816(acc, a0, a1, a2, a3, st.qf[hh][2 * k], st.qf[hh][2 * k + 1]);
+#pragma unroll
+        for (int q = 0; q < QT; ++q)
+          mma16816(acc[q], a0, a1, a2, a3, st[q].qf[hh][2 * k], st[q].qf[hh][2 * k + 1]);
       }
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) s[u][c] = acc[c] * scale_log2;
-    if (boundary) {  // fragment: [0] (ta, col 2tig), [1] (ta, 2tig+1), [2] (tb, 2tig), [3] (tb, 2tig+1)
-      const int pa = pos0 + ta, pb = pos0 + tb;
-      if (pa < t_lo || pa >= th0) s[u][0] = -INFINITY;
-      if (pa < t_lo || pa >= th1) s[u][1] = -INFINITY;
-      if (pb < t_lo || pb >= th0) s[u][2] = -INFINITY;
-      if (pb < t_lo || pb >= th1) s[u][3] = -INFINITY;
+    for (int q = 0; q < QT; ++q) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[q][u][c] = acc[q][c] * scale_log2;
+      if (boundary) {  // fragment: [0] (ta, col 2tig), [1] (ta, 2tig+1), [2] (tb, 2tig), [3] (tb, 2tig+1)
+        const int pa = pos0 + ta, pb = pos0 + tb;
+        if (pa < t_lo || pa >= th[q][0]) s[q][u][0] = -INFINITY;
+        if (pa < t_lo || pa >= th[q][1]) s[q][u][1] = -INFINITY;
+        if (pb < t_lo || pb >= th[q][0]) s[q][u][2] = -INFINITY;
+        if (pb < t_lo || pb >= th[q][1]) s[q][u][3] = -INFINITY;
+      }
     }
   }
 
-  // ---- online softmax (heads 2*tig, 2*tig+1 live in this lane) ----
-  float mx0 = -INFINITY, mx1 = -INFINITY;
+  // ---- online softmax per tile (heads 2*tig, 2*tig+1 live in this lane) ----
+  uint32_t pb[QT][NU][2];
 #pragma unroll
-  for (int u = 0; u < NU; ++u) {
-    mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
-    mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
-  }
+  for (int q = 0; q < QT; ++q) {
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-  }
-  const float mn0 = fmaxf(st.m[0], mx0), mn1 = fmaxf(st.m[1], mx1);
-  const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
-  const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
-  const float al0 = exp2f(st.m[0] - b0), al1 = exp2f(st.m[1] - b1);
-  st.m[0] = mn0;
-  st.m[1] = mn1;
-  float ps0 = 0.f, ps1 = 0.f;
-  uint32_t pb[NU][2];
+    for (int u = 0; u < NU; ++u) {
+      mx0 = fmaxf(mx0, fmaxf(s[q][u][0], s[q][u][2]));
+      mx1 = fmaxf(mx1, fmaxf(s[q][u][1], s[q][u][3]));
+    }
 #pragma unroll
-  for (int u = 0; u < NU; ++u) {
-    const float p0 = exp2f(s[u][0] - b0), p1 = exp2f(s[u][1] - b1);
-    const float p2 = exp2f(s[u][2] - b0), p3 = exp2f(s[u][3] - b1);
-    ps0 += p0 + p2;
-    ps1 += p1 + p3;
-    pb[u][0] = movm_trans(f2h2(p0, p1));
-    pb[u][1] = movm_trans(f2h2(p2, p3));
-  }
-  st.l[0] = st.l[0] * al0 + ps0;
-  st.l[1] = st.l[1] * al1 + ps1;
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(st[q].m[0], mx0), mn1 = fmaxf(st[q].m[1], mx1);
+    const float b0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = exp2f(st[q].m[0] - b0), al1 = exp2f(st[q].m[1] - b1);
+    st[q].m[0] = mn0;
+    st[q].m[1] = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-  for (int mt = 0; mt < D / 16; ++mt) {
-    st.o[mt][0] *= al0;
-    st.o[mt][1] *= al1;
-    st.o[mt][2] *= al0;
-    st.o[mt][3] *= al1;
+    for (int u = 0; u < NU; ++u) {
+      const float p0 = exp2f(s[q][u][0] - b0), p1 = exp2f(s[q][u][1] - b1);
+      const float p2 = exp2f(s[q][u][2] - b0), p3 = exp2f(s[q][u][3] - b1);
+      ps0 += p0 + p2;
+      ps1 += p1 + p3;
+      pb[q][u][0] = movm_trans(f2h2(p0, p1));
+      pb[q][u][1] = movm_trans(f2h2(p2, p3));
+    }
+    st[q].l[0] = st[q].l[0] * al0 + ps0;
+    st[q].l[1] = st[q].l[1] * al1 + ps1;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      st[q].o[mt][0] *= al0;
+      st[q].o[mt][1] *= al1;
+      st[q].o[mt][2] *= al0;
+      st[q].o[mt][3] *= al1;
+    }
   }
 
   // ---- V phase: Oᵀ += Vdeqᵀ · Pᵀ ----
@@ -324,7 +337,8 @@ __device__ __forceinline__ void tc_subblock(const uint8_t* __restrict__ sb, TCSt
           a2 = deq2(xv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
           a3 = deq2(yv[u], 0x4342u, vs[2 * u + 1], vz[2 * u + 1]);
         }
-        mma16816(st.o[mt], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+#pragma unroll
+        for (int q = 0; q < QT; ++q) mma16816(st[q].o[mt], a0, a1, a2, a3, pb[q][u][0], pb[q][u][1]);
       }
     }
   }
@@ -723,7 +737,11 @@ constexpr int kConsumerRegs = 224;
 // exact only while every scale in the pool is below 64 in magnitude; the
 // kernel picks one specialization per launch from the pool's large-scale flag
 // (set by the kernels that store scales), so the hot loop carries one path.
-template <int D, int NG, int NCW, int R, int NSTAGE, int FMT, bool FAST>
+// QT = 2: every unit of the launch is the first 8 columns of a multi-query
+// unit whose other columns are the next unit (AttnUnit::nq; its shadow, with
+// the same sequence, layer and pieces, but its own queries, bounds and
+// records); both tiles are computed from each staged sub-block.
+template <int D, int NG, int NCW, int R, int NSTAGE, int FMT, bool FAST, int QT>
 __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem, uint8_t* stages,
                                              uint32_t bar_base, volatile int* cta_abort,
                                              volatile uint32_t* tags, int warp, int lane, int it0,
@@ -731,8 +749,10 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
   constexpr int SB = SM::SB;
   constexpr int HPR = NCW / R;
+  static_assert(QT == 1 || (R == 1 && FMT == kFmtInt8), "two query tiles: one warp per head, int8");
   const int hr = warp / R, rr = warp % R;
-  TCState<D> st;
+  TCState<D> sts[QT];
+  TCState<D>& st = sts[0];
   uint32_t J = 0;
   AttnItem item_next{};
   AttnUnit un_next{};
@@ -760,6 +780,15 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
       const int h = item.h0 + rd * HPR + hr;
       reset_state(st);
       set_q<D, FMT>(st, qr, p.q_dtype);
+      // the shadow unit's queries (second tile), fetched here: items are long
+      AttnUnit un2 = un;
+      if constexpr (QT == 2) {
+        un2 = p.units[item.unit + 1];
+        QRaw<D> qr2;
+        fetch_q<D>(qr2, p.q, q_row(un2, h), p.g, unit_cols(un2, p.g), q_row_elems, lane);
+        reset_state(sts[1]);
+        set_q<D, FMT>(sts[1], qr2, p.q_dtype);
+      }
       // prefetch state: 0 nothing yet, 1 next unit requested, 2 next q fetched
       int pf = 0;
       auto prefetch_step = [&]() {
@@ -777,10 +806,19 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
           pf = 2;
         }
       };
-      // per-column bounds of a multi-query unit (AttnUnit::nq)
-      const int nq = un.nq > 1 ? un.nq : 1;
-      const int th0 = un.t_hi - (nq - 1 - (2 * (lane & 3)) / p.g);
-      const int th1 = un.t_hi - (nq - 1 - (2 * (lane & 3) + 1) / p.g);
+      // per-column bounds of a multi-query unit (AttnUnit::nq); the tiles'
+      // union of positions is [t_lo, t_hi), the first column's bound b_min
+      int th[QT][2];
+      int b_min = INT32_MAX, t_hi = 0;
+#pragma unroll
+      for (int q = 0; q < QT; ++q) {
+        const AttnUnit& uq = q == 0 ? un : un2;
+        const int nq = uq.nq > 1 ? uq.nq : 1;
+        th[q][0] = uq.t_hi - (nq - 1 - (2 * (lane & 3)) / p.g);
+        th[q][1] = uq.t_hi - (nq - 1 - (2 * (lane & 3) + 1) / p.g);
+        b_min = min(b_min, uq.t_hi - (nq - 1));
+        t_hi = max(t_hi, uq.t_hi);
+      }
       for (int k = rr; k < n_sb; k += R) {
         const uint32_t jj = J + (uint32_t)k * HPR + hr;
         const uint32_t stage = jj % NSTAGE;
@@ -789,13 +827,12 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
         const int j = item.sb_begin + k;
         constexpr int T = SubGeom<D, NG, FMT>::T;
         const int pos0 = j * T;
-        const bool boundary = pos0 < un.t_lo || pos0 + T > un.t_hi - (nq - 1);
+        const bool boundary = pos0 < un.t_lo || pos0 + T > b_min;
         const uint8_t* sbp = stages + (size_t)stage * SB;
         if constexpr (FMT == kFmtBf16)
           tc_subblock_raw<D>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi);
         else
-          tc_subblock<D, NG, FAST>(sbp, st, lane, p.scale_log2, boundary, pos0, un.t_lo, un.t_hi, th0,
-                                   th1);
+          tc_subblock<D, NG, FAST, QT>(sbp, sts, lane, p.scale_log2, boundary, pos0, un.t_lo, t_hi, th);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_base + 8 * (NSTAGE + stage));
         if (pf < 2) prefetch_step();
@@ -851,11 +888,20 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
         }
       }
       if (rr == 0) finish_head<D>(p, st, l0, l1, un, item, h, lane);
+      if constexpr (QT == 2) {
+        float m0 = sts[1].l[0], m1 = sts[1].l[1];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          m0 += __shfl_xor_sync(0xffffffffu, m0, off);
+          m1 += __shfl_xor_sync(0xffffffffu, m1, off);
+        }
+        finish_head<D>(p, sts[1], m0, m1, un2, item, h, lane);
+      }
     }
   }
 }
 
-template <int D, int NG, int NCW, int R, int NSTAGE, int FMT>
+template <int D, int NG, int NCW, int R, int NSTAGE, int FMT, int QT = 1>
 __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p) {
   static_assert(NCW == 8, "two consumer warpgroups");
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
@@ -985,14 +1031,14 @@ __global__ void __launch_bounds__((NCW + 4) * 32, 1) attn_tc_kernel(AttnParams p
   // ---------------- consumers ----------------
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   if (FMT == kFmtInt8 && *reinterpret_cast<volatile const int*>(p.large_scale) != 0)
-    attn_consume<D, NG, NCW, R, NSTAGE, FMT, false>(p, smem, stages, bar_base, cta_abort, tags, warp,
+    attn_consume<D, NG, NCW, R, NSTAGE, FMT, false, QT>(p, smem, stages, bar_base, cta_abort, tags, warp,
                                                     lane, it0, it1, rounds);
   else
-    attn_consume<D, NG, NCW, R, NSTAGE, FMT, true>(p, smem, stages, bar_base, cta_abort, tags, warp,
+    attn_consume<D, NG, NCW, R, NSTAGE, FMT, true, QT>(p, smem, stages, bar_base, cta_abort, tags, warp,
                                                    lane, it0, it1, rounds);
 }
 
-template <int D, int NG, int NCW, int R, int FMT>
+template <int D, int NG, int NCW, int R, int FMT, int QT = 1>
 cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
   constexpr int NSTAGE = stages_for<D, NG, NCW, R, FMT>();
   using SM = AttnSmem<D, NG, NCW, R, NSTAGE, FMT>;
@@ -1008,11 +1054,11 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
     // setmaxnreg.inc waits until the producer's released registers cover it:
     // refuse to launch a build whose register count would not balance
     cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>);
+    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT, QT>);
     if (e != cudaSuccess) return e;
     if (fa.numRegs * (NCW + 4) * 32 < 128 * kProducerRegs + NCW * 32 * kConsumerRegs)
       return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>,
+    e = cudaFuncSetAttribute(attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT, QT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
@@ -1029,9 +1075,9 @@ cudaError_t launch_tc(const AttnParams& p, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT>, p);
+    return cudaLaunchKernelEx(&cfg, attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT, QT>, p);
   }
-  attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
+  attn_tc_kernel<D, NG, NCW, R, NSTAGE, FMT, QT><<<grid, (NCW + 4) * 32, SM::TOTAL, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -1040,7 +1086,10 @@ cudaError_t launch_tc_r(const AttnParams& p, int grid, cudaStream_t stream) {
   const int hpr = p.hg < NCW ? p.hg : NCW;
   if (NCW % hpr != 0 || p.hg % hpr != 0) return cudaErrorInvalidValue;
   cudaError_t e = cudaErrorInvalidValue;
-  switch (NCW / hpr) {
+  if (p.qt == 2) {  // two query tiles per unit: one warp per head only
+    if constexpr (FMT == kFmtInt8 && D <= 128)
+      if (hpr == NCW) e = launch_tc<D, NG, NCW, 1, FMT, 2>(p, grid, stream);
+  } else switch (NCW / hpr) {
     case 1: e = launch_tc<D, NG, NCW, 1, FMT>(p, grid, stream); break;
     case 2: e = launch_tc<D, NG, NCW, 2, FMT>(p, grid, stream); break;
     case 4: e = launch_tc<D, NG, NCW, 4, FMT>(p, grid, stream); break;
@@ -1242,6 +1291,8 @@ int tc_desc(char* buf, size_t cap) {
 template <int D, int NG, int FMT = kFmtInt8>
 int tc_desc_r(const AttnParams& p, char* buf, size_t cap) {
   const int hpr = p.hg < 8 ? p.hg : 8;
+  if (p.qt == 2)
+    return snprintf(buf, cap, "attn_tc_kernel<%d,%d,8,1,%d,%d,2>", D, NG, stages_for<D, NG, 8, 1, FMT>(), FMT);
   if (hpr <= 0 || 8 % hpr != 0) return snprintf(buf, cap, "none");
   switch (8 / hpr) {
     case 1: return tc_desc<D, NG, 8, 1, FMT>(buf, cap);
