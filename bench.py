@@ -707,7 +707,7 @@ def run_next_row(args, cfg, kb, torch, rank, world, local_rank):
                     value=n * nq / (ms / 1e3), unit="tokens/s", ms_per_step=ms, dtype="u8", **base,
                     config={"workload": args.config, "seqs": n, "n_query": nq, "layers": layers,
                             "q_heads": hq, "kv_heads": hkv, "head_dim": D, "group_size": G,
-                            "mean_len": float(np.mean(lens)), "path": "decode units of up to 8 / GQA queries, one query per tile column (n_query x GQA < 64 rows)"},
+                            "mean_len": float(np.mean(lens)), "path": "decode kernel, query tiles of 8 columns (up to 2 per unit), each column one (query, head) (n_query x GQA < 64 rows)"},
                     roofline={"bound": "hbm", "kernel": "attn_tc_kernel", "attn_ms": attn_ms,
                               "achieved_unique": uniq / (attn_ms / 1e3) / 1e9,
                               "achieved_logical": logical / (attn_ms / 1e3) / 1e9,
