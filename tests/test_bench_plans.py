@@ -51,3 +51,28 @@ def test_bench_workload_plan_is_pinned(key, seqs):
     else:
         seen = _plans(cfg, lengths, cfg["layers"])
     assert seen == {PLANS[key]}
+
+
+def test_verify_workload_uses_two_query_tiles():
+    # bench.py --config next_verify4: 4 drafts x GQA 4 = 16 columns per
+    # sequence, one decode item per piece with two 8-column query tiles
+    cfg = bench.CONFIGS["next_verify4"]
+    lengths = bench.sample_lengths(cfg, cfg["seqs"])
+    layers, nq = cfg["layers"], cfg["n_query"]
+    p = kb.KVPool(layers, cfg["hkv"], cfg["hq"], cfg["D"], num_blocks=1 << 20, group_size=cfg["G"],
+                  device=-1)
+    seqs = [p.create_sequence() for _ in lengths]
+    arr = (C.c_uint64 * len(seqs))(*[s.handle for s in seqs])
+    for s, Lq in zip(seqs, lengths):
+        one = (C.c_uint64 * 1)(s.handle)
+        L.check(L.lib.krill_append_quantize(p.handle, 1, one, 0, layers, Lq, None, None,
+                                            L.DTYPE_BF16, None))
+    kernels = set()
+    for _ in range(3):
+        L.check(L.lib.krill_append_quantize(p.handle, len(seqs), arr, 0, layers, nq, None, None,
+                                            L.DTYPE_BF16, None))
+        L.check(L.lib.krill_verify_attention(p.handle, len(seqs), arr, 0, layers, nq, None,
+                                             L.DTYPE_BF16, None, L.DTYPE_BF16, 1.0, None))
+        kernels.add(p.last_kernels())
+    p.close()
+    assert kernels == {"attn_tc_kernel<128,2,8,1,13,0,2>+attn_combine_kernel<128>"}, kernels

@@ -28,6 +28,7 @@ from tests.test_gpu_attention import ATOL  # noqa: E402
     (128, 64, 32, 4, BF16, 2),
     (64, 64, 32, 8, F16, 5),
     (256, 64, 8, 4, F16, 3),
+    (64, 64, 32, 8, F16, 3),   # 12 columns: two query tiles, the second half full
 ])
 def test_verify_matches_sequential_oracle(D, G, hq, hkv, dtype, nq):
     rng = np.random.default_rng(9)
@@ -53,6 +54,11 @@ def test_verify_matches_sequential_oracle(D, G, hq, hkv, dtype, nq):
     kb.verify_attention(pool, seqs, 0, dev_bits(qb, dtype), out, scale)
     torch.cuda.synchronize()
     assert pool.device_error() == 0
+    # 9-16 columns per sequence (queries x GQA group) with 8+ kv heads run as
+    # two 8-column query tiles of one decode item
+    g = hq // hkv
+    two_tiles = 8 < nq * g <= 16 and hkv >= 8 and D <= 128
+    assert pool.last_kernels().split("+")[0].endswith(",2>") == two_tiles, pool.last_kernels()
     got = out.cpu().numpy().astype(np.float64)
     for i in range(n):
         for layer in range(layers):
