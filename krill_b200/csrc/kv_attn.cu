@@ -768,8 +768,9 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
   if (it0 < it1) {
     item_next = p.items[it0];
     un_next = p.units[item_next.unit];
-    fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
-                   q_row_elems, lane);
+    if constexpr (QT == 1)
+      fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
+                 q_row_elems, lane);
   }
   for (int it = it0; it < it1; ++it) {
     const AttnItem item = item_next;
@@ -778,9 +779,14 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
     const int n_sb = item.sb_end - item.sb_begin;
     for (int rd = 0; rd < rounds; ++rd) {
       const int h = item.h0 + rd * HPR + hr;
+      // with two tiles both queries are fetched here (no prefetch across the
+      // item, whose registers the second tile needs); items are long
+      if constexpr (QT == 2)
+        fetch_q<D>(qr, p.q, q_row(un, h), p.g, unit_cols(un, p.g), q_row_elems, lane);
       reset_state(st);
       set_q<D, FMT>(st, qr, p.q_dtype);
       // the shadow unit's queries (second tile), fetched here: items are long
+      // (the shadow record is read again at the finish, not kept in registers)
       AttnUnit un2 = un;
       if constexpr (QT == 2) {
         un2 = p.units[item.unit + 1];
@@ -793,7 +799,8 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
       int pf = 0;
       auto prefetch_step = [&]() {
         if (rd + 1 < rounds) {  // next round: same unit, the next head group
-          fetch_q<D>(qr, p.q, q_row(un, h + HPR), p.g, unit_cols(un, p.g), q_row_elems, lane);
+          if constexpr (QT == 1)
+            fetch_q<D>(qr, p.q, q_row(un, h + HPR), p.g, unit_cols(un, p.g), q_row_elems, lane);
           pf = 2;
         } else if (it + 1 >= it1) {
           pf = 2;
@@ -801,8 +808,9 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
           un_next = p.units[item_next.unit];
           pf = 1;
         } else {
-          fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
-                   q_row_elems, lane);
+          if constexpr (QT == 1)
+            fetch_q<D>(qr, p.q, q_row(un_next, item_next.h0 + hr), p.g, unit_cols(un_next, p.g),
+                       q_row_elems, lane);
           pf = 2;
         }
       };
@@ -895,7 +903,7 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
           m0 += __shfl_xor_sync(0xffffffffu, m0, off);
           m1 += __shfl_xor_sync(0xffffffffu, m1, off);
         }
-        finish_head<D>(p, sts[1], m0, m1, un2, item, h, lane);
+        finish_head<D>(p, sts[1], m0, m1, p.units[item.unit + 1], item, h, lane);
       }
     }
   }
