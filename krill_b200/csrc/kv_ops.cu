@@ -283,7 +283,14 @@ __device__ __forceinline__ void quantize_group_row(const uint32_t (&w)[G / 2], u
       else codes[j / 2] |= pr << 16;
     }
   } else {  // a non-finite input in the group: the divide decides every code
-    codes_by_divide(w, G, mn, scale, DT, codes);
+    // (through copies, so that only this rare path hands arrays to the
+    // out-of-line function and w / codes can stay in registers)
+    uint32_t wt[G / 2], ct[G / 4];
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) wt[j] = w[j];
+    codes_by_divide(wt, G, mn, scale, DT, ct);
+#pragma unroll
+    for (int j = 0; j < G / 4; ++j) codes[j] = ct[j];
   }
   s16 = __half_as_ushort(__float2half_rn(scale));
   z16 = __half_as_ushort(__float2half_rn(mn));
@@ -392,31 +399,24 @@ __device__ __forceinline__ void row_words_put(uint8_t* __restrict__ buf, int lan
 // Rotates this lane's staged K row in place (rotate-half: element d < D/2
 // with d + D/2) with the caller's cos/sin rows at the warp's 32 positions (f32
 // rows of D/2 values, row of lane r at table + r * D/2), 16 elements at a
-// time; the cos/sin chunk is staged warp-wide in cbuf (5 KB).
+// time. Each lane reads its own position's cos/sin straight from the table
+// (every head and layer of a call reads the same rows, so they are cache
+// hits); lanes of tokens outside the call read nothing and rotate zeros.
 template <int D, int DT>
-__device__ __forceinline__ void rope_row_in_place(uint8_t* kbuf, uint8_t* cbuf, const float* cos_rows,
+__device__ __forceinline__ void rope_row_in_place(uint8_t* kbuf, const float* cos_rows,
                                                   const float* sin_rows, uint32_t valid, int lane) {
   constexpr int H = D / 2, B = 2 * D;
+  const bool own = (valid >> lane) & 1u;
+  const uint4* cr = reinterpret_cast<const uint4*>(cos_rows + (int64_t)lane * H);
+  const uint4* sr = reinterpret_cast<const uint4*>(sin_rows + (int64_t)lane * H);
 #pragma unroll 1
   for (int jc = 0; jc < H / 16; ++jc) {
-    __syncwarp();
-    // rows of 64 bytes padded to 80: 16-byte loads of 8 consecutive lanes
-    // then fall in distinct bank groups (5 r + c mod 8)
-#pragma unroll
-    for (int q = lane; q < 256; q += 32) {
-      const int tb = q >> 7, r = (q >> 2) & 31, c = q & 3;
-      if ((valid >> r) & 1u) {
-        const float* src = (tb ? sin_rows : cos_rows) + (int64_t)r * H + 16 * jc;
-        *reinterpret_cast<uint4*>(cbuf + tb * 32 * 80 + r * 80 + 16 * c) =
-            __ldg(reinterpret_cast<const uint4*>(src) + c);
-      }
-    }
-    __syncwarp();
     uint32_t cw[16], sw[16];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint4 x = *reinterpret_cast<const uint4*>(cbuf + lane * 80 + 16 * c);
-      const uint4 y = *reinterpret_cast<const uint4*>(cbuf + 32 * 80 + lane * 80 + 16 * c);
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      const uint4 x = own ? __ldg(cr + 4 * jc + c) : z;
+      const uint4 y = own ? __ldg(sr + 4 * jc + c) : z;
       cw[4 * c] = x.x; cw[4 * c + 1] = x.y; cw[4 * c + 2] = x.z; cw[4 * c + 3] = x.w;
       sw[4 * c] = y.x; sw[4 * c + 1] = y.y; sw[4 * c + 2] = y.z; sw[4 * c + 3] = y.w;
     }
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(64) append_rows_kernel(uint8_t* __restrict__ p
   constexpr int T = sub_tokens(D), NG = D / G, WPT = T / 32, H = D / 2, B = 2 * D;
   extern __shared__ __align__(16) uint8_t rows_smem[];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
-  constexpr int WSMEM = 32 * B + (ROPE ? 2 * 32 * 80 : 0);  // shared memory per warp
+  constexpr int WSMEM = 32 * B;  // shared memory per warp: its 32 staged rows
   uint8_t* kbuf = rows_smem + (size_t)wl * WSMEM;
   const int64_t wg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t tile = wg / WPT;
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(64) append_rows_kernel(uint8_t* __restrict__ p
   // every lane runs the arithmetic (the RoPE staging inside is warp-wide);
   // only the call's tokens store
   if constexpr (ROPE)
-    rope_row_in_place<D, DT>(kbuf, kbuf + 32 * B, rope.cos + prow, rope.sin + prow, valid, lane);
+    rope_row_in_place<D, DT>(kbuf, rope.cos + prow, rope.sin + prow, valid, lane);
 #pragma unroll 1
   for (int g = 0; g < NG; ++g) {
     uint32_t w[G / 2], codes[G / 4];
@@ -670,7 +670,7 @@ cudaError_t launch_append(const Geom& g, uint8_t* pool, const AppendDst* d_dst, 
     const int64_t n_tiles = tiles;
     const int64_t warps_rows = n_tiles * (g.subt / 32);
     const unsigned rows_blocks = (unsigned)((warps_rows + 1) / 2);  // two warps per CTA
-    const size_t rows_smem = (size_t)2 * (32 * 2 * g.D + (rope.cos ? 2 * 32 * 80 : 0));
+    const size_t rows_smem = (size_t)2 * 32 * 2 * g.D;  // two warps' staged rows
     // above 48 KB of dynamic shared memory a kernel needs the opt-in (D = 256
     // with RoPE: 96 KB); the attribute is per device, set on every such call
 #define KRILL_ROWS_SMEM(DD, GG, DTT)                                                             \
