@@ -434,7 +434,7 @@ __device__ __forceinline__ void rope_row_in_place(uint8_t* kbuf, const float* co
 // RoPE, its cos/sin rows) in shared memory with coalesced loads, then each
 // lane quantizes its own token's groups; then the same for V.
 template <int D, int G, int DT, bool ROPE>
-__global__ void __launch_bounds__(64, G == 64 ? 12 : 0) append_rows_kernel(uint8_t* __restrict__ pool, Geom geom,
+__global__ void __launch_bounds__(64) append_rows_kernel(uint8_t* __restrict__ pool, Geom geom,
                                                          const AppendDst* __restrict__ dst,
                                                          int layer_begin, int n_seqs, int n_new,
                                                          int n_chunks, int64_t n_tiles,
