@@ -765,6 +765,9 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
     return ((int64_t)u.qo_row * p.Hq + (int64_t)hh * p.g) * D;
   };
   const int64_t q_row_elems = (int64_t)p.Hq * D;
+  // query index (within a multi-query unit) of this lane's two columns
+  const int col_q0 = D <= 128 ? (2 * (lane & 3)) / p.g : 0;
+  const int col_q1 = D <= 128 ? (2 * (lane & 3) + 1) / p.g : 0;
   if (it0 < it1) {
     item_next = p.items[it0];
     un_next = p.units[item_next.unit];
@@ -821,10 +824,15 @@ __device__ __forceinline__ void attn_consume(const AttnParams& p, uint8_t* smem,
 #pragma unroll
       for (int q = 0; q < QT; ++q) {
         const AttnUnit& uq = q == 0 ? un : un2;
-        const int nq = uq.nq > 1 ? uq.nq : 1;
-        th[q][0] = uq.t_hi - (nq - 1 - (2 * (lane & 3)) / p.g);
-        th[q][1] = uq.t_hi - (nq - 1 - (2 * (lane & 3) + 1) / p.g);
-        b_min = min(b_min, uq.t_hi - (nq - 1));
+        const int nq1 = uq.nq > 1 ? uq.nq - 1 : 0;  // column c: t_hi - (nq - 1 - c / g)
+        if constexpr (D <= 128) {  // per-lane quotients computed once per launch
+          th[q][0] = uq.t_hi - (nq1 - min(col_q0, nq1));
+          th[q][1] = uq.t_hi - (nq1 - min(col_q1, nq1));
+        } else {  // (at head_dim 256 two more live registers cost spills)
+          th[q][0] = uq.t_hi - (nq1 - (2 * (lane & 3)) / p.g);
+          th[q][1] = uq.t_hi - (nq1 - (2 * (lane & 3) + 1) / p.g);
+        }
+        b_min = min(b_min, uq.t_hi - nq1);
         t_hi = max(t_hi, uq.t_hi);
       }
       for (int k = rr; k < n_sb; k += R) {
