@@ -29,6 +29,7 @@ from tests.test_gpu_attention import ATOL  # noqa: E402
     (64, 64, 32, 8, F16, 5),
     (256, 64, 8, 4, F16, 3),
     (64, 64, 32, 8, F16, 3),   # 12 columns: two query tiles, the second half full
+    (128, 64, 64, 8, BF16, 2), # GQA 8 with 8 kv heads: one query per tile, two tiles
 ])
 def test_verify_matches_sequential_oracle(D, G, hq, hkv, dtype, nq):
     rng = np.random.default_rng(9)

@@ -397,7 +397,7 @@ def test_cascade_shared_part_stays_below_every_length():
 
 
 def test_verify_attention_planning():
-    """Multi-query verify: one unit per query, each bounded by its own token
+    """Multi-query verify: each query bounded by its own token
     (buildBatchedVerifyMask, BatchedDecode.swift:299-312); the queries must be
     in the cache; full-history pools only."""
     p = pool(layers=2, blocks=64)
@@ -430,3 +430,41 @@ def test_prefill_attention_takes_the_causal_cascade_path():
     assert p.last_plan()[2] == 0  # no decode items
     L.check(L.lib.krill_verify_attention(p.handle, 1, arr, 0, 2, 4, None, 1, None, 2, 1.0, None))
     assert p.last_cascade()[1] == 0 and p.last_plan()[2] > 0
+
+
+@pytest.mark.parametrize("hq,hkv,nq,two_tiles", [
+    (32, 8, 2, False),   # 8 columns: one unit, one tile
+    (32, 8, 3, True),    # 12 columns: the second unit is the second tile
+    (32, 8, 4, True),    # 16 columns
+    (32, 8, 5, False),   # 20 columns: three units of one tile each
+    (32, 4, 2, False),   # GQA 8 with 4 kv heads: no one-warp-per-head plan
+    (64, 8, 2, True),    # GQA 8 with 8 kv heads: one query per tile
+])
+def test_verify_query_tiles(hq, hkv, nq, two_tiles):
+    """Queries of one sequence share decode units as columns of the 8-column
+    query tile; 9-16 columns run as two tiles of one item when the plan has
+    one warp per kv head."""
+    p = pool(layers=2, hkv=hkv, hq=hq, blocks=64)
+    seqs = [p.create_sequence() for _ in range(3)]
+    for s, n in zip(seqs, (700, 40, 300)):
+        append(p, [s], n)
+    arr = (C.c_uint64 * 3)(*[s.handle for s in seqs])
+    L.check(L.lib.krill_verify_attention(p.handle, 3, arr, 0, 2, nq, None, 1, None, 2, 1.0, None))
+    first = p.last_kernels().split("+")[0]
+    assert first.startswith("attn_tc_kernel<") and first.endswith(",2>") == two_tiles, first
+
+
+def test_pair_cascade_is_opt_in():
+    """The CTA-pair cascade runs only under KRILL_ATTN_TENSOR_CORE_PAIR and
+    only for items of more than 128 rows; a pair counts as two CTAs."""
+    for impl, forks, kernel in [(L.ATTN_TENSOR_CORE, 40, "attn_shared_umma_kernel"),
+                                (L.ATTN_TENSOR_CORE_PAIR, 40, "attn_shared_pair_kernel"),
+                                (L.ATTN_TENSOR_CORE_PAIR, 20, "attn_shared_umma_kernel")]:
+        p = pool(layers=2, blocks=400, attn_impl=impl)
+        pc, _, fs = _forked_batch(p, 1024, forks, 10)
+        attend(p, fs)
+        groups, items, slots, ctas = p.last_cascade()
+        assert groups == 1 and p.last_kernels().startswith(kernel), (impl, forks, p.last_kernels())
+        if kernel == "attn_shared_pair_kernel":
+            assert ctas % 2 == 0
+        pc.close()
